@@ -1,0 +1,325 @@
+"""Benchmark of the quantized linear layer's decode hot path.
+
+One step = one decode token through every quantized projection of a Qwen3-0.6B-shaped decoder
+(28 layers x q, k, v, o, gate, up, down, then the 151936 x 1024 LM head; int8 per-row weights
+from N(0, 0.02), the first input N(0, 1)). q/k/v and gate/up share their input and QACT range,
+so each group is one launch: 113 fused QACT+MM launches a step, each reading the previous
+launch's output as a decode step does (opentpu_b200.decode.DecodeChain, dependent), replayed as
+one CUDA graph. The weights (598 MB) exceed the 126 MB L2, so each step streams them from
+HBM.
+
+--profile head|step runs a few launches and exits (the command the ncu summaries under
+profiles/ were captured with).
+
+metric: decode weight GB/s (whole job) with tok/s = steps / s beside it. With --gpus N each
+projection's output rows are split over the N ranks (the reference's Weight(shard=0)) and an
+NCCL all-gather assembles every projection's output on every rank (the reference's GATHER).
+
+--impl reference times the reference's CPU algorithm (the numpy port under oracle/, the same
+arithmetic as the reference's MM) on a bounded sample of the same step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from opentpu_b200 import workloads as WL  # noqa: E402
+
+METRIC = "decode weight GB/s"
+UNIT = "GB/s"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_run(what: str):
+    """A few launches for an ncu capture: the LM head GEMV alone, or two decode steps."""
+    import torch
+    from opentpu_b200 import linear
+    from opentpu_b200.decode import DecodeChain
+    torch.cuda.set_device(0)
+    shape = WL.QWEN3_0_6B
+    if what == "head":
+        W = torch.randn((shape.vocab, shape.hidden), device="cuda") * 0.02
+        w = linear.PackedWeight.from_float(W, "int8-row")
+        del W
+        x = torch.randn((1, shape.hidden), device="cuda")
+        y = torch.empty((1, shape.vocab), device="cuda")
+        for _ in range(5):
+            linear.qlinear(x, w, out=y)
+    else:
+        chain = DecodeChain(shape)
+        chain.capture()
+        chain.replay(2)
+        chain.release()
+    torch.cuda.synchronize()
+
+
+class Clocks:
+    """nvidia-smi sampling while the timed region runs (SM clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        mhz = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def cpu_sample_seconds(budget_s: float = 12.0):
+    """The oracle's exact decode GEMV chain on host cores over a bounded sample of the step's
+    projections: returns (GB/s of weight bytes, sample description, threads)."""
+    from oracle import fp32 as F
+    from oracle import mx as X
+    shape = WL.QWEN3_0_6B
+    rng = np.random.default_rng(0)
+    # one layer's seven projections plus a 16384-row slice of the head
+    shapes = [(N, K) for _, N, K in shape.projections()] + [(16384, shape.hidden)]
+    mats = []
+    for N, K in shapes:
+        W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        q, s = X.quantize_rows_rsc(W)
+        x = rng.standard_normal(K).astype(np.float32)
+        mats.append((q, s, x, K))
+    nbytes = sum(q.shape[0] * (q.shape[1] + 4) for q, _, _, _ in mats)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        for q, s, x, K in mats:
+            qa, Sa, da = F.quantize_rows(x[None, :], 32)
+            X.mm(qa, Sa, da, q, s, "int8", K, rsc=True)
+        done += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or done >= 50:
+            break
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:
+        threads = 1
+    desc = (f"{done} passes over 1 layer (7 projections) + a 16384-row head slice "
+            f"({nbytes / 1e6:.1f} MB of int8 rows), exact MM port, numpy")
+    return done * nbytes / el / 1e9, desc, threads
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    vals = []
+    desc, threads = "", 1
+    for i in range(args.warmup + args.steps):
+        v, desc, threads = cpu_sample_seconds(budget_s=8.0)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "Qwen3-0.6B-shaped int8 per-row decode GEMV chain (sample)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["head", "step"])
+    args = ap.parse_args()
+    if args.profile:
+        profile_run(args.profile)
+        return
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from opentpu_b200 import linear
+    from opentpu_b200.decode import DecodeChain
+
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    shape = WL.QWEN3_0_6B
+    fmt = "int8-row"
+    chain = DecodeChain(shape, fmt=fmt, head_fmt=fmt, world=world, rank=rank, group=group)
+    chain.capture()
+    stream = chain.stream
+    total_bytes = chain.weight_bytes
+
+    chain.replay(args.warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        chain.replay(args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = total_bytes / (ms * 1e-3) / 1e9
+
+    # the dominant kernel alone: the LM head GEMV (this rank's rows), 20 launches in a graph
+    head, hx, hy = chain.weights[-1], chain.inputs[shape.hidden], chain.outs[-1]
+    hg = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            linear.qlinear(hx, head, out=hy)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(hg, stream=stream):
+        for _ in range(20):
+            linear.qlinear(hx, head, out=hy)
+    with torch.cuda.stream(stream):
+        hg.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            hg.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    head_ms = e0.elapsed_time(e1) / 100
+    head_bytes = head.stream_bytes + head.K * 4 + head.N * 4
+    peak, peak_kind = peaks()
+    achieved = head_bytes / (head_ms * 1e-3) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists() and world == 1:
+        traffic = json.loads(tp.read_text()).get("mm_gemv_head_int8_row_bytes_per_launch")
+
+    # end to end through the public API from host buffers: inputs H2D, logits D2H each step
+    inputs_host = {shape.hidden: torch.randn((1, shape.hidden)).pin_memory()}
+    logits_host = torch.empty(tuple(chain.logits().shape), pin_memory=True)
+    h2d = sum(t.numel() * 4 for t in inputs_host.values())
+    d2h = logits_host.numel() * 4
+    for _ in range(3):
+        chain.run_host(inputs_host, logits_host)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    n_e2e = max(3, min(args.steps, 200))
+    e0.record(stream)
+    for _ in range(n_e2e):
+        chain.run_host(inputs_host, logits_host)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / n_e2e
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, desc, threads = cpu_sample_seconds()
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "Qwen3-0.6B-shaped int8 per-row decode step: 28 layers x "
+                                   "(QKV, O, GateUp, Down) + 151936x1024 LM head, M=1",
+                       "weights_bytes_per_step": total_bytes, "format": fmt,
+                       "parallelism": f"row-shard x{world}" + (" + NCCL all-gather per "
+                                                              "projection" if world > 1 else ""),
+                       "l2": "weights 598 MB > 126 MB L2 (no flush needed)",
+                       "graph": "one CUDA graph per step, PDL launches"},
+            "tok_s": 1e3 / ms,
+            "hbm_frac": value / world / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "mm_gemv (LM head launch, 151936x1024 int8-row, M=1)",
+                         "bytes_per_launch": head_bytes, "us_per_launch": head_ms * 1e3,
+                         "peak_kind": peak_kind},
+            "cpu_baseline": cpu,
+            "e2e": {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms, "api": "DecodeChain.run_host"},
+            "gpu_launches": chain.launches * args.steps,
+            "clocks": clocks.summary(),
+        }), flush=True)
+    chain.release()
+    del hg
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+/*
+ * libotq -- openTPU's quantized linear layer on NVIDIA B200 (sm_100a): the C ABI.
+ *
+ * The reference (FeSens/openTPU) is a Python package; this ABI is what its numpy call sites for
+ * the quantized linear layer would bind through ctypes (the binding is in INTEGRATION.md). Each
+ * entry point names the reference function (path:line inside the reference project) whose
+ * results it reproduces.
+ *
+ * Conventions
+ *  - Every pointer is a CUDA device pointer (or managed memory) owned by the caller; no entry
+ *    point allocates device memory and none keeps a pointer after it returns.
+ *  - `stream` is a cudaStream_t (NULL: the legacy default stream). Calls are asynchronous on
+ *    that stream and may be captured into CUDA graphs.
+ *  - Return 0 (OTQ_OK) or a negative status; nothing is thrown, nothing is printed, no device
+ *    assert is used. Shapes, strides and alignments are checked on the host before a launch.
+ *  - Row-major matrices with explicit leading dimensions in ELEMENTS; packed weight rows and
+ *    scale rows with strides in BYTES, exactly the reference's byte layouts.
+ */
+#ifndef OTQ_H_
+#define OTQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define OTQ_API __attribute__((visibility("default")))
+#else
+#define OTQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status codes */
+#define OTQ_OK 0
+#define OTQ_ERR_ARG (-1)    /* a size, stride, flag or null pointer out of range */
+#define OTQ_ERR_ALIGN (-2)  /* a pointer or stride not aligned as the entry point requires */
+#define OTQ_ERR_FORMAT (-3) /* unknown weight format, or a format/flag combination MM refuses */
+#define OTQ_ERR_CUDA (-4)   /* a CUDA runtime error (otq_last_cuda_error names it) */
+#define OTQ_ERR_DEVICE (-5) /* the current device is not a compute-capability 10.x GPU */
+
+/* ------------------------------------------------------------------ weight formats
+ * The MM instruction's WF codes (opentpu/isa.py:26-27; docs/isa.md "Weight formats"):
+ * int8 = int8x (one dw byte a 128-block), int4 = int4x and fp4 = fp4x6 (a word a block: dw and
+ * four 6-bit multipliers), nvfp4 (eight E4M3 bytes a block), each under a per-row fp32 Sw. */
+#define OTQ_FMT_INT8 0
+#define OTQ_FMT_INT4 1
+#define OTQ_FMT_FP4 2
+#define OTQ_FMT_NVFP4 3
+
+/* MM flag bits, the reference's own values (opentpu/isa.py:21 F_UNIT/F_ACC/F_ASCALE, :30 F_RSC) */
+#define OTQ_MM_UNIT 0x1   /* no scale rows: Sw = 1, dw = 0, m = 1 */
+#define OTQ_MM_ACC 0x2    /* y = y_old + MM */
+#define OTQ_MM_ASCALE 0x8 /* y = y_old * alpha[j] + MM (needs UNIT) */
+#define OTQ_MM_RSC 0x80   /* scale rows are Sw alone (4 bytes a row): dw = 0, m = 1 */
+
+/* The quantization block D of every MX entry point (the MXU's D on the reference's targets). */
+#define OTQ_D 128
+
+OTQ_API const char* otq_version(void);
+OTQ_API const char* otq_status_string(int status);
+/* The message of the last CUDA error an entry point met on this thread ("" if none). */
+OTQ_API const char* otq_last_cuda_error(void);
+/* OTQ_OK if the current device is compute capability 10.x (the library is built for sm_100a). */
+OTQ_API int otq_device_check(void);
+
+/* ------------------------------------------------------------------ quantizers */
+
+/* QACT / QST row quantization: fp32.quantize_mx (opentpu/fp32.py:321-343), QACT
+ * (opentpu/isasim.py:913-959). Rows of x [rows, n] (ldx floats apart) -> q int8 [rows, n]
+ * (ldq bytes apart), S fp32 [rows], d uint8 [rows, n/group] (ldd bytes apart; may be NULL in
+ * row mode). group: a multiple of 32 dividing n (QACT: 32 = D/4; QST and int8x weights: 128).
+ * row_mode != 0: every d = 0 (QACT/QST flag ROW). n <= 32768. */
+OTQ_API int otq_quantize_rows(const float* x, int64_t rows, int64_t n, int64_t ldx, int group,
+                      int row_mode, int8_t* q, int64_t ldq, float* S, uint8_t* d, int64_t ldd,
+                      void* stream);
+
+/* int8 weight rows as MM streams them. rsc == 0: quant.quantize_mxu(W, "int8") -- int8x
+ * (opentpu/quant.py:316-323, scale rows by pack_scales :403-426): rows [N, K] int8 and scale
+ * rows [N, srs] = Sw, one dw byte a 128-block, zero padding (srs >= 4 + 4*ceil(K/512)).
+ * rsc != 0: runtime.quantize_rows(W, D, row=True) (opentpu/runtime.py:66-76), the
+ * "int8 per output row with an fp32 scale" of quant.quantize(W, "int8", g=K)
+ * (opentpu/quant.py:218-224): scale rows are Sw alone (srs >= 4). K % 128 == 0, K <= 32768. */
+OTQ_API int otq_pack_int8(const float* W, int64_t N, int64_t K, int64_t ldw, int rsc, uint8_t* rows,
+                  int64_t rs, uint8_t* srows, int64_t srs, void* stream);
+
+/* Every MX weight format: quant.quantize_mxu(W, fmt) (opentpu/quant.py:510-524 -> quantize_mx
+ * :484-503): int8 (_int8x :316-323), int4 / fp4 (_x4 :325-367: int4x / fp4x6, the 13-point
+ * squared-error search of the 6-bit multipliers, in float64), nvfp4 (_nv :370-401, per-row
+ * fp32 scale, E4M3 per 16 by the same search). rows [N, rs bytes] (rs >= row_bytes: K for
+ * int8, 128*ceil(K/256) for 4-bit; padding written 0), scale rows [N, srs bytes]
+ * (srs >= quant.scale_bytes; padding written 0). K % 128 == 0, K <= 32768. */
+OTQ_API int otq_quantize_mxu(int fmt, const float* W, int64_t N, int64_t K, int64_t ldw,
+                             uint8_t* rows, int64_t rs, uint8_t* srows, int64_t srs,
+                             void* stream);
+
+/* ------------------------------------------------------------------ MM */
+
+/* MM over one QACT range: Slice._mm (opentpu/isasim.py:749-910; docs/isa.md "MM").
+ * Weights: rows [N, rs bytes] (int8: K bytes used; 4-bit: K/2, element 2i in the low nibble),
+ * scale rows [N, srs bytes] read at block k0 + k (NULL with OTQ_MM_UNIT).
+ * Activations as otq_quantize_rows(group 32) leaves them: q [M, K] (ldq), Sa [M],
+ * da [M, K/32] (ldd). Output y [M, N] (ldy floats apart); alpha [M] for OTQ_MM_ASCALE.
+ * Bit-exact: one exact integer per output, then the reference's three-product fp32 epilogue.
+ * K % 128 == 0, K <= 32640 (KB < 256, the MM field), rows/rs 16-byte aligned, scale rows aligned
+ * to 4 (int8, RSC), 8 (int4, fp4) or 16 (nvfp4) bytes; nvfp4 takes no RSC. */
+OTQ_API int otq_mm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows, int64_t srs,
+           int k0, int64_t N, int64_t K, const int8_t* q, int64_t ldq, const float* Sa,
+           const uint8_t* da, int64_t ldd, int64_t M, const float* alpha, float* y, int64_t ldy,
+           void* stream);
+
+/* QACT then MM on fp32 rows, fused in one kernel: what the reference's ol.dot does to a TMEM
+ * tile (opentpu/language.py:150-162; compiler.py:2622-2726 emits one QACT for the whole row
+ * and one MM; isasim.py:913-959 then 749-910). x [M, K] (ldx floats apart); row_mode != 0 is
+ * QACT ROW. Same weight arguments, flags and output as otq_mm. The QACT bytes are recomputed
+ * by every CTA in shared memory: nothing is written to global memory but y. */
+OTQ_API int otq_qmm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+            int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx, int row_mode,
+            int64_t M, const float* alpha, float* y, int64_t ldy, void* stream);
+
+/* Launch-tuning variant of otq_qmm for benchmarks and tests: k_split in {1, 2, 4, 8} warps share
+ * the K groups of each 16-row weight tile; 16 selects the persistent ring kernel (weights
+ * streamed through shared memory by bulk copies); 0 picks. pdl != 0 launches with programmatic
+ * dependent launch (the kernel waits on griddepcontrol before reading x). Same results as
+ * otq_qmm for every setting. */
+OTQ_API int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+               int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx,
+               int row_mode, int64_t M, const float* alpha, float* y, int64_t ldy,
+               int k_split, int pdl, void* stream);
+
+/* The device status word of the current device (synchronous): bit 0 set means a kernel's
+ * bounded wait on a shared-memory barrier ran out and that kernel returned early (its outputs
+ * are not valid). reset != 0 clears it. No counterpart in the reference (a simulator has no
+ * such failure). */
+OTQ_API int otq_status_word(int* value, int reset);
+
+/* ------------------------------------------------------------------ 4-bit group-32 fp16 */
+
+/* quant.quantize(W, "int4", g=32, scale="fp16") (opentpu/quant.py:225-227 -> quant_block
+ * :132-142 -> _quant_rows :144-170): per 32 elements s = fp16(min(amax/7, 65504)) (1 if amax or
+ * s is 0) and w = clip(rint(x/s), -7, 7), computed in float64 as the reference does. Output:
+ * codes [N, K/2] bytes (two's-complement nibbles, element 2i low), scales [N, K/32] fp16 bits.
+ * K % 32 == 0. */
+OTQ_API int otq_pack_g32(const float* W, int64_t N, int64_t K, int64_t ldw, uint8_t* codes,
+                 uint16_t* scales, void* stream);
+
+/* Weight-only linear over that format: y [M, N] = x [M, K] @ deq^T with deq = w * s, fp32
+ * accumulation (the reference's `quant.quantize(...).deq @ x` pattern,
+ * tests/test_quant.py:276-287, reference.py:14-17). Tolerance, not bit-exact. ACC: y += . */
+OTQ_API int otq_linear_g32(const uint8_t* codes, const uint16_t* scales, int64_t N, int64_t K,
+                   const float* x, int64_t ldx, int64_t M, int accumulate, float* y, int64_t ldy,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OTQ_H_ */

@@ -1,0 +1,81 @@
+"""ctypes binding of libotq.so (the C ABI of include/otq.h).
+
+The library is built in-tree (`python -m opentpu_b200.csrc.build` or `__graft_entry__.build()`).
+There is no fallback: if the library is missing or the GPU is not a compute-capability 10.x
+device, every GPU entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_char_p, c_int, c_int64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libotq.so"
+
+OK, ERR_ARG, ERR_ALIGN, ERR_FORMAT, ERR_CUDA, ERR_DEVICE = 0, -1, -2, -3, -4, -5
+FMT = {"int8": 0, "int4": 1, "fp4": 2, "nvfp4": 3}     # MM's WF codes (opentpu/isa.py:26-27)
+MM_UNIT, MM_ACC, MM_ASCALE, MM_RSC = 0x1, 0x2, 0x8, 0x80
+
+# name -> (restype, argtypes); every pointer is passed as an integer address
+_P, _I, _L = c_void_p, c_int, c_int64
+SIGNATURES = {
+    "otq_version": (c_char_p, []),
+    "otq_status_string": (c_char_p, [_I]),
+    "otq_last_cuda_error": (c_char_p, []),
+    "otq_device_check": (_I, []),
+    "otq_quantize_rows": (_I, [_P, _L, _L, _L, _I, _I, _P, _L, _P, _P, _L, _P]),
+    "otq_pack_int8": (_I, [_P, _L, _L, _L, _I, _P, _L, _P, _L, _P]),
+    "otq_quantize_mxu": (_I, [_I, _P, _L, _L, _L, _P, _L, _P, _L, _P]),
+    "otq_mm": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _P, _P, _L, _L, _P, _P, _L, _P]),
+    "otq_qmm": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _L, _P, _P, _L, _P]),
+    "otq_qmm_ex": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _L, _P, _P, _L, _I, _I,
+                        _P]),
+    "otq_status_word": (_I, [_P, _I]),
+    "otq_pack_g32": (_I, [_P, _L, _L, _L, _P, _P, _P]),
+    "otq_linear_g32": (_I, [_P, _P, _L, _L, _P, _L, _L, _I, _P, _L, _P]),
+}
+
+_lib = None
+
+
+def load():
+    """The loaded library (ctypes.CDLL), loading it on first use; raises if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m opentpu_b200.csrc.build` "
+            "(nvcc, sm_100a). There is no CPU implementation of this library.")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    """Raise for a non-zero status: ValueError for argument errors (the reference raises
+    ValueError for bad shapes and formats), RuntimeError for CUDA and device errors."""
+    if status == OK:
+        return
+    lib = load()
+    msg = f"{what}: {lib.otq_status_string(status).decode()}"
+    if status == ERR_CUDA:
+        msg += f" ({lib.otq_last_cuda_error().decode()})"
+    if status in (ERR_ARG, ERR_ALIGN, ERR_FORMAT):
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)
+
+
+def status_word(reset: bool = True) -> int:
+    """The device status word (synchronous): bit 0 = a kernel's bounded wait ran out."""
+    v = ctypes.c_int(0)
+    call("otq_status_word", ctypes.byref(v), int(reset))
+    return v.value

@@ -1,0 +1,342 @@
+// The extern "C" entry points of libotq (declared in include/otq.h): host-side validation of
+// every shape, stride, alignment and flag, then the launch. No exception crosses the ABI and
+// nothing is allocated.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "otq_internal.h"
+
+namespace otq {
+
+int quantize_rows_launch(const float* x, int64_t rows, int n, int64_t ldx, int group,
+                         int row_mode, int8_t* q, int64_t ldq, float* S, uint8_t* d, int64_t ldd,
+                         int pack, int rsc, uint8_t* prow, int64_t rs, uint8_t* srow, int64_t srs,
+                         cudaStream_t stream);
+int pack_mx4_launch(int fmt, const float* W, int64_t N, int K, int64_t ldw, uint8_t* rows,
+                    int64_t rs, uint8_t* srows, int64_t srs, cudaStream_t stream);
+int pack_g32_launch(const float* W, int64_t N, int64_t K, int64_t ldw, uint8_t* codes,
+                    uint16_t* scales, cudaStream_t stream);
+int linear_g32_launch(const uint8_t* codes, const uint16_t* scales, int64_t N, int K,
+                      const float* x, int64_t ldx, int M, int accumulate, float* y, int64_t ldy,
+                      cudaStream_t stream);
+
+// The library's device status word (one per device that loads the library): kernels record
+// a bounded wait that ran out here; otq_status_word reads and clears it.
+__device__ int g_status_word = 0;
+
+namespace {
+
+thread_local char g_last_cuda[256] = "";
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return kOk;
+  std::strncpy(g_last_cuda, cudaGetErrorString(e), sizeof(g_last_cuda) - 1);
+  return kErrCuda;
+}
+
+int finish(int st) {
+  if (st == kErrCuda) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) cuda_status(e);
+  }
+  return st;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int device_ok() {
+  static int checked[kMaxDevices] = {0};   // 0 unknown, 1 ok, -1 refused
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= kMaxDevices) return kErrDevice;
+  if (checked[dev] == 0) {
+    int major = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_status(e);
+    checked[dev] = major == 10 ? 1 : -1;
+  }
+  return checked[dev] == 1 ? kOk : kErrDevice;
+}
+
+int fmt_window(int fmt) {
+  switch (fmt) {
+    case kFmtInt8: return 16;
+    case kFmtInt4:
+    case kFmtFp4: return 11;
+    case kFmtNvfp4: return 13;
+    default: return -1;
+  }
+}
+
+// Scale-row alignment MM requires (docs/isa.md "MM": ssa/srs multiples of 4, 8 or 16).
+int64_t scale_align(int fmt, bool rsc) {
+  if (rsc || fmt == kFmtInt8) return 4;
+  return fmt == kFmtNvfp4 ? 16 : 8;
+}
+
+// Bytes of scale row that MM reads for blocks [k0, k0 + KB).
+int64_t scale_need(int fmt, bool rsc, int k0, int64_t KB) {
+  if (rsc) return 4;
+  switch (fmt) {
+    case kFmtInt8: return 4 + k0 + KB;
+    case kFmtInt4:
+    case kFmtFp4: return 8 + 4 * (k0 + KB);
+    default: return 16 + 8 * (k0 + KB);
+  }
+}
+
+int check_weights(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+                  int64_t srs, int k0, int64_t N, int64_t K) {
+  if (fmt_window(fmt) < 0) return kErrFormat;
+  if (flags & ~(kMmUnit | kMmAcc | kMmAscale | kMmRsc)) return kErrArg;
+  const bool unit = flags & kMmUnit, rsc = flags & kMmRsc;
+  if (rsc && fmt == kFmtNvfp4) return kErrFormat;            // isa.py:527
+  if ((flags & kMmAscale) && !(unit && (flags & kMmAcc))) {  // isa.py ASCALE needs UNIT and ACC
+    return kErrArg;
+  }
+  if (N <= 0 || K <= 0 || K % OTQ_D != 0 || K > 255 * OTQ_D) return kErrArg;
+  if (k0 < 0 || k0 > 255) return kErrArg;
+  if (rows == nullptr) return kErrArg;
+  const int64_t used = fmt == kFmtInt8 ? K : K / 2;
+  if (rs < used) return kErrArg;
+  if (!aligned(rows, 16) || rs % 16) return kErrAlign;
+  if (!unit) {
+    if (srows == nullptr) return kErrArg;
+    const int64_t a = scale_align(fmt, rsc);
+    if (!aligned(srows, a) || srs % a) return kErrAlign;
+    if (srs < scale_need(fmt, rsc, k0, K / OTQ_D)) return kErrArg;
+  }
+  return kOk;
+}
+
+int mt_bucket(int64_t M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+
+int check_out(int64_t M, int64_t N, const float* y, int64_t ldy, int flags, const float* alpha) {
+  if (M <= 0 || M > 0x7FFFFFFF || y == nullptr || ldy < N) return kErrArg;
+  if ((flags & kMmAscale) && alpha == nullptr) return kErrArg;
+  return kOk;
+}
+
+}  // namespace
+
+int* status_word() {
+  static int* addr[kMaxDevices] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int*>(p);
+  }
+  return addr[dev];
+}
+
+int sm_count(int dev) {
+  static int cache[kMaxDevices] = {0};
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace otq
+
+using namespace otq;
+
+extern "C" {
+
+const char* otq_version(void) { return "libotq 0.1 (sm_100a)"; }
+
+const char* otq_status_string(int status) {
+  switch (status) {
+    case OTQ_OK: return "ok";
+    case OTQ_ERR_ARG: return "invalid argument (size, stride, flag or null pointer)";
+    case OTQ_ERR_ALIGN: return "misaligned pointer or stride";
+    case OTQ_ERR_FORMAT: return "unknown weight format or unsupported format/flag combination";
+    case OTQ_ERR_CUDA: return "CUDA error";
+    case OTQ_ERR_DEVICE: return "the current device is not compute capability 10.x";
+    default: return "unknown status";
+  }
+}
+
+const char* otq_last_cuda_error(void) { return g_last_cuda; }
+
+int otq_device_check(void) { return device_ok(); }
+
+int otq_quantize_rows(const float* x, int64_t rows, int64_t n, int64_t ldx, int group,
+                      int row_mode, int8_t* q, int64_t ldq, float* S, uint8_t* d, int64_t ldd,
+                      void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (rows < 0 || n <= 0 || n > 32768 || group <= 0 || group % 32 || n % group) return kErrArg;
+  if (x == nullptr || q == nullptr || S == nullptr || ldx < n || ldq < n) return kErrArg;
+  if (!row_mode && (d == nullptr || ldd < n / group)) return kErrArg;
+  if (!aligned(x, 4)) return kErrAlign;
+  return finish(quantize_rows_launch(x, rows, static_cast<int>(n), ldx, group, row_mode, q, ldq, S,
+                                     d, ldd, 0, 0, nullptr, 0, nullptr, 0,
+                                     static_cast<cudaStream_t>(stream)));
+}
+
+int otq_pack_int8(const float* W, int64_t N, int64_t K, int64_t ldw, int rsc, uint8_t* rows,
+                  int64_t rs, uint8_t* srows, int64_t srs, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (N < 0 || K <= 0 || K % OTQ_D || K > 32768 || ldw < K) return kErrArg;
+  if (W == nullptr || rows == nullptr || srows == nullptr || rs < K) return kErrArg;
+  const int64_t need = rsc ? 4 : 4 + 4 * ((K / OTQ_D + 3) / 4);
+  if (srs < need) return kErrArg;
+  if (!aligned(srows, 4) || srs % 4) return kErrAlign;
+  return finish(quantize_rows_launch(W, N, static_cast<int>(K), ldw, OTQ_D, rsc ? 1 : 0, nullptr,
+                                     0, nullptr, nullptr, 0, 1, rsc ? 1 : 0, rows, rs, srows, srs,
+                                     static_cast<cudaStream_t>(stream)));
+}
+
+int otq_quantize_mxu(int fmt, const float* W, int64_t N, int64_t K, int64_t ldw, uint8_t* rows,
+                     int64_t rs, uint8_t* srows, int64_t srs, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (fmt_window(fmt) < 0) return kErrFormat;
+  if (N < 0 || K <= 0 || K % OTQ_D || K > 32768 || ldw < K) return kErrArg;
+  if (W == nullptr || rows == nullptr || srows == nullptr) return kErrArg;
+  const int64_t KB = K / OTQ_D;
+  const int64_t need_rs = fmt == kFmtInt8 ? K : 128 * ((K + 255) / 256);
+  const int64_t need_srs = fmt == kFmtInt8 ? 4 + 4 * ((KB + 3) / 4)
+                           : fmt == kFmtNvfp4 ? 16 + 16 * ((KB + 1) / 2)
+                                              : 8 + 8 * ((KB + 1) / 2);
+  if (rs < need_rs || srs < need_srs) return kErrArg;
+  if (!aligned(srows, scale_align(fmt, false)) || srs % scale_align(fmt, false)) return kErrAlign;
+  if (!aligned(W, 4)) return kErrAlign;
+  if (fmt == kFmtInt8)
+    return finish(quantize_rows_launch(W, N, static_cast<int>(K), ldw, OTQ_D, 0, nullptr, 0,
+                                       nullptr, nullptr, 0, 1, 0, rows, rs, srows, srs,
+                                       static_cast<cudaStream_t>(stream)));
+  return finish(pack_mx4_launch(fmt, W, N, static_cast<int>(K), ldw, rows, rs, srows, srs,
+                                static_cast<cudaStream_t>(stream)));
+}
+
+int otq_mm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows, int64_t srs,
+           int k0, int64_t N, int64_t K, const int8_t* q, int64_t ldq, const float* Sa,
+           const uint8_t* da, int64_t ldd, int64_t M, const float* alpha, float* y, int64_t ldy,
+           void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if ((st = check_weights(fmt, flags, rows, rs, srows, srs, k0, N, K))) return st;
+  if ((st = check_out(M, N, y, ldy, flags, alpha))) return st;
+  if (q == nullptr || Sa == nullptr || da == nullptr || ldq < K || ldd < K / 32) return kErrArg;
+  if (mm_smem_bytes(fmt, mt_bucket(M), static_cast<int>(K), false) > 227 * 1024) return kErrArg;
+  MMParams p{};
+  p.fmt = fmt;
+  p.flags = flags;
+  p.rows = rows;
+  p.rs = rs;
+  p.srows = srows;
+  p.srs = srs;
+  p.k0 = k0;
+  p.N = N;
+  p.K = static_cast<int>(K);
+  p.q = q;
+  p.ldq = ldq;
+  p.Sa = Sa;
+  p.da = da;
+  p.ldd = ldd;
+  p.M = static_cast<int>(M);
+  p.alpha = alpha;
+  p.y = y;
+  p.ldy = ldy;
+  return finish(mm_launch(p, static_cast<cudaStream_t>(stream), false));
+}
+
+int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+               int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx,
+               int row_mode, int64_t M, const float* alpha, float* y, int64_t ldy,
+               int k_split, int pdl, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if ((st = check_weights(fmt, flags, rows, rs, srows, srs, k0, N, K))) return st;
+  if ((st = check_out(M, N, y, ldy, flags, alpha))) return st;
+  if (x == nullptr || ldx < K) return kErrArg;
+  if (!aligned(x, 4)) return kErrAlign;
+  if (k_split != 0 && k_split != 1 && k_split != 2 && k_split != 4 && k_split != 8 &&
+      k_split != 16)
+    return kErrArg;
+  if (mm_smem_bytes(fmt, mt_bucket(M), static_cast<int>(K), true) > 227 * 1024) return kErrArg;
+  MMParams p{};
+  p.fmt = fmt;
+  p.flags = flags;
+  p.rows = rows;
+  p.rs = rs;
+  p.srows = srows;
+  p.srs = srs;
+  p.k0 = k0;
+  p.N = N;
+  p.K = static_cast<int>(K);
+  p.x = x;
+  p.ldx = ldx;
+  p.row_mode = row_mode ? 1 : 0;
+  p.M = static_cast<int>(M);
+  p.alpha = alpha;
+  p.y = y;
+  p.ldy = ldy;
+  p.lpr = k_split;
+  return finish(mm_launch(p, static_cast<cudaStream_t>(stream), pdl != 0));
+}
+
+int otq_qmm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+            int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx, int row_mode,
+            int64_t M, const float* alpha, float* y, int64_t ldy, void* stream) {
+  return otq_qmm_ex(fmt, flags, rows, rs, srows, srs, k0, N, K, x, ldx, row_mode, M, alpha, y,
+                    ldy, 0, 0, stream);
+}
+
+int otq_status_word(int* value, int reset) {
+  int st = device_ok();
+  if (st) return st;
+  if (value == nullptr) return kErrArg;
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_status_word, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e);
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_status_word, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  *value = v;
+  return kOk;
+}
+
+int otq_pack_g32(const float* W, int64_t N, int64_t K, int64_t ldw, uint8_t* codes,
+                 uint16_t* scales, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (N < 0 || K <= 0 || K % 32 || ldw < K || W == nullptr || codes == nullptr ||
+      scales == nullptr)
+    return kErrArg;
+  if (!aligned(scales, 2)) return kErrAlign;
+  return finish(pack_g32_launch(W, N, K, ldw, codes, scales, static_cast<cudaStream_t>(stream)));
+}
+
+int otq_linear_g32(const uint8_t* codes, const uint16_t* scales, int64_t N, int64_t K,
+                   const float* x, int64_t ldx, int64_t M, int accumulate, float* y, int64_t ldy,
+                   void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (N <= 0 || K <= 0 || K % 128 || K > 65536 || M <= 0 || M > 0x7FFFFFFF) return kErrArg;
+  if (codes == nullptr || scales == nullptr || x == nullptr || y == nullptr) return kErrArg;
+  if (ldx < K || ldy < N) return kErrArg;
+  if (!aligned(codes, 16) || (K / 2) % 16 || !aligned(scales, 2) || !aligned(x, 16) ||
+      ldx % 4)
+    return kErrAlign;
+  if (static_cast<int64_t>(K) * 4 * 2 > 227 * 1024) return kErrArg;
+  return finish(linear_g32_launch(codes, scales, N, static_cast<int>(K), x, ldx,
+                                  static_cast<int>(M), accumulate, y, ldy,
+                                  static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

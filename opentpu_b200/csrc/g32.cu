@@ -1,0 +1,259 @@
+// The reference's 4-bit group-32 fp16-scale weight format (its survey quantizer,
+// opentpu/quant.py:225-227 -> 132-170): the quantizer, bit-exact in float64 as the reference
+// computes it, and the weight-only linear layer over it (fp32 activations, fp32 accumulation;
+// the reference's `deq @ x`, tests/test_quant.py:276-287).
+//
+// Packed layout in HBM: codes [N, K/2] (two's-complement nibbles, element 2i in the low
+// nibble), scales [N, K/32] fp16 -- 4.5 bits a weight, streamed once per call.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "otq_internal.h"
+
+namespace otq {
+namespace {
+
+constexpr int kThreads = 256;
+
+// double -> IEEE binary16 bits, round to nearest even, for 0 <= v <= 65504 (written from the
+// format's definition: 10 fraction bits, exponent bias 15, subnormal quantum 2^-24).
+__device__ __forceinline__ uint16_t f64_to_f16_bits(double v) {
+  if (!(v > 0.0)) return 0;
+  if (v < 6.103515625e-05) {                          // below 2^-14: the subnormal grid
+    const double r = rint(v * 16777216.0);            // exact scaling by 2^24, then RNE
+    return static_cast<uint16_t>(r);                  // 1024 becomes the smallest normal
+  }
+  int e;
+  const double m = frexp(v, &e);                      // v = m 2^e, m in [0.5, 1)
+  double frac = rint((m * 2.0 - 1.0) * 1024.0);       // exact, then RNE to 10 bits
+  int ex = e - 1;
+  if (frac >= 1024.0) {
+    frac = 0.0;
+    ++ex;
+  }
+  return static_cast<uint16_t>(((ex + 15) << 10) | static_cast<int>(frac));
+}
+
+__device__ __forceinline__ double f16_bits_to_f64(uint16_t h) {
+  const int ex = (h >> 10) & 31;
+  const int fr = h & 1023;
+  if (ex == 0) return ldexp(static_cast<double>(fr), -24);
+  return ldexp(1.0 + fr / 1024.0, ex - 15);
+}
+
+// One warp per (row, group of 32): lane l holds element l.
+__global__ void __launch_bounds__(kThreads) pack_g32_kernel(const float* __restrict__ W,
+                                                            int64_t N, int64_t K, int64_t ldw,
+                                                            uint8_t* __restrict__ codes,
+                                                            uint16_t* __restrict__ scales) {
+  const int64_t ng = K / 32;
+  const int64_t task = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (task >= N * ng) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = task / ng, g = task % ng;
+  const double x = static_cast<double>(W[n * ldw + g * 32 + lane]);
+  double amax = fabs(x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmax(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  double s = fmin(amax * 1.0 / 7.0, 65504.0);
+  const uint16_t hb = f64_to_f16_bits(s);
+  s = f16_bits_to_f64(hb);
+  if (amax == 0.0 || s == 0.0) s = 1.0;
+  double c = rint(x / s);
+  c = fmin(fmax(c, -7.0), 7.0);
+  const int nib = static_cast<int>(c) & 15;
+  const int other = __shfl_down_sync(0xFFFFFFFFu, nib, 1);
+  if ((lane & 1) == 0) codes[n * (K / 2) + g * 16 + (lane >> 1)] =
+      static_cast<uint8_t>(nib | (other << 4));
+  if (lane == 0) scales[n * ng + g] = (amax == 0.0 || hb == 0) ? static_cast<uint16_t>(0x3C00) : hb;
+}
+
+struct G32Params {
+  const uint8_t* codes;
+  const uint16_t* scales;
+  int64_t N;
+  int K;
+  const float* x;
+  int64_t ldx;
+  int M;
+  int accumulate;
+  float* y;
+  int64_t ldy;
+};
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+  float f;
+  asm("{ .reg .b16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"(h));
+  return f;
+}
+
+// LPR lanes per weight row, one 16-byte chunk (a whole group) per lane step; activations of
+// MT rows in shared memory as fp32. Signed nibbles become exact floats by the 2^23 + u trick.
+template <int MT, int LPR>
+__global__ void __launch_bounds__(kThreads) linear_g32_kernel(const G32Params p) {
+  extern __shared__ __align__(16) float xs[];   // [MT][K]
+  constexpr int R = 32 / LPR;
+  constexpr int U = 4;
+  const int K = p.K;
+  const int NC = K >> 5;
+  const int lane = threadIdx.x & 31;
+  const int li = lane % LPR;
+  const int r = lane / LPR;
+  const int64_t ntasks = (p.N + R - 1) / R;
+  const int64_t wstride = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  const int64_t wfirst = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int m0 = 0; m0 < p.M; m0 += MT) {
+    const int mt = min(MT, p.M - m0);
+    for (int j = 0; j < mt; ++j)
+      for (int i = threadIdx.x; i < K; i += kThreads)
+        xs[j * K + i] = __ldcg(p.x + static_cast<int64_t>(m0 + j) * p.ldx + i);
+    __syncthreads();
+    for (int64_t t = wfirst; t < ntasks; t += wstride) {
+      const int64_t n = t * R + r;
+      const bool valid = n < p.N;
+      const uint8_t* crow = p.codes + (valid ? n : 0) * (K / 2);
+      const uint16_t* srow = p.scales + (valid ? n : 0) * NC;
+      float acc[MT];
+#pragma unroll
+      for (int j = 0; j < MT; ++j) acc[j] = 0.0f;
+      for (int c0 = li; c0 < NC; c0 += LPR * U) {
+        uint4 wv[U];
+        float sc[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int c = c0 + u * LPR;
+          const bool ok = valid && c < NC;
+          wv[u] = ok ? ld_stream(crow + static_cast<int64_t>(c) * 16) : make_uint4(0, 0, 0, 0);
+          sc[u] = ok ? half_bits_to_float(__ldg(srow + c)) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int c = c0 + u * LPR;
+          if (!valid || c >= NC) continue;
+          const uint32_t ww[4] = {wv[u].x ^ 0x88888888u, wv[u].y ^ 0x88888888u,
+                                  wv[u].z ^ 0x88888888u, wv[u].w ^ 0x88888888u};
+          float wf[32];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const uint32_t bitsv = ((ww[q] >> (4 * e)) & 0xFu) | 0x4B000000u;   // 2^23 + u
+              wf[q * 8 + e] = __fsub_rn(__uint_as_float(bitsv), 8388616.0f);     // u - 8
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < MT; ++j) {
+            if (j < mt) {
+              const float4* xp = reinterpret_cast<const float4*>(xs + j * K + c * 32);
+              float part = 0.0f;
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                const float4 xv = xp[v];
+                part = __fmaf_rn(wf[4 * v + 0], xv.x, part);
+                part = __fmaf_rn(wf[4 * v + 1], xv.y, part);
+                part = __fmaf_rn(wf[4 * v + 2], xv.z, part);
+                part = __fmaf_rn(wf[4 * v + 3], xv.w, part);
+              }
+              acc[j] = __fmaf_rn(sc[u], part, acc[j]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int off = LPR / 2; off > 0; off >>= 1) {
+#pragma unroll
+        for (int j = 0; j < MT; ++j) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], off);
+      }
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < MT; ++j) {
+          if (j < mt && (j % LPR) == li) {
+            float* yp = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
+            *yp = p.accumulate ? *yp + acc[j] : acc[j];
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <int MT, int LPR>
+int launch_g32(const G32Params& p, cudaStream_t stream) {
+  auto kern = linear_g32_kernel<MT, LPR>;
+  const size_t smem = static_cast<size_t>(MT) * p.K * 4;
+  static int configured[kMaxDevices] = {0};
+  static int occ_cache[kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return kErrCuda;
+  if (smem > 48 * 1024 && configured[dev] < static_cast<int>(smem)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return kErrCuda;
+    configured[dev] = static_cast<int>(smem);
+    occ_cache[dev] = 0;
+  }
+  if (occ_cache[dev] == 0) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess)
+      return kErrCuda;
+    occ_cache[dev] = occ > 0 ? occ : 1;
+  }
+  constexpr int R = 32 / LPR;
+  const int64_t ntasks = (p.N + R - 1) / R;
+  const int64_t want = (ntasks + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(sm_count(dev)) * occ_cache[dev];
+  return launch_kernel(reinterpret_cast<const void*>(kern), static_cast<int>(want < cap ? want : cap),
+                       kThreads, smem, stream, false, p);
+}
+
+template <int MT>
+int launch_g32_lpr(const G32Params& p, cudaStream_t stream, int lpr) {
+  switch (lpr) {
+    case 4: return launch_g32<MT, 4>(p, stream);
+    case 8: return launch_g32<MT, 8>(p, stream);
+    case 16: return launch_g32<MT, 16>(p, stream);
+    default: return launch_g32<MT, 32>(p, stream);
+  }
+}
+
+}  // namespace
+
+int pack_g32_launch(const float* W, int64_t N, int64_t K, int64_t ldw, uint8_t* codes,
+                    uint16_t* scales, cudaStream_t stream) {
+  const int64_t tasks = N * (K / 32);
+  if (tasks == 0) return kOk;
+  const int64_t blocks = (tasks + 7) / 8;
+  if (blocks > 0x7FFFFFFF) return kErrArg;
+  pack_g32_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(W, N, K, ldw, codes,
+                                                                          scales);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int linear_g32_launch(const uint8_t* codes, const uint16_t* scales, int64_t N, int K,
+                      const float* x, int64_t ldx, int M, int accumulate, float* y, int64_t ldy,
+                      cudaStream_t stream) {
+  G32Params p{codes, scales, N, K, x, ldx, M, accumulate, y, ldy};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  const int nc = K / 32;
+  int lpr = 4;
+  while (lpr < 32 && nc / lpr > 8) lpr *= 2;
+  while (lpr < 32 && N * lpr / 32 < static_cast<int64_t>(sm_count(dev)) * 16) lpr *= 2;
+  if (M <= 1) return launch_g32_lpr<1>(p, stream, lpr);
+  if (M <= 2 || static_cast<int64_t>(K) * 4 * 4 > 200 * 1024) return launch_g32_lpr<2>(p, stream, lpr);
+  return launch_g32_lpr<4>(p, stream, lpr);
+}
+
+}  // namespace otq

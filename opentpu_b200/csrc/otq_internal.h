@@ -1,0 +1,98 @@
+// Internal declarations shared by the CUDA translation units of libotq.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/otq.h"
+
+namespace otq {
+
+constexpr int kOk = OTQ_OK;
+constexpr int kErrArg = OTQ_ERR_ARG;
+constexpr int kErrAlign = OTQ_ERR_ALIGN;
+constexpr int kErrFormat = OTQ_ERR_FORMAT;
+constexpr int kErrCuda = OTQ_ERR_CUDA;
+constexpr int kErrDevice = OTQ_ERR_DEVICE;
+
+constexpr int kFmtInt8 = OTQ_FMT_INT8;
+constexpr int kFmtInt4 = OTQ_FMT_INT4;
+constexpr int kFmtFp4 = OTQ_FMT_FP4;
+constexpr int kFmtNvfp4 = OTQ_FMT_NVFP4;
+
+constexpr int kMmUnit = OTQ_MM_UNIT;
+constexpr int kMmAcc = OTQ_MM_ACC;
+constexpr int kMmAscale = OTQ_MM_ASCALE;
+constexpr int kMmRsc = OTQ_MM_RSC;
+
+constexpr int kMaxDevices = 64;
+
+// Bits of the library's device status word (otq_status_word): a bounded wait ran out.
+constexpr int kStatusTimeout = 1;
+
+// Shared-memory ring of the persistent GEMV (mm_stream.cu).
+struct RingCfg {
+  int chunk_bytes;   // bytes of a weight row per stage
+  int row_stride;    // bytes between rows in a stage (chunk + padding)
+  int ns;            // stages
+};
+
+struct MMParams {
+  int fmt;
+  int flags;
+  const uint8_t* rows;
+  int64_t rs;
+  const uint8_t* srows;
+  int64_t srs;
+  int k0;
+  int64_t N;
+  int K;
+  // activations: x (fp32, quantized by the kernel's QACT prologue) or q / Sa / da
+  const float* x;
+  int64_t ldx;
+  int row_mode;
+  const int8_t* q;
+  int64_t ldq;
+  const float* Sa;
+  const uint8_t* da;
+  int64_t ldd;
+  int M;
+  const float* alpha;
+  float* y;
+  int64_t ldy;
+  int lpr;   // K-split warps per 16-row tile (1, 2, 4, 8); 16: the ring kernel; 0: pick
+  int* status;   // device status word (may be null): kStatusTimeout bits
+};
+
+int sm_count(int dev);
+size_t mm_smem_bytes(int fmt, int mt, int K, bool fused);
+int mm_pick_split(int fmt, int64_t N, int K, int dev);
+int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);
+RingCfg ring_config(int fmt, int K, int M, bool fused);
+size_t ring_smem_bytes(int fmt, int K, int M, bool fused);
+int mm_ring_launch(const MMParams& p, cudaStream_t stream, bool pdl);
+int* status_word();   // this device's status word (device address), or null
+
+// Launch with an optional programmatic-dependent-launch attribute (the kernel then may start
+// while the previous kernel in the stream finishes; it waits with griddepcontrol.wait before
+// reading anything that kernel wrote).
+template <class P>
+int launch_kernel(const void* fn, int grid, int block, size_t smem, cudaStream_t stream, bool pdl,
+                  const P& params) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(block, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  void* args[] = {const_cast<P*>(&params)};
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+  return e == cudaSuccess ? kOk : kErrCuda;
+}
+
+}  // namespace otq

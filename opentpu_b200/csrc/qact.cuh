@@ -1,0 +1,122 @@
+// QACT / QST row quantization as a CTA-wide device routine (reference docs/isa.md
+// "Quantization"; opentpu/fp32.py:321-343 quantize_mx; opentpu/isasim.py:913-959 QACT).
+//
+// One row x[0..n) of fp32 is quantized by the whole CTA:
+//   amax = the largest |x| by bit pattern (after the flush), S = amax * f32(1/127),
+//   inv = 127 * recip(amax) (S = inv = 0 for an all-zero row);
+//   per group of g elements (g a multiple of 32): d = the group offset (0 in ROW mode),
+//   q = q8(x * (inv * 2^d)).
+// The row is first staged into shared memory with cp.async (every load in flight at once,
+// so the latency is paid once, not once per segment); pass 1 reduces each 32-element
+// segment's magnitude maximum with one warp reduction, the row maximum and the group maxima
+// come from those, and pass 2 emits the bytes through a caller functor.
+#pragma once
+#include "otq_fp32.cuh"
+
+namespace otq {
+
+// The threads that run a row quantization together: the whole CTA (BAR = 0, a CTA barrier), or
+// NT threads that meet on named barrier BAR. tid is the thread's index within the group.
+template <int NT, int BAR = 0>
+struct ThreadGroup {
+  int tid;
+  __device__ __forceinline__ void sync() const {
+    if constexpr (BAR == 0) {
+      __syncthreads();
+    } else {
+      asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+    }
+  }
+};
+
+struct QactRowResult {
+  float S;      // the row's scale
+  float inv;    // 127 * recip(amax), or 0
+  uint32_t amax_bits;
+};
+
+// Copy x[0..n) (global) into xs (shared) with cp.async, 16 bytes a copy when x is 16-byte
+// aligned, else 4. The global side is read through L2 only (.cg / .ca on the first touch): x
+// may have been written by the kernel launched just before this one. Ends with every copy
+// complete and a barrier of the group.
+template <int NT, int BAR>
+__device__ __forceinline__ void stage_row(const ThreadGroup<NT, BAR>& grp,
+                                          const float* __restrict__ x, float* xs, int n) {
+  const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(xs));
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    for (int i = grp.tid * 4; i < n; i += NT * 4)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(base + 4u * i), "l"(x + i)
+                   : "memory");
+  } else {
+    for (int i = grp.tid; i < n; i += NT)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(base + 4u * i), "l"(x + i)
+                   : "memory");
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  grp.sync();
+}
+
+// xs: the row in shared memory (stage_row); seg: shared scratch of n/32 words; red: shared
+// scratch of 40 words. All threads of the group call it; emit(i, q, d_group) is called once per
+// element i with the quantized byte and the offset of element i's group. The 32 lanes of a
+// warp call emit together for the 32 elements of one segment, so emit may use warp
+// collectives.
+template <int NT, int BAR, class Emit>
+__device__ __forceinline__ QactRowResult qact_row(const ThreadGroup<NT, BAR>& grp, const float* xs,
+                                                  int n, int g, bool row_mode, uint32_t* seg,
+                                                  uint32_t* red, Emit emit) {
+  const int lane = grp.tid & 31;
+  const int warp = grp.tid >> 5;
+  constexpr int NW = NT / 32;
+  const int nseg = n >> 5;
+  // pass 1: segment maxima
+  uint32_t tmax = 0u;
+  for (int s = warp; s < nseg; s += NW) {
+    const float v = otq_flush(xs[(s << 5) + lane]);
+    const uint32_t mb = __float_as_uint(v) & 0x7FFFFFFFu;
+    const uint32_t sm = __reduce_max_sync(0xFFFFFFFFu, mb);
+    if (lane == 0) seg[s] = sm;
+    tmax = sm > tmax ? sm : tmax;   // identical on every lane
+  }
+  if (lane == 0) red[warp] = tmax;
+  grp.sync();
+  if (warp == 0) {
+    uint32_t m = lane < NW ? red[lane] : 0u;
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if (lane == 0) {
+      float S = 0.0f, inv = 0.0f;
+      if (m != 0u) {
+        const float amax = __uint_as_float(m);
+        S = fmul(amax, __uint_as_float(kInv127Bits));
+        inv = fmul(127.0f, recip(amax));
+      }
+      red[NW] = __float_as_uint(S);
+      red[NW + 1] = __float_as_uint(inv);
+      red[NW + 2] = m;
+    }
+  }
+  grp.sync();
+  QactRowResult r;
+  r.S = __uint_as_float(red[NW]);
+  r.inv = __uint_as_float(red[NW + 1]);
+  r.amax_bits = red[NW + 2];
+  // pass 2: offsets and bytes
+  const int spg = g >> 5;   // segments per group
+  for (int s = warp; s < nseg; s += NW) {
+    int d = 0;
+    if (!row_mode) {
+      const int s0 = (s / spg) * spg;
+      uint32_t gm = 0u;
+      for (int t = 0; t < spg; ++t) gm = max(gm, seg[s0 + t]);
+      d = group_offset(gm, r.amax_bits);
+    }
+    const float scale = fmul(r.inv, pow2i(d));
+    const int i = (s << 5) + lane;
+    const int qv = q8(fmul(xs[i], scale));
+    emit(i, qv, d);
+  }
+  grp.sync();   // seg / red / xs are reused by the next row
+  return r;
+}
+
+}  // namespace otq

@@ -1,0 +1,119 @@
+"""The quantized projections of one decode token, replayed as one CUDA graph.
+
+A decoder layer's projections in the order a decode step runs them (the reference's
+qwen3_step: _attention's q/k/v/o dots, _mlp's gate/up/down, then _lm_head; qwen3.py:1550-2087):
+
+    QKV   [n_q*d + 2*n_kv*d, H]   one GEMV: q, k and v share the input and its QACT range, so
+                                  the fused rows give the same bits as three MMs
+    O     [H, n_q*d]
+    GateUp[2F, H]                 one GEMV for the same reason
+    Down  [H, F]
+and the LM head [vocab, H] after the last layer.
+
+With world > 1 every projection's rows are split over the ranks (runtime.Weight(shard=0),
+runtime.py:138-142) and an all-gather assembles each output on every rank (the reference's
+GATHER, isasim.py:1413-1438), captured in the same graph.
+
+dependent=True (the default) chains the projections through their outputs the way a decode
+step does: each projection reads the first K outputs of the previous one (QKV's q part feeds O,
+O feeds GateUp, GateUp's gate part feeds Down, Down feeds the next layer's QKV and, after the
+last layer, the head), so every launch waits for the one before it -- the serialization of a
+real decode step without the non-linear-layer ops in between. dependent=False gives every
+projection its own fixed input.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import linear
+from .workloads import DecoderShape
+
+
+class DecodeChain:
+    def __init__(self, shape: DecoderShape, fmt: str = "int8-row", head_fmt: str = "int8-row",
+                 seed: int = 0, world: int = 1, rank: int = 0, group=None, pdl: bool = True,
+                 std: float = 0.02, dependent: bool = True):
+        self.shape, self.world, self.rank, self.group, self.pdl = shape, world, rank, group, pdl
+        self.dependent = dependent
+        H, d = shape.hidden, shape.head_dim
+        qkv = shape.n_q * d + 2 * shape.n_kv * d
+        layer = [("qkv", qkv, H), ("o", H, shape.n_q * d), ("gateup", 2 * shape.ffn, H),
+                 ("down", H, shape.ffn)]
+        self.plan = [(f"layers.{i}.{n}", N, K, fmt) for i in range(shape.layers)
+                     for n, N, K in layer]
+        self.plan.append(("head", shape.vocab, H, head_fmt))
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        self.weights, self.outs, self.gathered = [], [], []
+        self.inputs: dict[int, torch.Tensor] = {}
+        self.weight_bytes = 0
+        for name, N, K, f in self.plan:
+            if N % world:
+                raise ValueError(f"{name}: {N} rows do not split over {world} ranks")
+            n = N // world
+            W = torch.randn((N, K), generator=gen, device="cuda")[rank * n:(rank + 1) * n] * std
+            w = linear.PackedWeight.from_float(W, f)
+            del W
+            self.weights.append(w)
+            self.weight_bytes += w.stream_bytes * world
+            if K not in self.inputs:
+                self.inputs[K] = torch.randn((1, K), generator=gen, device="cuda")
+            self.outs.append(torch.zeros((1, n), device="cuda"))
+            self.gathered.append(torch.zeros((world, n), device="cuda") if world > 1 else None)
+        # the input each projection reads: a fixed vector, or the previous projection's output
+        self.x_of = []
+        for i, (name, N, K, f) in enumerate(self.plan):
+            if not dependent or i == 0:
+                self.x_of.append(self.inputs[K])
+            else:
+                prev = self.full_out(i - 1)
+                if prev.shape[1] < K:
+                    raise ValueError(f"{name}: the previous output has {prev.shape[1]} < {K}")
+                self.x_of.append(prev[:, :K])
+        self.graph = None
+        self.stream = torch.cuda.Stream()
+
+    @property
+    def launches(self) -> int:
+        return len(self.plan)
+
+    def full_out(self, i: int) -> torch.Tensor:
+        """Projection i's whole output row [1, N] (the gathered one with world > 1)."""
+        return self.gathered[i].reshape(1, -1) if self.world > 1 else self.outs[i]
+
+    def step_eager(self):
+        import torch.distributed as dist
+        for x, w, y, g in zip(self.x_of, self.weights, self.outs, self.gathered):
+            linear.qlinear(x, w, out=y, pdl=self.pdl)
+            if self.world > 1:
+                dist.all_gather_into_tensor(g, y, group=self.group)
+
+    def capture(self, warmup: int = 3):
+        with torch.cuda.stream(self.stream):
+            for _ in range(warmup):
+                self.step_eager()
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.step_eager()
+        torch.cuda.synchronize()
+
+    def replay(self, n: int = 1):
+        with torch.cuda.stream(self.stream):
+            for _ in range(n):
+                self.graph.replay()
+
+    def run_host(self, inputs_host: dict, logits_host: torch.Tensor):
+        """One step from host buffers: each input vector copied from pinned host memory, the
+        graph replayed, the logits copied back (all on the chain's stream, asynchronous)."""
+        with torch.cuda.stream(self.stream):
+            for K, t in inputs_host.items():
+                if not self.dependent or K == self.plan[0][2]:
+                    self.inputs[K].copy_(t, non_blocking=True)
+            self.graph.replay()
+            logits_host.copy_(self.logits(), non_blocking=True)
+
+    def logits(self) -> torch.Tensor:
+        return self.full_out(len(self.plan) - 1)
+
+    def release(self):
+        self.graph = None

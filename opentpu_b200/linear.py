@@ -1,0 +1,258 @@
+"""The quantized linear layer as torch-level operators over libotq.
+
+Reference surface this mirrors:
+- `runtime.Weight(array, shard, fmt)` (opentpu/runtime.py:38-51) and the quantizers
+  `quant.quantize_mxu` (quant.py:510-524), `runtime.quantize_rows` (runtime.py:66-76) and
+  `quant.quantize(W, "int4", g=32, scale="fp16")` (quant.py:225-227) -> `PackedWeight`;
+- `fp32.quantize_mx` / QACT (fp32.py:321-343) -> `quantize_act`;
+- MM (isasim.py:749-910) -> `mm`; `ol.dot` of an fp32 tile (language.py:150-162, one QACT
+  over the row then one MM) -> `qlinear`.
+
+Formats: the MX formats "int8" (int8x), "int4" (int4x), "fp4" (fp4x6), "nvfp4", plus
+"int8-row" (int8 per output row with an fp32 scale: MM RSC) and "int4-g32" (4-bit, group 32,
+fp16 scale; weight-only: fp32 activations, not bit-exact by construction).
+
+Every tensor lives on a CUDA device; every call runs on torch's current stream. Nothing here
+computes on the CPU.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib as L
+
+D = 128
+MX_FORMATS = ("int8", "int4", "fp4", "nvfp4")
+FORMATS = MX_FORMATS + ("int8-row", "int4-g32")
+WINDOW = {"int8": 16, "int4": 11, "fp4": 11, "nvfp4": 13}     # opentpu/isa.py:28 MX_W
+
+
+def row_bytes(K: int, fmt: str) -> int:
+    """Streamed bytes of one weight row (quant.py:287-289; int4-g32: K/2)."""
+    if fmt in ("int8", "int8-row"):
+        return K
+    if fmt == "int4-g32":
+        return K // 2
+    return -(-K // (2 * D)) * D
+
+
+def scale_bytes(K: int, fmt: str) -> int:
+    """Bytes of one scale row (quant.py:292-309; int8-row: Sw alone; int4-g32: fp16 a group)."""
+    if K % D and fmt != "int4-g32":
+        raise ValueError(f"inner dimension {K} is not a multiple of D={D}")
+    KB = K // D
+    if fmt == "int8-row":
+        return 4
+    if fmt == "int8":
+        return 4 + 4 * -(-KB // 4)
+    if fmt in ("int4", "fp4"):
+        return 8 + 8 * -(-KB // 2)
+    if fmt == "nvfp4":
+        return 16 + 16 * -(-KB // 2)
+    if fmt == "int4-g32":
+        return 2 * (K // 32)
+    raise ValueError(f"unknown format {fmt!r}")
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _cuda(t: torch.Tensor, what: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{what} must be a CUDA tensor")
+    return t
+
+
+@dataclass
+class PackedWeight:
+    """A weight matrix [N, K] resident in HBM in one format.
+
+    MX formats: `rows` uint8 [N, rs] (rs a multiple of 16) and `srows` uint8 [N, srs] -- the
+    reference's byte layout (or srows None: UNIT, no scales); `k0` the first scale block (a
+    column part, quant.part_scales). int4-g32: `rows` the nibble codes [N, K/2] and `srows` the
+    fp16 scales [N, K/32] (torch.float16)."""
+    fmt: str
+    N: int
+    K: int
+    rows: torch.Tensor
+    srows: torch.Tensor | None
+    k0: int = 0
+    rsc: bool = False
+
+    def __post_init__(self):
+        if self.fmt == "int8-row":
+            self.rsc = True
+        if self.rsc and self.fmt in ("nvfp4", "int4-g32"):
+            raise ValueError("RSC (row scales only) does not take nvfp4 (isa.py:527)")
+
+    @property
+    def mx_fmt(self) -> str:
+        return "int8" if self.fmt == "int8-row" else self.fmt
+
+    @property
+    def flags(self) -> int:
+        f = 0
+        if self.srows is None:
+            f |= L.MM_UNIT
+        if self.rsc:
+            f |= L.MM_RSC
+        return f
+
+    @property
+    def stream_bytes(self) -> int:
+        """HBM bytes one pass over the weight reads (elements and scales actually used)."""
+        if self.srows is None:
+            s = 0
+        elif self.rsc:
+            s = 4 * self.N
+        else:
+            s = self.N * scale_bytes(self.K, self.fmt)
+        return self.N * row_bytes(self.K, self.fmt) + s
+
+    @staticmethod
+    def from_float(W: torch.Tensor, fmt: str) -> "PackedWeight":
+        """Quantize fp32 W [N, K] on the GPU into `fmt` (the reference quantizer's bytes)."""
+        if fmt not in FORMATS:
+            raise ValueError(f"Weight fmt must be one of {FORMATS}")
+        W = _cuda(W, "W")
+        if W.ndim != 2:
+            raise ValueError("Weight must be 2-D [N, K]")
+        W = W.to(torch.float32).contiguous()
+        N, K = W.shape
+        dev = W.device
+        if fmt == "int8-row":
+            rows = torch.empty((N, -(-K // 16) * 16), dtype=torch.uint8, device=dev)
+            srows = torch.empty((N, 4), dtype=torch.uint8, device=dev)
+            L.call("otq_pack_int8", W.data_ptr(), N, K, K, 1, rows.data_ptr(), rows.shape[1],
+                   srows.data_ptr(), 4, _stream())
+            return PackedWeight(fmt, N, K, rows, srows)
+        if fmt == "int4-g32":
+            codes = torch.empty((N, K // 2), dtype=torch.uint8, device=dev)
+            scales = torch.empty((N, K // 32), dtype=torch.float16, device=dev)
+            L.call("otq_pack_g32", W.data_ptr(), N, K, K, codes.data_ptr(), scales.data_ptr(),
+                   _stream())
+            return PackedWeight(fmt, N, K, codes, scales)
+        rows = torch.empty((N, -(-row_bytes(K, fmt) // 16) * 16), dtype=torch.uint8, device=dev)
+        srows = torch.empty((N, scale_bytes(K, fmt)), dtype=torch.uint8, device=dev)
+        L.call("otq_quantize_mxu", L.FMT[fmt], W.data_ptr(), N, K, K, rows.data_ptr(),
+               rows.shape[1], srows.data_ptr(), srows.shape[1], _stream())
+        return PackedWeight(fmt, N, K, rows, srows)
+
+    @staticmethod
+    def from_packed(rows, srows, fmt: str, K: int, device="cuda", k0: int = 0,
+                    rsc: bool = False) -> "PackedWeight":
+        """Wrap packed bytes (e.g. the reference's quant.quantize_mxu output) without
+        re-quantizing: copied to `device` once, padded to 16-byte row strides. rsc: the scale
+        rows are Sw alone (MM RSC)."""
+        if fmt not in FORMATS:
+            raise ValueError(f"Weight fmt must be one of {FORMATS}")
+        r = torch.as_tensor(rows).to(device)
+        N = r.shape[0]
+        if fmt != "int4-g32":
+            r = r.to(torch.uint8)
+            rs = -(-r.shape[1] // 16) * 16
+            if rs != r.shape[1]:
+                r = torch.nn.functional.pad(r, (0, rs - r.shape[1]))
+            s = None if srows is None else torch.as_tensor(srows).to(device).to(torch.uint8)
+        else:
+            r = r.to(torch.uint8)
+            s = torch.as_tensor(srows)
+            if s.dtype != torch.float16:
+                s = s.to(torch.float16)
+            s = s.to(device)
+        return PackedWeight(fmt, N, K, r.contiguous(), None if s is None else s.contiguous(), k0,
+                            rsc)
+
+    def row_slice(self, n0: int, n1: int) -> "PackedWeight":
+        """Rows n0..n1 (a row shard: runtime.Weight(shard=0), runtime.py:138-142); a view."""
+        return PackedWeight(self.fmt, n1 - n0, self.K, self.rows[n0:n1],
+                            None if self.srows is None else self.srows[n0:n1], self.k0,
+                            self.rsc)
+
+
+def _as_rows(x: torch.Tensor, K: int) -> tuple[torch.Tensor, bool]:
+    _cuda(x, "x")
+    if x.dtype != torch.float32:
+        raise ValueError("x must be float32")
+    vec = x.ndim == 1
+    x2 = x.reshape(1, -1) if vec else x
+    if x2.ndim != 2 or x2.shape[1] != K:
+        raise ValueError(f"x must be [M, {K}] (or [{K}])")
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    return x2, vec
+
+
+def quantize_act(x: torch.Tensor, row_mode: bool = False, group: int = 32):
+    """QACT of the rows of x [M, K] (fp32.quantize_mx): (q int8 [M, K], S fp32 [M],
+    d uint8 [M, K/group])."""
+    x2, _ = _as_rows(x, x.shape[-1])
+    M, K = x2.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    S = torch.empty((M,), dtype=torch.float32, device=x.device)
+    d = torch.empty((M, K // group), dtype=torch.uint8, device=x.device)
+    L.call("otq_quantize_rows", x2.data_ptr(), M, K, x2.stride(0), group, int(row_mode),
+           q.data_ptr(), K, S.data_ptr(), d.data_ptr(), K // group, _stream())
+    return q, S, d
+
+
+def _out(y, M, N, dev, need_old: bool):
+    if y is None:
+        if need_old:
+            raise ValueError("acc / alpha need `out` holding the old values")
+        return torch.empty((M, N), dtype=torch.float32, device=dev)
+    _cuda(y, "out")
+    if y.dtype != torch.float32 or y.shape[-1] != N or y.stride(-1) != 1:
+        raise ValueError(f"out must be float32 [M, {N}] with unit column stride")
+    return y.reshape(M, N) if y.ndim == 1 else y
+
+
+def mm(q, S, d, w: PackedWeight, *, out=None, acc: bool = False, alpha=None):
+    """MM of pre-quantized activations (quantize_act's) against w: y [M, N] fp32, bit-exact
+    with the reference's MM. acc: y = out + MM; alpha: y = out * alpha + MM (ASCALE: w UNIT)."""
+    if w.fmt == "int4-g32":
+        raise ValueError("int4-g32 is weight-only: use qlinear on fp32 activations")
+    M, K = q.shape
+    if K != w.K:
+        raise ValueError(f"activations have K={K}, the weight {w.K}")
+    y = _out(out, M, w.N, q.device, acc or alpha is not None)
+    flags = w.flags | (L.MM_ACC if acc or alpha is not None else 0) | \
+        (L.MM_ASCALE if alpha is not None else 0)
+    L.call("otq_mm", L.FMT[w.mx_fmt], flags, w.rows.data_ptr(), w.rows.stride(0),
+           _ptr(w.srows), 0 if w.srows is None else w.srows.stride(0), w.k0, w.N, w.K,
+           q.data_ptr(), q.stride(0), S.data_ptr(), d.data_ptr(), d.stride(0), M,
+           _ptr(alpha), y.data_ptr(), y.stride(0), _stream())
+    return y
+
+
+def qlinear(x: torch.Tensor, w: PackedWeight, *, out=None, acc: bool = False, alpha=None,
+            row_mode: bool = False, k_split: int = 0, pdl: bool = False):
+    """y = x @ W^T through the quantized weight (ol.dot on an fp32 tile).
+
+    MX formats: QACT of each row of x (offsets per 32, or ROW mode) fused with MM in one kernel,
+    bit-exact with the reference. int4-g32: weight-only, fp32 accumulation (tolerance).
+    x [M, K] or [K]; returns [M, N] (or [N]); out / acc / alpha as in `mm`. k_split: warps per
+    16-row weight tile (0 picks; results are identical for every value)."""
+    x2, vec = _as_rows(x, w.K)
+    M = x2.shape[0]
+    y = _out(out, M, w.N, x.device, acc or alpha is not None)
+    if w.fmt == "int4-g32":
+        if alpha is not None:
+            raise ValueError("int4-g32 takes no alpha")
+        L.call("otq_linear_g32", w.rows.data_ptr(), w.srows.data_ptr(), w.N, w.K, x2.data_ptr(),
+               x2.stride(0), M, int(acc), y.data_ptr(), y.stride(0), _stream())
+    else:
+        flags = w.flags | (L.MM_ACC if acc or alpha is not None else 0) | \
+            (L.MM_ASCALE if alpha is not None else 0)
+        L.call("otq_qmm_ex", L.FMT[w.mx_fmt], flags, w.rows.data_ptr(), w.rows.stride(0),
+               _ptr(w.srows), 0 if w.srows is None else w.srows.stride(0), w.k0, w.N, w.K,
+               x2.data_ptr(), x2.stride(0), int(row_mode), M, _ptr(alpha), y.data_ptr(),
+               y.stride(0), k_split, int(pdl), _stream())
+    return y.reshape(-1) if vec and out is None else y

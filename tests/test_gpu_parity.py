@@ -1,0 +1,235 @@
+"""GPU parity: libotq through its C ABI against the reference's own vectors
+(tests/golden/reference_vectors.npz, made by running the reference) and against the CPU
+oracle on seeded inputs. Integer and byte results and the MM outputs are compared bit for bit;
+the weight-only 4-bit layer within a stated float tolerance."""
+import hashlib
+
+import numpy as np
+import pytest
+
+from conftest import bits, rel
+from oracle import fp32 as F
+from oracle import mx as X
+from oracle import survey as SV
+from opentpu_b200 import workloads as WL
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+FMT_OF_WF = {0: "int8", 1: "int4", 2: "fp4", 3: "nvfp4"}
+# weight-only 4-bit: fp32 accumulation against float64, relative to max |y|
+G32_TOL = 2e-6
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.fail("these tests need a CUDA device")
+    from opentpu_b200 import linear
+    return linear
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+# ---------------------------------------------------------------------------- QACT
+@pytest.mark.parametrize("g", [32, 128])
+@pytest.mark.parametrize("row", [0, 1])
+def test_qact_matches_reference(ops, golden, g, row):
+    q, S, d = ops.quantize_act(dev(golden["qact_x"]), row_mode=bool(row), group=g)
+    assert np.array_equal(host(q), golden[f"qact_g{g}_r{row}_q"])
+    assert np.array_equal(bits(host(S)), golden[f"qact_g{g}_r{row}_S"])
+    if not row:
+        assert np.array_equal(host(d), golden[f"qact_g{g}_r{row}_d"])
+
+
+# ---------------------------------------------------------------------------- weight formats
+@pytest.mark.parametrize("fmt", X.FORMATS)
+def test_weight_quantizers_match_reference(ops, golden, fmt):
+    W = golden["fmt_W"]
+    w = ops.PackedWeight.from_float(dev(W), fmt)
+    rows, srows = host(w.rows), host(w.srows)
+    want_r, want_s = golden[f"fmt_{fmt}_rows"], golden[f"fmt_{fmt}_srows"]
+    assert np.array_equal(rows[:, :want_r.shape[1]], want_r)
+    assert np.array_equal(srows, want_s)
+
+
+def test_rsc_rows_match_reference(ops, golden):
+    w = ops.PackedWeight.from_float(dev(golden["fmt_W"]), "int8-row")
+    assert np.array_equal(host(w.rows)[:, :1024].view(np.int8), golden["fmt_rsc_q"])
+    assert np.array_equal(host(w.srows), golden["fmt_rsc_s"])
+
+
+# ---------------------------------------------------------------------------- MM programs
+def _mm_case(golden, key):
+    wf, unit, rsc, k0, KB, M, N, row_mode = (int(v) for v in golden[key + "_meta"])
+    return FMT_OF_WF[wf], bool(unit), bool(rsc), k0, KB, M, N, bool(row_mode)
+
+
+def _packed(ops, golden, key, fmt, unit, rsc, k0, K):
+    srows = None if unit else golden[key + "_srows"]
+    return ops.PackedWeight.from_packed(golden[key + "_data"], srows, fmt, K, k0=k0, rsc=rsc)
+
+
+@pytest.mark.parametrize("path", ["mm", "qmm"])
+def test_mm_programs_match_reference(ops, golden, path):
+    """Every format x UNIT / RSC / k0 / ROW case the reference ISA simulator ran at D=128:
+    MM of the simulator's own ACT bytes (path mm) and QACT+MM fused from fp32 (path qmm)."""
+    for key in [str(k) for k in golden["mm128_cases"]]:
+        fmt, unit, rsc, k0, KB, M, N, row_mode = _mm_case(golden, key)
+        K = KB * 128
+        w = _packed(ops, golden, key, fmt, unit, rsc, k0, K)
+        if path == "mm":
+            q = dev(golden[key + "_q"])
+            Sa = dev(golden[key + "_Sa"].view(np.float32))
+            da = dev(golden[key + "_da"].reshape(M, KB * 4))
+            y = ops.mm(q, Sa, da, w)
+        else:
+            y = ops.qlinear(dev(golden[key + "_x"]), w, row_mode=row_mode)
+        assert np.array_equal(bits(host(y)), golden[key + "_y"]), (key, fmt, unit, rsc, k0)
+
+
+def test_acc_and_ascale_match_reference(ops, golden):
+    k = "mm128_acc"
+    x, data, srows = golden[k + "_x"], golden[k + "_data"], golden[k + "_srows"]
+    K = x.shape[1]
+    w = ops.PackedWeight.from_packed(data, srows, "int8", K)
+    out = dev(golden[k + "_old"])
+    ops.qlinear(dev(x), w, out=out, acc=True)
+    assert np.array_equal(bits(host(out)), golden[k + "_y_acc"])
+    wu = ops.PackedWeight.from_packed(data, None, "int8", K)
+    out = dev(golden[k + "_old"])
+    ops.qlinear(dev(x), wu, out=out, alpha=dev(golden[k + "_alpha"]))
+    assert np.array_equal(bits(host(out)), golden[k + "_y_ascale"])
+
+
+@pytest.mark.parametrize("fmt", X.FORMATS)
+def test_k_dot_pipeline_matches_reference(ops, golden, fmt):
+    """runtime.launch(k_dot): quantize the weight on the GPU, QACT + MM on the GPU."""
+    x, W = golden[f"dot_{fmt}_x"], golden[f"dot_{fmt}_W"]
+    w = ops.PackedWeight.from_float(dev(W), fmt)
+    y = ops.qlinear(dev(x), w)
+    assert np.array_equal(bits(host(y)), golden[f"dot_{fmt}_y"])
+
+
+def test_config1_matches_reference(ops, golden):
+    W, x = WL.gemv_config1(0)
+    w = ops.PackedWeight.from_float(dev(W), "int8-row")
+    r, s = host(w.rows)[:, :1024], host(w.srows)
+    assert hashlib.sha256(r.tobytes() + s.tobytes()).hexdigest() == str(golden["cfg1_rsc_digest"])
+    y = ops.qlinear(dev(x), w)
+    assert np.array_equal(bits(host(y)), golden["cfg1_rsc_y"])
+    w8 = ops.PackedWeight.from_float(dev(W), "int8")
+    r, s = host(w8.rows)[:, :1024], host(w8.srows)
+    assert hashlib.sha256(r.tobytes() + s.tobytes()).hexdigest() == \
+        str(golden["cfg1_int8x_digest"])
+    assert np.array_equal(bits(host(ops.qlinear(dev(x), w8))), golden["cfg1_int8x_y"])
+
+
+# ---------------------------------------------------------------------------- vs the oracle
+SHAPES = [(1, 1, 128), (1, 5, 256), (3, 37, 384), (1, 1024, 1024), (8, 513, 1024),
+          (2, 300, 3072), (4, 64, 11008), (5, 2048, 2048), (1, 7, 32640)]
+
+
+@pytest.mark.parametrize("fmt", ["int8", "int8-row", "int4", "fp4", "nvfp4"])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_qlinear_matches_oracle(ops, fmt, M, N, K):
+    rng = np.random.default_rng(M * 1000003 + N * 131 + K)
+    if fmt == "nvfp4" and K == 32640:
+        K = 32512
+    W = WL.spread_rows(rng, N, K, 2.0, 32)
+    x = WL.spread_acts(rng, M, K, 3.0, 8)
+    w = ops.PackedWeight.from_float(dev(W), fmt)
+    mfmt = "int8" if fmt == "int8-row" else fmt
+    rows, srows = host(w.rows), host(w.srows)
+    if fmt == "int8-row":
+        want_rows, want_srows = X.quantize_rows_rsc(W)
+    else:
+        want_rows, want_srows = X.quantize_weights(W, fmt)
+    assert np.array_equal(rows[:, :want_rows.shape[1]], want_rows)
+    assert np.array_equal(srows, want_srows)
+    want = X.qlinear(x, want_rows, want_srows, mfmt, rsc=fmt == "int8-row")
+    for split in (0, 1, 8, 16):        # 16: the persistent ring kernel
+        y = ops.qlinear(dev(x), w, k_split=split, pdl=split >= 8)
+        assert np.array_equal(bits(host(y)), bits(want)), (fmt, M, N, K, split)
+    from opentpu_b200 import _lib
+    assert _lib.status_word() == 0
+    q, S, d = ops.quantize_act(dev(x))
+    qo, So, do = F.quantize_rows(x, 32)
+    assert np.array_equal(host(q), qo) and np.array_equal(bits(host(S)), bits(So))
+    assert np.array_equal(host(d), do)
+    assert np.array_equal(bits(host(ops.mm(q, S, d, w))), bits(want))
+
+
+def test_row_mode_and_k0_column_part(ops):
+    rng = np.random.default_rng(9)
+    N, K = 96, 1024
+    W = WL.spread_rows(rng, N, K, 2.0, 32)
+    x = WL.spread_acts(rng, 2, 512, 2.0, 8)
+    rows, srows = X.quantize_weights(W, "int4")
+    part = rows[:, 128:384]                         # columns 256..768: blocks 2..5
+    w = ops.PackedWeight.from_packed(part, srows, "int4", 512, k0=2)
+    want = X.qlinear(x, part, srows, "int4", k0=2, row_mode=True)
+    assert np.array_equal(bits(host(ops.qlinear(dev(x), w, row_mode=True))), bits(want))
+
+
+@pytest.mark.parametrize("fmt", ["int8-row", "int4"])
+def test_lm_head_full_size(ops, fmt):
+    """The LM head of the Qwen3-0.6B shape (151936 x 1024) at M = 1 and 8, every engine."""
+    rng = np.random.default_rng(0)
+    N, K = WL.QWEN3_0_6B.vocab, WL.QWEN3_0_6B.hidden
+    Wt = torch.randn(N, K, generator=torch.Generator().manual_seed(0)) * 0.02
+    x = rng.standard_normal((8, K)).astype(np.float32)
+    w = ops.PackedWeight.from_float(Wt.cuda(), fmt)
+    rows, srows = host(w.rows), host(w.srows)
+    want = X.qlinear(x, rows, srows, "int8" if fmt == "int8-row" else fmt,
+                     rsc=fmt == "int8-row")
+    for split in (0, 1, 16):
+        assert np.array_equal(bits(host(ops.qlinear(dev(x[:1]), w, k_split=split))),
+                              bits(want[:1])), split
+        assert np.array_equal(bits(host(ops.qlinear(dev(x), w, k_split=split))), bits(want))
+
+
+def test_errors_are_refused_on_the_host(ops):
+    w = ops.PackedWeight.from_float(torch.randn(64, 256, device="cuda"), "int8")
+    with pytest.raises(ValueError):
+        ops.qlinear(torch.randn(3, 128, device="cuda"), w)          # K mismatch
+    bad = ops.PackedWeight("nvfp4", 64, 256, w.rows, w.srows[:, :4])
+    with pytest.raises(ValueError):
+        ops.qlinear(torch.randn(1, 256, device="cuda"), bad)        # scale rows too short
+    with pytest.raises(ValueError):
+        ops.PackedWeight.from_float(torch.randn(8, 100, device="cuda"), "int8")   # K % 128
+
+
+# ---------------------------------------------------------------------------- int4-g32
+def test_g32_quantizer_matches_reference(ops, golden):
+    w = ops.PackedWeight.from_float(dev(golden["g32_W"]), "int4-g32")
+    codes = SV.unpack_g32(host(w.rows), 512).astype(np.float64)
+    scales = host(w.srows).astype(np.float64)
+    assert np.array_equal(scales, golden["g32_scales"])
+    deq = (codes.reshape(40, 16, 32) * scales[..., None]).reshape(40, 512).astype(np.float32)
+    assert np.array_equal(deq, golden["g32_deq"])
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 1024), (4, 3072, 1024), (1, 1024, 3072),
+                                   (8, 640, 8192), (2, 100, 11008), (1, 151936, 1024)])
+def test_g32_linear_within_tolerance(ops, M, N, K):
+    rng = np.random.default_rng(N + K + M)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = ops.PackedWeight.from_float(dev(W), "int4-g32")
+    codes, scales, _ = SV.quantize_g32(W)
+    assert np.array_equal(SV.unpack_g32(host(w.rows), K), codes)
+    want = SV.linear_g32(x, codes, scales)
+    got = host(ops.qlinear(dev(x), w)).astype(np.float64)
+    assert np.abs(got - want).max() <= G32_TOL * np.abs(want).max()
+    assert rel(got, want) < G32_TOL
