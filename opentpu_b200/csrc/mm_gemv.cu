@@ -32,6 +32,7 @@
 
 #include <cstdint>
 
+#include "mm_common.cuh"
 #include "otq_fp32.cuh"
 #include "otq_internal.h"
 #include "qact.cuh"
@@ -49,46 +50,6 @@ struct Fmt {
   static constexpr int kLaneBytes = (FMT == kFmtInt8) ? 8 : 4;      // what one lane reads of it
   static constexpr int kU = (FMT == kFmtInt8) ? 4 : 8;              // groups in flight per lane
 };
-
-__device__ __forceinline__ uint2 ld_stream8(const void* p) {
-  uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v2.u32 {%0,%1}, [%2];"
-               : "=r"(v.x), "=r"(v.y)
-               : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ uint32_t ld_stream4(const void* p) {
-  uint32_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-
-// Bring [p, p + bytes) into L2 (bytes a multiple of 16, p 16-byte aligned).
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// D = A (16x32 s8, row) * B (32x8 s8, col), exact int32 (the C input is zero).
-__device__ __forceinline__ void imma(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                     uint32_t b0, uint32_t b1, int (&d)[4]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%10,%10,%10};"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-}
 
 // Shared memory of a CTA.
 struct Smem {
@@ -212,27 +173,6 @@ __device__ void load_activations(const MMParams& p, const Smem& s, int m0, int m
   __syncthreads();
 }
 
-// E2M1 codes (stored doubled: {0,1,2,3,4,6,8,12}, sign in bit 3) of one 8-nibble word ->
-// exact signed bytes: elements 0..3 in lo, 4..7 in hi.
-__device__ __forceinline__ void fp4_bytes(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  constexpr uint32_t kPosLo = 0x03020100u, kPosHi = 0x0C080604u;   // +0 +1 +2 +3 | +4 +6 +8 +12
-  constexpr uint32_t kNegLo = 0xFDFEFF00u, kNegHi = 0xF4F8FAFCu;   // -0 -1 -2 -3 | -4 -6 -8 -12
-  const uint32_t sel_lo = w & 0x7777u, sel_hi = (w >> 16) & 0x7777u;
-  const uint32_t w4 = w << 4;
-  const uint32_t s_lo = prmt(w4, w, 0xD9C8u);   // nibble k's sign bit replicated over byte k
-  const uint32_t s_hi = prmt(w4, w, 0xFBEAu);
-  lo = (prmt(kPosLo, kPosHi, sel_lo) & ~s_lo) | (prmt(kNegLo, kNegHi, sel_lo) & s_lo);
-  hi = (prmt(kPosLo, kPosHi, sel_hi) & ~s_hi) | (prmt(kNegLo, kNegHi, sel_hi) & s_hi);
-}
-
-// int4 two's-complement nibbles of one word -> value + 8 (0..15) as bytes: the even elements
-// (low nibbles) in lo, the odd ones in hi.
-__device__ __forceinline__ void int4_bytes(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t x8 = w ^ 0x88888888u;
-  lo = x8 & 0x0F0F0F0Fu;
-  hi = (x8 >> 4) & 0x0F0F0F0Fu;
-}
-
 // The scale data of (row, group G): int8 the block's dw byte, int4 / fp4 the block's word,
 // nvfp4 the sub-block's two E4M3 bytes.
 template <int FMT>
@@ -244,11 +184,6 @@ __device__ __forceinline__ uint32_t load_scale(const uint8_t* srow, int k0, int 
   } else {
     return __ldg(reinterpret_cast<const uint16_t*>(srow + 16 + 8 * (k0 + (G >> 2)) + 2 * (G & 3)));
   }
-}
-
-__device__ __forceinline__ int shifted(int m, int shA, int dw) {
-  const int sh = shA - dw;
-  return sh >= 0 ? (m << sh) : 0;
 }
 
 // One lane's registers for one group: weight words of rows g and g+8, and their scale data.
@@ -357,15 +292,10 @@ __device__ __forceinline__ void mma_group(const Smem& s, int G, int lane, const 
     const int A0 = s.gA[G * MT + cc0], A1 = s.gA[G * MT + cc1];
     int mg0 = 1, mg1 = 1, mh0 = 1, mh1 = 1, dg0 = 0, dg1 = 0, dh0 = 0, dh1 = 0;
     if constexpr (!PLAIN) {
-      auto e4 = [](uint32_t e, int& m, int& dw) {
-        const int E = (e >> 3) & 15;
-        m = E ? 8 + static_cast<int>(e & 7u) : static_cast<int>(e & 7u);
-        dw = 15 - max(E, 1);
-      };
-      e4(sl.sc[0] & 0xFFu, mg0, dg0);
-      e4((sl.sc[0] >> 8) & 0xFFu, mg1, dg1);
-      e4(sl.sc[1] & 0xFFu, mh0, dh0);
-      e4((sl.sc[1] >> 8) & 0xFFu, mh1, dh1);
+      e4m3_term(sl.sc[0] & 0xFFu, mg0, dg0);
+      e4m3_term((sl.sc[0] >> 8) & 0xFFu, mg1, dg1);
+      e4m3_term(sl.sc[1] & 0xFFu, mh0, dh0);
+      e4m3_term((sl.sc[1] >> 8) & 0xFFu, mh1, dh1);
     }
     acc[0] += static_cast<long long>(d0[0]) * shifted(mg0, A0, dg0) +
               static_cast<long long>(d1[0]) * shifted(mg1, A0, dg1);
@@ -592,13 +522,26 @@ int mm_launch(const MMParams& p0, cudaStream_t stream, bool pdl) {
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
   MMParams p = p0;
   p.status = status_word();
-  // large matrices: the persistent ring kernel (its smem permitting); small ones: K-split tiles
-  const int64_t ntiles = (p.N + 15) / 16;
-  const bool ring_fits = ring_smem_bytes(p.fmt, p.K, p.M, p.x != nullptr) <= 227 * 1024;
-  if (ring_fits && (p.lpr == 16 || (p.lpr == 0 && p.M <= 8 && ntiles >= 2 * sm_count(dev))))
+  const bool fused = p.x != nullptr;
+  int kernel = p.kernel;
+  if (kernel == kKernelAuto) {
+    // one or two activation rows: row spans (contiguous loads, few instructions a byte); more:
+    // 16-row tiles, whose MMA serves up to 8 activation rows at once
+    kernel = (p.M <= 2 && rows_smem_bytes(p.M, p.K, fused) <= 227 * 1024) ? kKernelRows
+                                                                            : kKernelTile;
+  }
+  if (kernel == kKernelGemv) return gemv_launch(p, stream, pdl, p.split);
+  if (kernel == kKernelRows) {
+    if (rows_smem_bytes(p.M <= 1 ? 1 : 2, p.K, fused) > 227 * 1024) return kErrArg;
+    return mm_rows_launch(p, stream, pdl, p.split);
+  }
+  if (kernel == kKernelRing) {
+    if (ring_smem_bytes(p.fmt, p.K, p.M, fused) > 227 * 1024) return kErrArg;
     return mm_ring_launch(p, stream, pdl);
-  // (a ring that does not fit next to a long activation row falls back to the tile kernel)
-  const int split = (p.lpr > 0 && p.lpr < 16) ? p.lpr : mm_pick_split(p.fmt, p.N, p.K, dev);
+  }
+  const int mt = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
+  if (mm_smem_bytes(p.fmt, mt, p.K, fused) > 227 * 1024) return kErrArg;
+  const int split = p.split > 0 ? p.split : mm_pick_split(p.fmt, p.N, p.K, dev);
   switch (p.fmt) {
     case kFmtInt8: return launch_fmt<kFmtInt8>(p, stream, pdl, split);
     case kFmtInt4: return launch_fmt<kFmtInt4>(p, stream, pdl, split);
