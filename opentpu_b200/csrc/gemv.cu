@@ -7,12 +7,13 @@
 //   y   = (i2f(acc) * Sw[n]) * (Sa[j] * 2^-W)      -- otq_fp32.cuh mm_epilogue
 //
 // Streaming. Each warp owns a contiguous range of weight rows (ranges balanced by rows) and walks
-// it in blocks of R rows, 128-byte chunks of K at a time. The chunks go through a ring of NS
-// shared-memory stages with cp.async (16 bytes a lane, 512 contiguous bytes a warp instruction,
-// nothing held in registers while in flight; cp.async.wait_group is a hardware wait), so each warp
-// keeps NS - 1 chunks of R rows in flight. Stage rows are padded to 160 bytes, which makes the
-// fragment reads below conflict free. The first stages are issued before griddepcontrol.wait:
-// weights never depend on the kernel launched before this one.
+// it in blocks of R rows, one 128-byte chunk of K at a time. A chunk of the block's rows moves
+// into one stage of the warp's ring of NS shared-memory stages by 2-D tensor copies (the TMA
+// engine, one instruction for 8 rows x 128 bytes, 128-byte swizzle so that the 8-row fragment
+// reads below are free of bank conflicts), completing on the stage's mbarrier; NS - 1 chunks stay
+// in flight while one is computed. The first stages are issued before griddepcontrol.wait:
+// weights never depend on the kernel launched before this one. MX scale data (a few bytes a row
+// and chunk) comes with cp.async. Every mbarrier wait is bounded (mm_common.cuh).
 //
 // Dot products: one mma.sync m16n8k32 (s8 x s8 -> s32) takes one 32-element group of 8 weight
 // rows (B, one row a column: lane (g, t) supplies row g's bytes [8t, 8t+8) of the group) against
@@ -22,9 +23,9 @@
 // Class path (RSC / UNIT rows, one activation row, every group's offset representable): a
 // group's multiplier 2^(W - da) depends on the activation alone, so A row c carries the bytes of
 // the groups whose offset da is c (zeros elsewhere) and the MMA accumulates every group of a row
-// exactly in int32 (|sum| < 2^31 for K <= 32640). At the end of a row block each class is scaled
-// once by 2^(W - c) into int64 and the 8 class rows are summed across lanes. Groups below the
-// window (sh < 0) are in no class: they are dropped.
+// exactly in int32 (|sum| < 2^31 for K <= 32640). The A fragments are built once per CTA. At the
+// end of a row block each class is scaled once by 2^(W - c) into int64 and the 8 class rows are
+// summed across lanes. Groups below the window (sh < 0) are in no class: they are dropped.
 //
 // General path (MX rows with per-block weight offsets, several activation rows, or an int8 row
 // whose offset 16 has no class row): A row j is activation row j; each group's int32 result is
@@ -33,7 +34,9 @@
 //
 // Rows with few outputs split K: S warps of a CTA take the same rows, each a range of chunks,
 // and add their int64 partials through shared memory.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <cstdint>
 
@@ -47,75 +50,88 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kChunk = 128;           // bytes of a weight row in one stage
-constexpr int kPitch = kChunk + 32;   // a stage row: conflict-free 8-row fragment reads
+constexpr int kChunk = 128;   // bytes of a weight row in one stage
+constexpr int kBox = 8;       // rows of one tensor copy (8 x 128 bytes: one swizzle atom)
+constexpr int kActPad = 16;   // activation row pitch = K (padded) + 16: conflict-free 8-row reads
 
 template <int FMT>
 struct GF {
   static constexpr int kW = (FMT == kFmtInt8) ? 16 : (FMT == kFmtNvfp4 ? 13 : 11);
   static constexpr int kElems = (FMT == kFmtInt8) ? 128 : 256;   // elements of a chunk
   static constexpr int kGroups = kElems / 32;
-  static constexpr int kGroupBytes = (FMT == kFmtInt8) ? 32 : 16;
-  static constexpr int kBlocks = kElems / 128;
 };
 
-// A stage: R rows x kPitch, then (MX rows) 16 bytes of scale data a row.
+// A stage: R rows x 128 bytes (1024-byte aligned, 128-byte swizzle), and (MX rows) a scale stage
+// of 16 bytes a row.
 template <int R, bool PLAIN>
 struct Stage {
-  static constexpr int kScaleOff = R * kPitch;
-  static constexpr int kBytes = kScaleOff + (PLAIN ? 0 : R * 16);
+  static constexpr int kBytes = R * kChunk;
+  static constexpr int kScaleBytes = PLAIN ? 0 : R * 16;
 };
 
 struct GSmem {
-  uint8_t* act;      // [MT][KP] activation bytes (int4: each run of 8 as evens, then odds)
-  int* term;         // [MT][KG] general path: a group's activation-side term (group_term)
+  uint8_t* act;      // [MT][ap] activation bytes (int4: each run of 8 as evens, then odds)
+  int* term;         // [KG][MT] general path: a group's activation-side term (group_term)
   uint8_t* cls;      // [KG] class path: the group's class (its offset), 255 = dropped
+  uint4* afrag;      // [KG][32] class path: each lane's A fragment of each group
   float* Sa;         // [MT]
   int* flag;         // [1] 1: some group of activation row 0 has no class
   long long* red;    // [kWarps][32][VPL] K-split partials
   float* xs;         // [K] the fp32 row being quantized (fused QACT)
   uint32_t* seg;     // [K / 32]
   uint32_t* qred;    // [40]
-  uint8_t* ring;     // [kWarps][NS][stage]
+  uint64_t* bar;     // [kWarps][NS] stage barriers
+  uint8_t* sring;    // [kWarps][NS][scale stage]
+  uint8_t* ring;     // [kWarps][NS][stage], 1024-byte aligned
 };
 
-__host__ __device__ inline size_t gemv_layout(int MT, int K, int kp, bool fused, int vpl, int S,
-                                              int stage_bytes, int ns, size_t* offs) {
-  const size_t KG = K / 32;
+struct GLayout {
+  int MT, K, ap, vpl, S, stage_bytes, scale_bytes, ns;
+  bool fused, frag;
+};
+
+__host__ __device__ inline size_t gemv_layout(const GLayout& L, size_t* offs) {
+  const size_t KG = L.K / 32;
   size_t off = 0;
   auto take = [&](int i, size_t bytes) {
     off = (off + 15) & ~size_t(15);
     if (offs) offs[i] = off;
     off += bytes;
   };
-  take(0, static_cast<size_t>(MT) * kp);
-  take(1, static_cast<size_t>(MT) * KG * 4);
+  take(0, static_cast<size_t>(L.MT) * L.ap);
+  take(1, static_cast<size_t>(L.MT) * KG * 4);
   take(2, KG);
-  take(3, MT * 4);
-  take(4, 16);
-  take(5, S > 1 ? static_cast<size_t>(kWarps) * 32 * vpl * 8 : 0);
-  take(6, fused ? static_cast<size_t>(K) * 4 : 0);
-  take(7, KG * 4);
-  take(8, 40 * 4);
-  take(9, static_cast<size_t>(kWarps) * ns * stage_bytes);
+  take(3, L.frag ? KG * 32 * 16 : 0);
+  take(4, L.MT * 4);
+  take(5, 16);
+  take(6, L.S > 1 ? static_cast<size_t>(kWarps) * 32 * L.vpl * 8 : 0);
+  take(7, L.fused ? static_cast<size_t>(L.K) * 4 : 0);
+  take(8, KG * 4);
+  take(9, 40 * 4);
+  take(10, static_cast<size_t>(kWarps) * L.ns * 8);
+  take(11, static_cast<size_t>(kWarps) * L.ns * L.scale_bytes);
+  take(12, static_cast<size_t>(kWarps) * L.ns * L.stage_bytes + 1024);   // + alignment slack
   return off;
 }
 
-__device__ __forceinline__ GSmem gemv_carve(unsigned char* base, int MT, int K, int kp, bool fused,
-                                            int vpl, int S, int stage_bytes, int ns) {
-  size_t o[10];
-  gemv_layout(MT, K, kp, fused, vpl, S, stage_bytes, ns, o);
+__device__ __forceinline__ GSmem gemv_carve(unsigned char* base, const GLayout& L) {
+  size_t o[13];
+  gemv_layout(L, o);
   GSmem s;
   s.act = base + o[0];
   s.term = reinterpret_cast<int*>(base + o[1]);
   s.cls = base + o[2];
-  s.Sa = reinterpret_cast<float*>(base + o[3]);
-  s.flag = reinterpret_cast<int*>(base + o[4]);
-  s.red = reinterpret_cast<long long*>(base + o[5]);
-  s.xs = reinterpret_cast<float*>(base + o[6]);
-  s.seg = reinterpret_cast<uint32_t*>(base + o[7]);
-  s.qred = reinterpret_cast<uint32_t*>(base + o[8]);
-  s.ring = base + o[9];
+  s.afrag = reinterpret_cast<uint4*>(base + o[3]);
+  s.Sa = reinterpret_cast<float*>(base + o[4]);
+  s.flag = reinterpret_cast<int*>(base + o[5]);
+  s.red = reinterpret_cast<long long*>(base + o[6]);
+  s.xs = reinterpret_cast<float*>(base + o[7]);
+  s.seg = reinterpret_cast<uint32_t*>(base + o[8]);
+  s.qred = reinterpret_cast<uint32_t*>(base + o[9]);
+  s.bar = reinterpret_cast<uint64_t*>(base + o[10]);
+  s.sring = base + o[11];
+  const uint32_t r = smem_addr(base + o[12]);
+  s.ring = base + o[12] + (((r + 1023u) & ~1023u) - r);
   return s;
 }
 
@@ -142,65 +158,107 @@ __device__ __forceinline__ int group_term(int da) {
   }
 }
 
+// Class path: a group's class (its offset), or 255 where it has none: above W it is below the
+// window (dropped); the int8 offset 16 (multiplier 1) has no class row.
+template <int FMT>
+__device__ __forceinline__ int class_of(int da) {
+  return (da <= GF<FMT>::kW && da < 16) ? da : 255;
+}
+
 template <int FMT, int MT, bool PLAIN>
-__device__ __forceinline__ void put_group(const GSmem& s, int KG, int j, int G, int da) {
-  s.term[j * KG + G] = group_term<FMT, PLAIN>(da);
+__device__ __forceinline__ void put_group(const GSmem& s, int j, int G, int da) {
+  s.term[G * MT + j] = group_term<FMT, PLAIN>(da);
   if (j == 0) {
-    const int W = GF<FMT>::kW;
-    int c = da <= W ? da : 255;   // above W: below the window, dropped
-    if (c == 16) {                // int8 offset 16 (multiplier 1): no class row for it
-      c = 255;
-      *s.flag = 1;
-    }
-    s.cls[G] = static_cast<uint8_t>(c);
+    if (da == 16 && FMT == kFmtInt8) *s.flag = 1;
+    s.cls[G] = static_cast<uint8_t>(class_of<FMT>(da));
   }
 }
 
 // Activation rows [m0, m0 + mt) into shared memory (QACT of fp32 x, or copied bytes). Bytes past
-// K, and rows mt..MT-1, are zeros.
+// K, and rows mt..MT-1, are zeros. With `frag`, the class path's A fragments as well.
 template <int FMT, int MT, bool PLAIN>
-__device__ void gemv_load_activations(const MMParams& p, const GSmem& s, int m0, int mt, int kp) {
+__device__ void gemv_load_activations(const MMParams& p, const GSmem& s, int m0, int mt, int kp,
+                                      int ap, bool frag) {
   const int K = p.K, KG = K / 32;
   if (threadIdx.x == 0) *s.flag = 0;
   for (int j = 0; j < MT; ++j) {
     const int from = j < mt ? K : 0;
-    uint32_t* aw = reinterpret_cast<uint32_t*>(s.act + static_cast<size_t>(j) * kp);
+    uint32_t* aw = reinterpret_cast<uint32_t*>(s.act + static_cast<size_t>(j) * ap);
     for (int i = (from >> 2) + threadIdx.x; i < (kp >> 2); i += kThreads) aw[i] = 0u;
     if (j >= mt)
-      for (int G = threadIdx.x; G < KG; G += kThreads) s.term[j * KG + G] = 0;
+      for (int G = threadIdx.x; G < KG; G += kThreads) s.term[G * MT + j] = 0;
   }
   if (threadIdx.x < MT && static_cast<int>(threadIdx.x) >= mt) s.Sa[threadIdx.x] = 0.0f;
   __syncthreads();   // flag cleared before any group can set it
   if (p.x != nullptr) {
-    const ThreadGroup<kThreads> grp{static_cast<int>(threadIdx.x)};
+    if (frag)   // the class path's A fragments start as zeros (ordered before the emits below
+                // by the first barrier of qact_row4)
+      for (int i = threadIdx.x; i < KG * 32; i += kThreads) s.afrag[i] = make_uint4(0u, 0u, 0u, 0u);
     for (int j = 0; j < mt; ++j) {
-      stage_row(grp, p.x + static_cast<int64_t>(m0 + j) * p.ldx, s.xs, K);
-      uint8_t* arow = s.act + static_cast<size_t>(j) * kp;
-      QactRowResult r = qact_row(grp, s.xs, K, 32, p.row_mode != 0, s.seg, s.qred,
-                                 [&](int i, int qv, int d) {
-                                   arow[act_pos<FMT>(i)] = static_cast<uint8_t>(static_cast<int8_t>(qv));
-                                   if ((threadIdx.x & 31) == 0) put_group<FMT, MT, PLAIN>(s, KG, j, i >> 5, d);
-                                 });
+      const float* xr = p.x + static_cast<int64_t>(m0 + j) * p.ldx;
+      const bool x4 = (reinterpret_cast<uintptr_t>(xr) & 15u) == 0;
+      uint8_t* arow = s.act + static_cast<size_t>(j) * ap;
+      QactRowResult r = qact_row4<kThreads>(
+          xr, x4, s.xs, K, p.row_mode != 0, s.seg, s.qred,
+          [&](int i, int q0, int q1, int q2, int q3, int d) {
+            const int G = i >> 3;
+            if ((threadIdx.x & 7) == 0) put_group<FMT, MT, PLAIN>(s, j, G, d);
+            const uint32_t packed = (q0 & 0xFFu) | ((q1 & 0xFFu) << 8) | ((q2 & 0xFFu) << 16) |
+                                    (static_cast<uint32_t>(q3 & 0xFF) << 24);
+            const int c = class_of<FMT>(d);
+            // lane (g, t) of the group holds its bytes [8t, 8t+8) in A row g (class g) or g + 8
+            uint8_t* fb = reinterpret_cast<uint8_t*>(s.afrag + G * 32);
+            const int cg = 4 * (c & 7), ch = c >= 8 ? 4 : 0;
+            if constexpr (FMT == kFmtInt4) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int pos = act_pos<FMT>(4 * i + k);
+                const uint8_t b = static_cast<uint8_t>((packed >> (8 * k)) & 0xFFu);
+                arow[pos] = b;
+                if (frag && j == 0 && c != 255) {
+                  const int e = pos & 31;
+                  fb[(cg + (e >> 3)) * 16 + ((e & 7) >= 4 ? 8 : 0) + ch + (e & 3)] = b;
+                }
+              }
+            } else {
+              *reinterpret_cast<uint32_t*>(arow + 4 * i) = packed;
+              if (frag && j == 0 && c != 255) {
+                const int e = (4 * i) & 31;   // a whole aligned word of lane t = e / 8
+                *reinterpret_cast<uint32_t*>(fb + (cg + (e >> 3)) * 16 + ((e & 7) >= 4 ? 8 : 0) + ch) = packed;
+              }
+            }
+          });
       if (threadIdx.x == 0) s.Sa[j] = r.S;
     }
   } else {
     for (int j = 0; j < mt; ++j) {
       const int8_t* qr = p.q + static_cast<int64_t>(m0 + j) * p.ldq;
       const uint8_t* dr = p.da + static_cast<int64_t>(m0 + j) * p.ldd;
-      uint8_t* arow = s.act + static_cast<size_t>(j) * kp;
+      uint8_t* arow = s.act + static_cast<size_t>(j) * ap;
       for (int i = threadIdx.x; i < K; i += kThreads)
         arow[act_pos<FMT>(i)] = static_cast<uint8_t>(__ldcg(qr + i));
-      for (int G = threadIdx.x; G < KG; G += kThreads) put_group<FMT, MT, PLAIN>(s, KG, j, G, __ldcg(dr + G));
+      for (int G = threadIdx.x; G < KG; G += kThreads) put_group<FMT, MT, PLAIN>(s, j, G, __ldcg(dr + G));
       if (threadIdx.x == 0) s.Sa[j] = __ldcg(p.Sa + m0 + j);
     }
   }
   __syncthreads();
+  if (frag && p.x == nullptr) {
+    // lane (g, t) of group G: the 8 bytes it holds of the group in row g (class g) or row g + 8
+    for (int i = threadIdx.x; i < KG * 32; i += kThreads) {
+      const int G = i >> 5, lane = i & 31, g = lane >> 2, t = lane & 3;
+      const uint2 q = *reinterpret_cast<const uint2*>(s.act + 32 * G + 8 * t);
+      const int c = s.cls[G];
+      uint4 a;
+      a.x = c == g ? q.x : 0u;
+      a.y = c == g + 8 ? q.x : 0u;
+      a.z = c == g ? q.y : 0u;
+      a.w = c == g + 8 ? q.y : 0u;
+      s.afrag[i] = a;
+    }
+    __syncthreads();
+  }
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(dst), "l"(src)
-               : "memory");
-}
 __device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -215,59 +273,67 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Copy chunk kc of rows [row0, row0 + nrows) (nrows <= R) into a stage (shared address st).
-// Rows past nrows and the part of a chunk past K are not copied: the stage keeps stale bytes
-// there, which meet zero activation bytes or are never stored.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Issue chunk kc of rows [row0, row0 + nrows) (0 <= nrows <= R) into a stage (shared address st,
+// barrier bar): lane 0 arrives announcing the bytes, then lane j copies the box of rows
+// row0 + 8j .. + 7 (rows past the matrix and columns past the row's bytes read as zeros; rows
+// of the next worker are loaded and never stored). MX scale data goes by cp.async into the scale
+// stage sst, one commit group per issue.
 template <int FMT, int R, bool PLAIN>
-__device__ __forceinline__ void gemv_issue(uint32_t st, const MMParams& p, int64_t row0, int nrows,
-                                           int kc, int lane) {
-  using F = GF<FMT>;
-  const int c = lane & 7, sub = lane >> 3;   // 16-byte piece c of row sub (+ 4i)
-  if (kc * F::kElems + c * (F::kElems / 8) < p.K) {
-    const uint8_t* src = p.rows + (row0 + sub) * p.rs + static_cast<int64_t>(kc) * kChunk + 16 * c;
-    const uint32_t dst = st + sub * kPitch + 16 * c;
-#pragma unroll
-    for (int i = 0; i < R / 4; ++i)
-      if (4 * i + sub < nrows) cp_async16(dst + 4 * i * kPitch, src + 4 * i * p.rs);
-  }
+__device__ __forceinline__ void gemv_issue(uint32_t st, uint32_t sst, uint32_t bar,
+                                           const CUtensorMap* map, const MMParams& p, int64_t row0,
+                                           int nrows, int kc, int lane) {
+  const int boxes = (nrows + kBox - 1) / kBox;
+  if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(boxes * kBox * kChunk));
+  __syncwarp();
+  if (lane < boxes)
+    tma_load_2d(st + lane * kBox * kChunk, map, kc * kChunk, static_cast<int>(row0) + kBox * lane, bar);
   if constexpr (!PLAIN) {
+    if (lane < nrows) {
+      const uint8_t* srow = p.srows + (row0 + lane) * p.srs;
+      const uint32_t dst = sst + lane * 16;
+      const int KB = p.K / 128;
+      if constexpr (FMT == kFmtInt8) {
+        cp_async4(dst, srow + ((4 + p.k0 + kc) & ~3));
+      } else {
 #pragma unroll
-    for (int r0 = 0; r0 < R; r0 += 32) {
-      const int r = r0 + lane;
-      if (r < R && r < nrows) {
-        const uint8_t* srow = p.srows + (row0 + r) * p.srs;
-        const uint32_t dst = st + Stage<R, PLAIN>::kScaleOff + r * 16;
-        const int KB = p.K / 128;
-        if constexpr (FMT == kFmtInt8) {
-          cp_async4(dst, srow + ((4 + p.k0 + kc) & ~3));
-        } else {
-#pragma unroll
-          for (int b = 0; b < 2; ++b) {
-            const int blk = 2 * kc + b;
-            if (blk < KB) {
-              if constexpr (FMT == kFmtNvfp4) {
-                cp_async8(dst + 8 * b, srow + 16 + 8 * (p.k0 + blk));
-              } else {
-                cp_async4(dst + 4 * b, srow + 8 + 4 * (p.k0 + blk));
-              }
+        for (int b = 0; b < 2; ++b) {
+          const int blk = 2 * kc + b;
+          if (blk < KB) {
+            if constexpr (FMT == kFmtNvfp4) {
+              cp_async8(dst + 8 * b, srow + 16 + 8 * (p.k0 + blk));
+            } else {
+              cp_async4(dst + 4 * b, srow + 8 + 4 * (p.k0 + blk));
             }
           }
         }
       }
     }
+    cp_async_commit();
   }
 }
 
 // Row g's bytes of group s of a stage for lane (g, t), as the B fragment of one MMA (two for
 // nvfp4, whose 16-element sub-blocks are lanes t < 2 and t >= 2).
+// row: the row's 128 bytes in a stage, whose 16-byte pieces are swizzled by g (the row's index
+// in its 8-row box).
 template <int FMT>
-__device__ __forceinline__ void b_frag(const uint8_t* row, int s, int t, uint32_t& b0, uint32_t& b1) {
+__device__ __forceinline__ void b_frag(const uint8_t* row, int s, int g, int t, uint32_t& b0,
+                                       uint32_t& b1) {
   if constexpr (FMT == kFmtInt8) {
-    const uint2 v = *reinterpret_cast<const uint2*>(row + 32 * s + 8 * t);
+    const int piece = (2 * s + (t >> 1)) ^ g;
+    const uint2 v = *reinterpret_cast<const uint2*>(row + 16 * piece + 8 * (t & 1));
     b0 = v.x;
     b1 = v.y;
   } else {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + 16 * s + 4 * t);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + 16 * (s ^ g) + 4 * t);
     if constexpr (FMT == kFmtInt4) {
       b0 = (w << 4) & 0xF0F0F0F0u;   // even elements, 16x
       b1 = w & 0xF0F0F0F0u;          // odd elements, 16x
@@ -311,23 +377,43 @@ __device__ __forceinline__ long long class_reduce(long long (&v)[NO][2], int lan
   return u[0];
 }
 
-// The multiplier of (weight row, group s of the chunk) for the general path: ta is the
-// activation-side term, sc the row's scale data in the stage.
+// Scale data of one weight row for one chunk (general path, MX rows), decoded per group.
+template <int FMT>
+struct RowScale {
+  uint32_t w[FMT == kFmtInt8 ? 1 : (FMT == kFmtNvfp4 ? 4 : 2)];
+};
+
+template <int FMT>
+__device__ __forceinline__ void read_row_scale(RowScale<FMT>& r, const uint8_t* sc, int k0, int kc) {
+  if constexpr (FMT == kFmtInt8) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(sc);
+    r.w[0] = min((w >> (8 * ((4 + k0 + kc) & 3))) & 0xFFu, 31u);   // dw, clamped below 32
+  } else if constexpr (FMT == kFmtNvfp4) {
+    const uint4 v = *reinterpret_cast<const uint4*>(sc);
+    r.w[0] = v.x;
+    r.w[1] = v.y;
+    r.w[2] = v.z;
+    r.w[3] = v.w;
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(sc);
+    r.w[0] = v.x;
+    r.w[1] = v.y;
+  }
+}
+
+// The multipliers of (weight row, group s of the chunk): ta the activation-side term; m1 is the
+// second sub-block's (nvfp4).
 template <int FMT, bool PLAIN>
-__device__ __forceinline__ void general_mult(const uint8_t* sc, int s, int k0, int kc, int ta,
-                                             int& m0, int& m1) {
+__device__ __forceinline__ void general_mult(const RowScale<FMT>& r, int s, int ta, int& m0, int& m1) {
   if constexpr (PLAIN) {
     m0 = m1 = ta;
   } else if constexpr (FMT == kFmtInt8) {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(sc);
-    const int dw = min(static_cast<int>((w >> (8 * ((4 + k0 + kc) & 3))) & 0xFFu), 31);
-    m0 = m1 = ta >> dw;   // ta < 2^17: shifts of 17 or more give 0
+    m0 = m1 = ta >> r.w[0];   // ta < 2^17: shifts of 17 or more give 0
   } else if constexpr (FMT == kFmtInt4 || FMT == kFmtFp4) {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(sc + 4 * (s >> 2));
-    const int sub = s & 3;
-    m0 = m1 = shifted(static_cast<int>((w >> (8 + 6 * sub)) & 63u), ta, static_cast<int>(w & 0xFFu));
+    const uint32_t w = r.w[s >> 2];
+    m0 = m1 = shifted(static_cast<int>((w >> (8 + 6 * (s & 3))) & 63u), ta, static_cast<int>(w & 0xFFu));
   } else {
-    const uint32_t e = *reinterpret_cast<const uint16_t*>(sc + 8 * (s >> 2) + 2 * (s & 3));
+    const uint32_t e = (r.w[2 * (s >> 2) + ((s & 3) >> 1)] >> (16 * (s & 1))) & 0xFFFFu;
     int mm, dw;
     e4m3_term(e & 0xFFu, mm, dw);
     m0 = shifted(mm, ta, dw);
@@ -337,17 +423,18 @@ __device__ __forceinline__ void general_mult(const uint8_t* sc, int s, int k0, i
 }
 
 template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
-__global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const MMParams p) {
+__global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2)
+    gemv_kernel(const MMParams p, const GLayout L, const __grid_constant__ CUtensorMap map) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   using F = GF<FMT>;
   using ST = Stage<R, PLAIN>;
-  constexpr int NO = R / 8;                  // row octets of a block
+  constexpr int NO = R / 8;                  // row octets (tensor-copy boxes) of a block
   constexpr int TPC = kWarps / S;            // row workers of a CTA
   constexpr int VPL = 2 * NO;                // general-path values a lane
-  const int K = p.K, KG = K / 32;
+  const int K = p.K;
   const int KCH = (K + F::kElems - 1) / F::kElems;   // chunks a row
   const int kp = KCH * F::kElems;
-  GSmem s = gemv_carve(smem_raw, MT, K, kp, p.x != nullptr, VPL, S, ST::kBytes, NS);
+  GSmem s = gemv_carve(smem_raw, L);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int slice = warp % S;
@@ -361,29 +448,38 @@ __global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const M
   const int64_t rb = p.N * worker / nworkers, re = p.N * (worker + 1) / nworkers;
   const int64_t most = (p.N + nworkers - 1) / nworkers;
   const int NBLK = static_cast<int>((most + R - 1) / R);   // blocks: the same in every CTA
+  const int total = NBLK * NIT;                             // items a pass
   uint8_t* const ring = s.ring + warp * NS * ST::kBytes;
-  const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
+  const uint32_t ring_s = smem_addr(ring);
+  uint8_t* const sring = s.sring + warp * NS * ST::kScaleBytes;
+  const uint32_t sring_s = smem_addr(sring);
+  const uint32_t bar0 = smem_addr(s.bar + warp * NS);
+  bool ok = true;   // false once a wait ran out: the remaining items are drained, not computed
 
+  if (lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map)) : "memory");
+    for (int i = 0; i < NS; ++i) mbar_init(bar0 + 8 * i, 1);
+    mbar_init_fence();
+  }
+  __syncwarp();
+
+  int f = 0;   // items issued and consumed over all passes: stage f % NS, parity (f / NS) & 1
   for (int m0 = 0; m0 < p.M; m0 += MT) {
     const int mt = min(MT, p.M - m0);
-    // Item (b, k): row block b of this worker, chunk c0 + k; items go through the warp's ring
-    // in order, NS - 1 of them in flight ahead of the one computed.
-    int bi = 0, ki = 0;   // the next item to issue
-    auto issue_next = [&](int slot) {
-      const int64_t r0 = rb + static_cast<int64_t>(bi) * R;
-      const int nrows = static_cast<int>(min(static_cast<int64_t>(R), re - r0));
-      if (bi < NBLK && ki < NSL && nrows > 0)
-        gemv_issue<FMT, R, PLAIN>(ring_s + slot * ST::kBytes, p, r0, nrows, c0 + ki, lane);
-      cp_async_commit();
-      if (++ki == NIT) {
-        ki = 0;
-        ++bi;
-      }
+    // Item i = (b, k): row block b of this worker, chunk c0 + k.
+    auto issue = [&](int i) {
+      const int b = i / NIT, k = i % NIT;
+      const int64_t r0 = rb + static_cast<int64_t>(b) * R;
+      int nrows = static_cast<int>(min(static_cast<int64_t>(R), re - r0));
+      if (k >= NSL || nrows < 0) nrows = 0;
+      const int st = (f + i) % NS;
+      gemv_issue<FMT, R, PLAIN>(ring_s + st * ST::kBytes, sring_s + st * ST::kScaleBytes, bar0 + 8 * st,
+                                &map, p, r0, nrows, c0 + k, lane);
     };
-#pragma unroll
-    for (int q = 0; q < NS - 1; ++q) issue_next(q);
+    const int pre = min(NS - 1, total);
+    for (int i = 0; i < pre; ++i) issue(i);
     if (m0 == 0) pdl_wait();   // the activations may come from the kernel launched before
-    gemv_load_activations<FMT, MT, PLAIN>(p, s, m0, mt, kp);
+    gemv_load_activations<FMT, MT, PLAIN>(p, s, m0, mt, kp, L.ap, L.frag);
     if (m0 + mt >= p.M) pdl_launch();
     const bool use_class = MT == 1 && PLAIN && *s.flag == 0;
 
@@ -395,43 +491,63 @@ __global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const M
       for (int i = 0; i < 4; ++i) D[o][i] = 0;
       acc[o][0] = acc[o][1] = 0;
     }
-    int slot = 0;
+    int i = 0;
     for (int b = 0; b < NBLK; ++b) {
-      for (int k = 0; k < NIT; ++k) {
+      for (int k = 0; k < NIT; ++k, ++i) {
         __syncwarp();   // every lane is done with the stage that the next issue overwrites
-        issue_next(slot == 0 ? NS - 1 : slot - 1);
-        cp_async_wait<NS - 1>();   // this lane's copies of item (b, k) have landed
-        __syncwarp();              // ... and every other lane's
-        const uint8_t* st = ring + slot * ST::kBytes;
-        slot = slot == NS - 1 ? 0 : slot + 1;
-        if (k >= NSL) continue;
+        if (i + NS - 1 < total) issue(i + NS - 1);
+        const int stn = (f + i) % NS;
+        const uint32_t parity = static_cast<uint32_t>(((f + i) / NS) & 1);
+        if (!mbar_wait(bar0 + 8 * stn, parity, p.status)) ok = false;
+        if constexpr (!PLAIN) {
+          if (i + NS - 1 < total) cp_async_wait<NS - 1>(); else cp_async_wait<0>();
+          __syncwarp();
+        }
+        if (k >= NSL || !ok) continue;
+        const uint8_t* st = ring + stn * ST::kBytes;
         const int kc = c0 + k;
         if (use_class) {
 #pragma unroll
           for (int sg = 0; sg < F::kGroups; ++sg) {
             const int G = kc * F::kGroups + sg;
-            const uint2 q = *reinterpret_cast<const uint2*>(s.act + 32 * G + 8 * t);
-            const int c = s.cls[G];
-            const uint32_t a0 = c == g ? q.x : 0u, a2 = c == g ? q.y : 0u;
-            const uint32_t a1 = c == g + 8 ? q.x : 0u, a3 = c == g + 8 ? q.y : 0u;
+            uint4 a;
+            if (L.frag) {
+              a = s.afrag[G * 32 + lane];
+            } else {
+              const uint2 q = *reinterpret_cast<const uint2*>(s.act + 32 * G + 8 * t);
+              const int c = s.cls[G];
+              a.x = c == g ? q.x : 0u;
+              a.y = c == g + 8 ? q.x : 0u;
+              a.z = c == g ? q.y : 0u;
+              a.w = c == g + 8 ? q.y : 0u;
+            }
 #pragma unroll
             for (int o = 0; o < NO; ++o) {
               uint32_t b0, b1;
-              b_frag<FMT>(st + (8 * o + g) * kPitch, sg, t, b0, b1);
-              imma_acc(a0, a1, a2, a3, b0, b1, D[o]);
+              b_frag<FMT>(st + (8 * o + g) * kChunk, sg, g, t, b0, b1);
+              imma_acc(a.x, a.y, a.z, a.w, b0, b1, D[o]);
             }
           }
         } else {
+          RowScale<FMT> rsc[NO][2];
+          if constexpr (!PLAIN) {
+#pragma unroll
+            for (int o = 0; o < NO; ++o)
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                read_row_scale<FMT>(rsc[o][h], sring + stn * ST::kScaleBytes + (8 * o + 2 * t + h) * 16, p.k0, kc);
+          }
+          const int gm = g < MT ? g : 0;
 #pragma unroll
           for (int sg = 0; sg < F::kGroups; ++sg) {
             const int G = kc * F::kGroups + sg;
-            const uint2 q = *reinterpret_cast<const uint2*>(s.act + static_cast<size_t>(g < MT ? g : 0) * kp + 32 * G + 8 * t);
+            const uint2 q = *reinterpret_cast<const uint2*>(s.act + static_cast<size_t>(gm) * L.ap + 32 * G + 8 * t);
             const uint32_t a0 = g < MT ? q.x : 0u, a2 = g < MT ? q.y : 0u;
-            const int ta = g < MT ? s.term[(g < MT ? g : 0) * KG + G] : 0;
+            const int ta = g < MT ? s.term[G * MT + gm] : 0;
 #pragma unroll
             for (int o = 0; o < NO; ++o) {
               uint32_t b0, b1;
-              b_frag<FMT>(st + (8 * o + g) * kPitch, sg, t, b0, b1);
+              b_frag<FMT>(st + (8 * o + g) * kChunk, sg, g, t, b0, b1);
               int d[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
               if constexpr (FMT == kFmtNvfp4) {
                 imma_acc(a0, 0u, a2, 0u, t < 2 ? b0 : 0u, t < 2 ? b1 : 0u, d);
@@ -446,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const M
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 int mA, mB;
-                general_mult<FMT, PLAIN>(st + ST::kScaleOff + (8 * o + 2 * t + h) * 16, sg, p.k0, kc, ta, mA, mB);
+                general_mult<FMT, PLAIN>(rsc[o][h], sg, ta, mA, mB);
                 acc[o][h] += static_cast<long long>(d[h]) * mA;
                 if constexpr (FMT == kFmtNvfp4) acc[o][h] += static_cast<long long>(e[h]) * mB;
               }
@@ -459,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const M
       const int nrows = static_cast<int>(max(static_cast<int64_t>(0), min(static_cast<int64_t>(R), re - r0)));
       if (use_class) {
         constexpr int W = F::kW;
-        const long long mlo = 1ll << (W - g);                        // class g
+        const long long mlo = 1ll << (W - g);                          // class g
         const long long mhi = g + 8 <= W ? (1ll << (W - g - 8)) : 0;   // class g + 8
         long long v[NO][2];
 #pragma unroll
@@ -474,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const M
             v[o][h] = lo * mlo + hi * mhi;
           }
 #pragma unroll
-          for (int i = 0; i < 4; ++i) D[o][i] = 0;
+          for (int q = 0; q < 4; ++q) D[o][q] = 0;
         }
         long long tot = class_reduce<NO>(v, lane);
         const int oct = NO >= 4 ? (lane >> 2) & 3 : (NO >= 2 ? (lane >> 3) & 1 : 0);
@@ -486,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const M
           if (slice == 0 && owner)
             for (int o = 1; o < S; ++o) tot += s.red[(warp + o) * 32 + lane];
         }
-        if (slice == 0 && owner && rr < nrows) {
+        if (slice == 0 && owner && rr < nrows && ok) {
           const int64_t row = r0 + rr;
           const float Sw = unit ? 1.0f : __ldg(reinterpret_cast<const float*>(p.srows + row * p.srs));
           float yv = mm_epilogue(tot, Sw, s.Sa[0], W);
@@ -513,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const M
 #pragma unroll
                 for (int h = 0; h < 2; ++h) acc[o][h] += s.red[((warp + w2) * 32 + lane) * VPL + 2 * o + h];
         }
-        if (slice == 0 && g < mt) {
+        if (slice == 0 && g < mt && ok) {
 #pragma unroll
           for (int o = 0; o < NO; ++o)
 #pragma unroll
@@ -538,21 +654,60 @@ __global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2) gemv_kernel(const M
         if constexpr (S > 1) __syncthreads();
       }
     }
-    cp_async_wait<0>();
-    __syncthreads();   // the next activation rows and ring contents overwrite shared memory
+    f += total;
+    __syncthreads();   // the next activation rows overwrite shared memory
   }
 }
 
-template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
-size_t gemv_smem(int K, bool fused) {
-  using F = GF<FMT>;
-  const int kp = ((K + F::kElems - 1) / F::kElems) * F::kElems;
-  return gemv_layout(MT, K, kp, fused, 2 * (R / 8), S, Stage<R, PLAIN>::kBytes, NS, nullptr);
+// The weight rows as a 2-D tensor of bytes: [N][row_bytes] with rows rs bytes apart, copied in
+// boxes of 8 rows x 128 bytes with the 128-byte swizzle. cuTensorMapEncodeTiled comes from the
+// driver through the runtime's entry-point query (nothing links libcuda).
+bool encode_rows_map(CUtensorMap* map, const uint8_t* rows, int row_bytes, int64_t N, int64_t rs) {
+  static PFN_cuTensorMapEncodeTiled encode = nullptr;
+  if (encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return false;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(N)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(rs)};
+  const cuuint32_t box[2] = {kChunk, kBox};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(rows), dims, strides, box,
+                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
-int gemv_cfg(const MMParams& p, cudaStream_t stream, bool pdl) {
-  const size_t smem = gemv_smem<FMT, MT, R, S, NS, PLAIN>(p.K, p.x != nullptr);
+GLayout gemv_geometry(int K, bool fused, bool frag) {
+  using F = GF<FMT>;
+  GLayout L;
+  L.MT = MT;
+  L.K = K;
+  const int kp = ((K + F::kElems - 1) / F::kElems) * F::kElems;
+  L.ap = kp + kActPad;
+  L.vpl = 2 * (R / 8);
+  L.S = S;
+  L.stage_bytes = Stage<R, PLAIN>::kBytes;
+  L.scale_bytes = Stage<R, PLAIN>::kScaleBytes;
+  L.ns = NS;
+  L.fused = fused;
+  L.frag = frag && MT == 1 && PLAIN;
+  return L;
+}
+
+template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
+bool gemv_fits(int K, bool fused, bool frag) {
+  return gemv_layout(gemv_geometry<FMT, MT, R, S, NS, PLAIN>(K, fused, frag), nullptr) <= 227 * 1024;
+}
+
+template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
+int gemv_cfg(const MMParams& p, cudaStream_t stream, bool pdl, bool frag) {
+  const GLayout L = gemv_geometry<FMT, MT, R, S, NS, PLAIN>(p.K, p.x != nullptr, frag);
+  const size_t smem = gemv_layout(L, nullptr);
   if (smem > 227 * 1024) return kErrArg;
   auto kern = gemv_kernel<FMT, MT, R, S, NS, PLAIN>;
   static size_t configured_smem[kMaxDevices] = {0};
@@ -571,25 +726,41 @@ int gemv_cfg(const MMParams& p, cudaStream_t stream, bool pdl) {
   constexpr int TPC = kWarps / S;
   const int64_t want = (p.N + static_cast<int64_t>(R) * TPC - 1) / (static_cast<int64_t>(R) * TPC);
   const int64_t grid = min(want, static_cast<int64_t>(sm_count(dev)) * occ);
-  return launch_kernel(reinterpret_cast<const void*>(kern), static_cast<int>(grid), kThreads, smem,
-                       stream, pdl, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  CUtensorMap map;
+  const int row_bytes = FMT == kFmtInt8 ? p.K : p.K / 2;
+  if (!encode_rows_map(&map, p.rows, row_bytes, p.N, p.rs)) return kErrCuda;
+  void* args[] = {const_cast<MMParams*>(&p), const_cast<GLayout*>(&L), &map};
+  return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kern), args) == cudaSuccess ? kOk
+                                                                                          : kErrCuda;
 }
 
-// (rows a block, K split): 32 rows a warp and no split for tall matrices; 8 rows with the split
-// that keeps about 8 warps on every SM for short ones.
+// (rows a block, K split, ring depth): 32 rows a warp, no split and the deepest ring that fits
+// for tall matrices; 8 rows with the split that keeps about 8 warps on every SM for short ones.
 template <int FMT, int MT, bool PLAIN>
 int gemv_split(const MMParams& p, cudaStream_t stream, bool pdl, int split) {
   const bool fused = p.x != nullptr;
   switch (split) {
     case 1:
-      if (gemv_smem<FMT, MT, 32, 1, 4, PLAIN>(p.K, fused) <= 227 * 1024)
-        return gemv_cfg<FMT, MT, 32, 1, 4, PLAIN>(p, stream, pdl);
-      if (gemv_smem<FMT, MT, 32, 1, 2, PLAIN>(p.K, fused) <= 227 * 1024)
-        return gemv_cfg<FMT, MT, 32, 1, 2, PLAIN>(p, stream, pdl);
-      return gemv_cfg<FMT, MT, 8, 1, 4, PLAIN>(p, stream, pdl);
-    case 2: return gemv_cfg<FMT, MT, 8, 2, 4, PLAIN>(p, stream, pdl);
-    case 4: return gemv_cfg<FMT, MT, 8, 4, 4, PLAIN>(p, stream, pdl);
-    default: return gemv_cfg<FMT, MT, 8, 8, 4, PLAIN>(p, stream, pdl);
+      if (gemv_fits<FMT, MT, 32, 1, 5, PLAIN>(p.K, fused, true))
+        return gemv_cfg<FMT, MT, 32, 1, 5, PLAIN>(p, stream, pdl, true);
+      if (gemv_fits<FMT, MT, 32, 1, 5, PLAIN>(p.K, fused, false))
+        return gemv_cfg<FMT, MT, 32, 1, 5, PLAIN>(p, stream, pdl, false);
+      if (gemv_fits<FMT, MT, 32, 1, 3, PLAIN>(p.K, fused, false))
+        return gemv_cfg<FMT, MT, 32, 1, 3, PLAIN>(p, stream, pdl, false);
+      return gemv_cfg<FMT, MT, 8, 2, 4, PLAIN>(p, stream, pdl, false);
+    case 2: return gemv_cfg<FMT, MT, 8, 2, 4, PLAIN>(p, stream, pdl, gemv_fits<FMT, MT, 8, 2, 4, PLAIN>(p.K, fused, true));
+    case 4: return gemv_cfg<FMT, MT, 8, 4, 4, PLAIN>(p, stream, pdl, gemv_fits<FMT, MT, 8, 4, 4, PLAIN>(p.K, fused, true));
+    default: return gemv_cfg<FMT, MT, 8, 8, 4, PLAIN>(p, stream, pdl, gemv_fits<FMT, MT, 8, 8, 4, PLAIN>(p.K, fused, true));
   }
 }
 

@@ -36,6 +36,10 @@ __device__ __forceinline__ float fsub(float a, float b) {
 // a in [1, 2) a magic seed, two Newton steps y*(2 - a*y), the correction step
 // y*(1 - a*y) + y, then 127 - field(x) added to y's exponent field and x's sign or-ed in.
 // Zero -> +0; |x| >= 2^126 (inf and NaN included) -> a zero with x's sign.
+// On the significand every operand and result of the steps is a normal number or zero (the
+// seed lies in (0.47, 0.96), a*y and the Newton factors near 1, the correction term a multiple
+// of 2^-24 times y), so the flushes and the NaN canonicalisation of fmul / fsub /
+// fadd are no-ops there and plain round-to-nearest operations give the same bits.
 __device__ __forceinline__ float recip(float x) {
   const uint32_t xb = __float_as_uint(otq_flush(x));
   const uint32_t mag = xb & 0x7FFFFFFFu;
@@ -44,9 +48,9 @@ __device__ __forceinline__ float recip(float x) {
   if (mag >= 0x7E800000u) return __uint_as_float(sign);
   const float a = __uint_as_float(0x3F800000u | (mag & 0x007FFFFFu));
   float y = __uint_as_float(0x7EF311C3u - __float_as_uint(a));
-  y = fmul(y, fsub(2.0f, fmul(a, y)));
-  y = fmul(y, fsub(2.0f, fmul(a, y)));
-  y = fadd(fmul(y, fsub(1.0f, fmul(a, y))), y);
+  y = __fmul_rn(y, __fsub_rn(2.0f, __fmul_rn(a, y)));
+  y = __fmul_rn(y, __fsub_rn(2.0f, __fmul_rn(a, y)));
+  y = __fadd_rn(__fmul_rn(y, __fsub_rn(1.0f, __fmul_rn(a, y))), y);
   const int k = 127 - static_cast<int>(mag >> 23);
   const uint32_t yb = static_cast<uint32_t>(static_cast<int>(__float_as_uint(y)) + k * (1 << 23));
   return __uint_as_float(yb | sign);

@@ -120,3 +120,86 @@ __device__ __forceinline__ QactRowResult qact_row(const ThreadGroup<NT, BAR>& gr
 }
 
 }  // namespace otq
+
+namespace otq {
+
+__device__ __forceinline__ float4 ld_cg4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t mag_bits(float v) {
+  return __float_as_uint(otq_flush(v)) & 0x7FFFFFFFu;
+}
+
+// The same QACT as qact_row for 32-element groups, four elements a thread at a time: one pass
+// reads x (straight from global memory through L2: x may be the output of the kernel launched
+// just before, read after griddepcontrol.wait) into xs, with each 32-element segment's maximum
+// from an 8-lane shuffle reduction; one more pass quantizes. n % 128 == 0; all NT threads of
+// the CTA call it. x4: x is 16-byte aligned (else four scalar loads). segm: shared scratch of
+// n/32 words; red: of NT/32 + 3 words. emit(i, q0, q1, q2, q3, d) gets elements 4i..4i+3 and
+// their group's offset; the 8 threads of a group call it together (lanes 8k..8k+7 of a warp).
+// Ends with a barrier.
+template <int NT, class Emit4>
+__device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, bool x4, float* xs,
+                                                   int n, bool row_mode, uint32_t* segm,
+                                                   uint32_t* red, Emit4 emit) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = NT / 32;
+  const int n4 = n >> 2;   // a multiple of 32: every lane of a warp runs the same iterations
+  uint32_t tmax = 0u;
+  for (int i = tid; i < n4; i += NT) {
+    float4 v;
+    if (x4) {
+      v = ld_cg4(x + 4 * i);
+    } else {
+      v.x = __ldcg(x + 4 * i);
+      v.y = __ldcg(x + 4 * i + 1);
+      v.z = __ldcg(x + 4 * i + 2);
+      v.w = __ldcg(x + 4 * i + 3);
+    }
+    *reinterpret_cast<float4*>(xs + 4 * i) = v;
+    uint32_t m = max(max(mag_bits(v.x), mag_bits(v.y)), max(mag_bits(v.z), mag_bits(v.w)));
+    m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+    m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
+    if ((lane & 7) == 0) segm[i >> 3] = m;
+    tmax = max(tmax, m);
+  }
+  tmax = __reduce_max_sync(0xFFFFFFFFu, tmax);
+  if (lane == 0) red[warp] = tmax;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t m = lane < NW ? red[lane] : 0u;
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if (lane == 0) {
+      float S = 0.0f, inv = 0.0f;
+      if (m != 0u) {
+        const float amax = __uint_as_float(m);
+        S = fmul(amax, __uint_as_float(kInv127Bits));
+        inv = fmul(127.0f, recip(amax));
+      }
+      red[NW] = __float_as_uint(S);
+      red[NW + 1] = __float_as_uint(inv);
+      red[NW + 2] = m;
+    }
+  }
+  __syncthreads();
+  QactRowResult r;
+  r.S = __uint_as_float(red[NW]);
+  r.inv = __uint_as_float(red[NW + 1]);
+  r.amax_bits = red[NW + 2];
+  for (int i = tid; i < n4; i += NT) {
+    const float4 v = *reinterpret_cast<const float4*>(xs + 4 * i);
+    const int d = row_mode ? 0 : group_offset(segm[i >> 3], r.amax_bits);
+    const float scale = fmul(r.inv, pow2i(d));
+    emit(i, q8(fmul(v.x, scale)), q8(fmul(v.y, scale)), q8(fmul(v.z, scale)), q8(fmul(v.w, scale)), d);
+  }
+  __syncthreads();
+  return r;
+}
+
+}  // namespace otq
