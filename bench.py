@@ -256,9 +256,11 @@ def main():
     peak, peak_kind = peaks()
     achieved = head_bytes / (head_ms * 1e-3) / 1e9
     traffic = None
-    tp = ROOT / "profiles" / "traffic.json"
+    tp = ROOT / "profiles" / "gemv_kernel_lm_head_int8row_151936x1024_m1.md"
     if tp.exists() and world == 1:
-        traffic = json.loads(tp.read_text()).get("mm_gemv_head_int8_row_bytes_per_launch")
+        for line in tp.read_text().splitlines():
+            if line.startswith("| dram_bytes_per_launch |"):
+                traffic = int(line.split("|")[2])
 
     # end to end through the public API from host buffers: inputs H2D, logits D2H each step
     inputs_host = {shape.hidden: torch.randn((1, shape.hidden)).pin_memory()}
@@ -304,7 +306,7 @@ def main():
             "hbm_frac": value / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "mm_gemv (LM head launch, 151936x1024 int8-row, M=1)",
+                         "kernel": "gemv_kernel (LM head launch, 151936x1024 int8-row, M=1)",
                          "bytes_per_launch": head_bytes, "us_per_launch": head_ms * 1e3,
                          "peak_kind": peak_kind},
             "cpu_baseline": cpu,

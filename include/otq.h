@@ -119,22 +119,15 @@ OTQ_API int otq_qmm(int fmt, int flags, const uint8_t* rows, int64_t rs, const u
             int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx, int row_mode,
             int64_t M, const float* alpha, float* y, int64_t ldy, void* stream);
 
-/* Kernel choices of otq_qmm_ex. */
-#define OTQ_KERNEL_AUTO 0 /* rows for one or two activation rows, else tiles */
-#define OTQ_KERNEL_TILE 1 /* 16-row weight tiles; up to 8 activation rows a pass */
-#define OTQ_KERNEL_ROWS 2 /* contiguous row spans; 1 or 2 activation rows a pass */
-#define OTQ_KERNEL_RING 3 /* persistent kernel, weights through a shared-memory ring */
-#define OTQ_KERNEL_GEMV 4 /* row ranges through cp.async rings; up to 8 activation rows a pass */
-
-/* Launch-tuning variant of otq_qmm for benchmarks and tests: kernel is one of OTQ_KERNEL_*;
- * k_split in {1, 2, 4, 8} warps share the K range of each weight row (tile) or row (rows);
- * 0 picks. pdl != 0 launches with programmatic dependent launch (the kernel waits on
- * griddepcontrol before reading x). Same results as otq_qmm for every setting. No counterpart
- * in the reference (its MM has one implementation). */
+/* Launch-tuning variant of otq_qmm for benchmarks and tests: k_split in {1, 2, 4, 8} warps
+ * share the K range of each weight row (1 also selects 32-row blocks a warp); 0 picks. pdl != 0
+ * launches with programmatic dependent launch (the kernel streams its first weight chunks, then
+ * waits on griddepcontrol before reading x). Same results as otq_qmm for every setting. No
+ * counterpart in the reference (its MM has one implementation). */
 OTQ_API int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
                int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx,
                int row_mode, int64_t M, const float* alpha, float* y, int64_t ldy,
-               int kernel, int k_split, int pdl, void* stream);
+               int k_split, int pdl, void* stream);
 
 /* The device status word of the current device (synchronous): bit 0 set means a kernel's
  * bounded wait on a shared-memory barrier ran out and that kernel returned early (its outputs

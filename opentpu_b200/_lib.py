@@ -15,7 +15,6 @@ LIB_PATH = Path(__file__).resolve().parent / "libotq.so"
 OK, ERR_ARG, ERR_ALIGN, ERR_FORMAT, ERR_CUDA, ERR_DEVICE = 0, -1, -2, -3, -4, -5
 FMT = {"int8": 0, "int4": 1, "fp4": 2, "nvfp4": 3}     # MM's WF codes (opentpu/isa.py:26-27)
 MM_UNIT, MM_ACC, MM_ASCALE, MM_RSC = 0x1, 0x2, 0x8, 0x80
-KERNELS = {"auto": 0, "tile": 1, "rows": 2, "ring": 3, "gemv": 4}   # otq_qmm_ex kernel choices
 
 # name -> (restype, argtypes); every pointer is passed as an integer address
 _P, _I, _L = c_void_p, c_int, c_int64
@@ -30,7 +29,7 @@ SIGNATURES = {
     "otq_mm": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _P, _P, _L, _L, _P, _P, _L, _P]),
     "otq_qmm": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _L, _P, _P, _L, _P]),
     "otq_qmm_ex": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _L, _P, _P, _L, _I, _I,
-                        _I, _P]),
+                        _P]),
     "otq_status_word": (_I, [_P, _I]),
     "otq_pack_g32": (_I, [_P, _L, _L, _L, _P, _P, _P]),
     "otq_linear_g32": (_I, [_P, _P, _L, _L, _P, _L, _L, _I, _P, _L, _P]),

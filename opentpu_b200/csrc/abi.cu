@@ -112,7 +112,6 @@ int check_weights(int fmt, int flags, const uint8_t* rows, int64_t rs, const uin
   return kOk;
 }
 
-int mt_bucket(int64_t M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
 int check_out(int64_t M, int64_t N, const float* y, int64_t ldy, int flags, const float* alpha) {
   if (M <= 0 || M > 0x7FFFFFFF || y == nullptr || ldy < N) return kErrArg;
@@ -255,15 +254,14 @@ int otq_mm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* s
 int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
                int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx,
                int row_mode, int64_t M, const float* alpha, float* y, int64_t ldy,
-               int kernel, int k_split, int pdl, void* stream) {
+               int k_split, int pdl, void* stream) {
   int st = device_ok();
   if (st) return st;
   if ((st = check_weights(fmt, flags, rows, rs, srows, srs, k0, N, K))) return st;
   if ((st = check_out(M, N, y, ldy, flags, alpha))) return st;
   if (x == nullptr || ldx < K) return kErrArg;
   if (!aligned(x, 4)) return kErrAlign;
-  if (kernel < kKernelAuto || kernel > kKernelGemv) return kErrArg;
-  if (k_split != 0 && k_split != 1 && k_split != 2 && k_split != 4 && k_split != 8 && k_split < 101) return kErrArg;
+  if (k_split != 0 && k_split != 1 && k_split != 2 && k_split != 4 && k_split != 8) return kErrArg;
   MMParams p{};
   p.fmt = fmt;
   p.flags = flags;
@@ -281,7 +279,6 @@ int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_
   p.alpha = alpha;
   p.y = y;
   p.ldy = ldy;
-  p.kernel = kernel;
   p.split = k_split;
   return finish(mm_launch(p, static_cast<cudaStream_t>(stream), pdl != 0));
 }
@@ -290,7 +287,7 @@ int otq_qmm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* 
             int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx, int row_mode,
             int64_t M, const float* alpha, float* y, int64_t ldy, void* stream) {
   return otq_qmm_ex(fmt, flags, rows, rs, srows, srs, k0, N, K, x, ldx, row_mode, M, alpha, y,
-                    ldy, kKernelAuto, 0, 0, stream);
+                    ldy, 0, 0, stream);
 }
 
 int otq_status_word(int* value, int reset) {

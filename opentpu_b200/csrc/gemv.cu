@@ -789,10 +789,12 @@ int gemv_pick_split(int fmt, int64_t N, int K, int dev) {
   return split;
 }
 
-int gemv_launch(const MMParams& p, cudaStream_t stream, bool pdl, int split) {
+int mm_launch(const MMParams& p0, cudaStream_t stream, bool pdl) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
-  if (split == 0) split = gemv_pick_split(p.fmt, p.N, p.K, dev);
+  MMParams p = p0;
+  p.status = status_word();
+  const int split = p.split > 0 ? p.split : gemv_pick_split(p.fmt, p.N, p.K, dev);
   switch (p.fmt) {
     case kFmtInt8: return gemv_fmt<kFmtInt8>(p, stream, pdl, split);
     case kFmtInt4: return gemv_fmt<kFmtInt4>(p, stream, pdl, split);

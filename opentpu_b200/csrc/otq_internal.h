@@ -31,13 +31,6 @@ constexpr int kMaxDevices = 64;
 // Bits of the library's device status word (otq_status_word): a bounded wait ran out.
 constexpr int kStatusTimeout = 1;
 
-// Shared-memory ring of the persistent GEMV (mm_stream.cu).
-struct RingCfg {
-  int chunk_bytes;   // bytes of a weight row per stage
-  int row_stride;    // bytes between rows in a stage (chunk + padding)
-  int ns;            // stages
-};
-
 struct MMParams {
   int fmt;
   int flags;
@@ -61,30 +54,13 @@ struct MMParams {
   const float* alpha;
   float* y;
   int64_t ldy;
-  int kernel;   // kKernelAuto, kKernelTile, kKernelRows, kKernelRing
   int split;    // warps that split a row's K (1, 2, 4, 8); 0: pick
   int* status;   // device status word (may be null): kStatusTimeout bits
 };
 
-// GEMV kernels (otq_qmm_ex's kernel argument).
-constexpr int kKernelAuto = 0;
-constexpr int kKernelTile = 1;   // mm_gemv.cu: 16-row tiles, up to 8 activation rows a pass
-constexpr int kKernelRows = 2;   // mm_rows.cu: row spans, 1 or 2 activation rows a pass
-constexpr int kKernelRing = 3;   // mm_stream.cu: persistent shared-memory ring
-constexpr int kKernelGemv = 4;   // gemv.cu: row ranges through cp.async rings, class path
-
 int sm_count(int dev);
-size_t mm_smem_bytes(int fmt, int mt, int K, bool fused);
-int mm_pick_split(int fmt, int64_t N, int K, int dev);
-int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);
-size_t rows_smem_bytes(int mr, int K, bool fused);
-int rows_pick_split(int64_t N, int K, int dev);
-int mm_rows_launch(const MMParams& p, cudaStream_t stream, bool pdl, int split);
 int gemv_pick_split(int fmt, int64_t N, int K, int dev);
-int gemv_launch(const MMParams& p, cudaStream_t stream, bool pdl, int split);
-RingCfg ring_config(int fmt, int K, int M, bool fused);
-size_t ring_smem_bytes(int fmt, int K, int M, bool fused);
-int mm_ring_launch(const MMParams& p, cudaStream_t stream, bool pdl);
+int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);   // gemv.cu
 int* status_word();   // this device's status word (device address), or null
 
 // Launch with an optional programmatic-dependent-launch attribute (the kernel then may start

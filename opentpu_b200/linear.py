@@ -233,14 +233,14 @@ def mm(q, S, d, w: PackedWeight, *, out=None, acc: bool = False, alpha=None):
 
 
 def qlinear(x: torch.Tensor, w: PackedWeight, *, out=None, acc: bool = False, alpha=None,
-            row_mode: bool = False, kernel: str = "auto", k_split: int = 0, pdl: bool = False):
+            row_mode: bool = False, k_split: int = 0, pdl: bool = False):
     """y = x @ W^T through the quantized weight (ol.dot on an fp32 tile).
 
     MX formats: QACT of each row of x (offsets per 32, or ROW mode) fused with MM in one kernel,
     bit-exact with the reference. int4-g32: weight-only, fp32 accumulation (tolerance).
-    x [M, K] or [K]; returns [M, N] (or [N]); out / acc / alpha as in `mm`. kernel ("auto",
-    "tile", "rows", "ring") and k_split (warps sharing a row's K range; 0 picks) tune the launch:
-    results are identical for every value."""
+    x [M, K] or [K]; returns [M, N] (or [N]); out / acc / alpha as in `mm`. k_split (warps
+    sharing a row's K range; 0 picks) and pdl tune the launch: results are identical for every
+    value."""
     x2, vec = _as_rows(x, w.K)
     M = x2.shape[0]
     y = _out(out, M, w.N, x.device, acc or alpha is not None)
@@ -255,5 +255,5 @@ def qlinear(x: torch.Tensor, w: PackedWeight, *, out=None, acc: bool = False, al
         L.call("otq_qmm_ex", L.FMT[w.mx_fmt], flags, w.rows.data_ptr(), w.rows.stride(0),
                _ptr(w.srows), 0 if w.srows is None else w.srows.stride(0), w.k0, w.N, w.K,
                x2.data_ptr(), x2.stride(0), int(row_mode), M, _ptr(alpha), y.data_ptr(),
-               y.stride(0), L.KERNELS[kernel], k_split, int(pdl), _stream())
+               y.stride(0), k_split, int(pdl), _stream())
     return y.reshape(-1) if vec and out is None else y
