@@ -119,8 +119,8 @@ OTQ_API int otq_qmm(int fmt, int flags, const uint8_t* rows, int64_t rs, const u
             int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx, int row_mode,
             int64_t M, const float* alpha, float* y, int64_t ldy, void* stream);
 
-/* Launch-tuning variant of otq_qmm for benchmarks and tests: k_split in {1, 2, 4, 8} warps
- * share the K range of each weight row (1 also selects 32-row blocks a warp); 0 picks. pdl != 0
+/* Launch-tuning variant of otq_qmm for benchmarks and tests: k_split 32 selects 32-row blocks a
+ * warp, 1 8-row blocks, 2 / 4 / 8 8-row blocks whose K range that many warps share; 0 picks. pdl != 0
  * launches with programmatic dependent launch (the kernel streams its first weight chunks, then
  * waits on griddepcontrol before reading x). Same results as otq_qmm for every setting. No
  * counterpart in the reference (its MM has one implementation). */
@@ -129,9 +129,36 @@ OTQ_API int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, cons
                int row_mode, int64_t M, const float* alpha, float* y, int64_t ldy,
                int k_split, int pdl, void* stream);
 
+/* One projection of a chain (otq_qmm_chain): the operands of otq_qmm for one activation row. */
+typedef struct otq_proj {
+  int fmt;               /* OTQ_FMT_* */
+  int flags;             /* OTQ_MM_UNIT / OTQ_MM_RSC / OTQ_MM_ACC (ASCALE needs otq_qmm) */
+  const uint8_t* rows;   /* weight rows [N][rs] (16-byte aligned, rs a multiple of 16) */
+  int64_t rs;
+  const uint8_t* srows;  /* scale rows [N][srs], or NULL with OTQ_MM_UNIT */
+  int64_t srs;
+  int k0;                /* first 128-element block of the scale rows (column part) */
+  int64_t N;
+  int64_t K;
+  const float* x;        /* the activation row [K]; may be an earlier projection's y */
+  int row_mode;          /* QACT ROW */
+  float* y;              /* [N] */
+} otq_proj;
+
+/* QACT + MM of `count` projections in order, one activation row each, in one persistent
+ * launch per run of projections of the same format and kind (RSC / UNIT or MX): a projection
+ * may read (x) what an earlier one wrote (y) -- a decode step's chain of linear layers. The
+ * results are those of otq_qmm called once per projection in order. The CTAs of a launch are
+ * co-resident (cooperative launch) and meet at a grid barrier between projections, whose two
+ * counter words are static device memory of this library: launches of chains on one device
+ * must not overlap (they serialise on a stream or on the device's SMs). A barrier wait is
+ * bounded: if it runs out, the status word records it (otq_status_word) and the results are
+ * not valid. No counterpart in the reference (its projections are separate programs). */
+OTQ_API int otq_qmm_chain(const otq_proj* projs, int count, void* stream);
+
 /* The device status word of the current device (synchronous): bit 0 set means a kernel's
- * bounded wait on a shared-memory barrier ran out and that kernel returned early (its outputs
- * are not valid). reset != 0 clears it. No counterpart in the reference (a simulator has no
+ * bounded wait (on a shared-memory barrier, or a chain's grid barrier) ran out; that launch's
+ * outputs are not valid. reset != 0 clears it (and, if it was set, re-arms the grid barrier). No counterpart in the reference (a simulator has no
  * such failure). */
 OTQ_API int otq_status_word(int* value, int reset);
 

@@ -16,6 +16,13 @@ OK, ERR_ARG, ERR_ALIGN, ERR_FORMAT, ERR_CUDA, ERR_DEVICE = 0, -1, -2, -3, -4, -5
 FMT = {"int8": 0, "int4": 1, "fp4": 2, "nvfp4": 3}     # MM's WF codes (opentpu/isa.py:26-27)
 MM_UNIT, MM_ACC, MM_ASCALE, MM_RSC = 0x1, 0x2, 0x8, 0x80
 
+class Proj(ctypes.Structure):
+    """struct otq_proj of include/otq.h: one projection of otq_qmm_chain."""
+    _fields_ = [("fmt", c_int), ("flags", c_int), ("rows", c_void_p), ("rs", c_int64),
+                ("srows", c_void_p), ("srs", c_int64), ("k0", c_int), ("N", c_int64),
+                ("K", c_int64), ("x", c_void_p), ("row_mode", c_int), ("y", c_void_p)]
+
+
 # name -> (restype, argtypes); every pointer is passed as an integer address
 _P, _I, _L = c_void_p, c_int, c_int64
 SIGNATURES = {
@@ -30,6 +37,7 @@ SIGNATURES = {
     "otq_qmm": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _L, _P, _P, _L, _P]),
     "otq_qmm_ex": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _L, _P, _P, _L, _I, _I,
                         _P]),
+    "otq_qmm_chain": (_I, [_P, _I, _P]),
     "otq_status_word": (_I, [_P, _I]),
     "otq_pack_g32": (_I, [_P, _L, _L, _L, _P, _P, _P]),
     "otq_linear_g32": (_I, [_P, _P, _L, _L, _P, _L, _L, _I, _P, _L, _P]),

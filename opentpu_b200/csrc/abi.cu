@@ -88,6 +88,8 @@ int64_t scale_need(int fmt, bool rsc, int k0, int64_t KB) {
   }
 }
 
+constexpr int64_t kStrideLimit = int64_t(1) << 31;   // strides are 32-bit in the kernels
+
 int check_weights(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
                   int64_t srs, int k0, int64_t N, int64_t K) {
   if (fmt_window(fmt) < 0) return kErrFormat;
@@ -103,6 +105,7 @@ int check_weights(int fmt, int flags, const uint8_t* rows, int64_t rs, const uin
   const int64_t used = fmt == kFmtInt8 ? K : K / 2;
   if (rs < used) return kErrArg;
   if (!aligned(rows, 16) || rs % 16) return kErrAlign;
+  if (rs >= kStrideLimit || srs >= kStrideLimit) return kErrArg;
   if (!unit) {
     if (srows == nullptr) return kErrArg;
     const int64_t a = scale_align(fmt, rsc);
@@ -114,7 +117,7 @@ int check_weights(int fmt, int flags, const uint8_t* rows, int64_t rs, const uin
 
 
 int check_out(int64_t M, int64_t N, const float* y, int64_t ldy, int flags, const float* alpha) {
-  if (M <= 0 || M > 0x7FFFFFFF || y == nullptr || ldy < N) return kErrArg;
+  if (M <= 0 || M > 0x7FFFFFFF || y == nullptr || ldy < N || ldy >= kStrideLimit) return kErrArg;
   if ((flags & kMmAscale) && alpha == nullptr) return kErrArg;
   return kOk;
 }
@@ -228,7 +231,9 @@ int otq_mm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* s
   if (st) return st;
   if ((st = check_weights(fmt, flags, rows, rs, srows, srs, k0, N, K))) return st;
   if ((st = check_out(M, N, y, ldy, flags, alpha))) return st;
-  if (q == nullptr || Sa == nullptr || da == nullptr || ldq < K || ldd < K / 32) return kErrArg;
+  if (q == nullptr || Sa == nullptr || da == nullptr || ldq < K || ldd < K / 32 ||
+      ldq >= kStrideLimit || ldd >= kStrideLimit)
+    return kErrArg;
   MMParams p{};
   p.fmt = fmt;
   p.flags = flags;
@@ -259,9 +264,10 @@ int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_
   if (st) return st;
   if ((st = check_weights(fmt, flags, rows, rs, srows, srs, k0, N, K))) return st;
   if ((st = check_out(M, N, y, ldy, flags, alpha))) return st;
-  if (x == nullptr || ldx < K) return kErrArg;
+  if (x == nullptr || ldx < K || ldx >= kStrideLimit) return kErrArg;
   if (!aligned(x, 4)) return kErrAlign;
-  if (k_split != 0 && k_split != 1 && k_split != 2 && k_split != 4 && k_split != 8) return kErrArg;
+  if (k_split != 0 && k_split != 1 && k_split != 2 && k_split != 4 && k_split != 8 && k_split != 32)
+    return kErrArg;
   MMParams p{};
   p.fmt = fmt;
   p.flags = flags;
@@ -290,6 +296,21 @@ int otq_qmm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* 
                     ldy, 0, 0, stream);
 }
 
+int otq_qmm_chain(const otq_proj* projs, int count, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (projs == nullptr || count < 0) return kErrArg;
+  for (int i = 0; i < count; ++i) {
+    const otq_proj& p = projs[i];
+    if ((st = check_weights(p.fmt, p.flags, p.rows, p.rs, p.srows, p.srs, p.k0, p.N, p.K))) return st;
+    if (p.flags & kMmAscale) return kErrArg;
+    if (p.x == nullptr || p.y == nullptr) return kErrArg;
+    if (!aligned(p.x, 4) || !aligned(p.y, 4)) return kErrAlign;
+  }
+  if (count == 0) return kOk;
+  return finish(chain_launch(projs, count, static_cast<cudaStream_t>(stream)));
+}
+
 int otq_status_word(int* value, int reset) {
   int st = device_ok();
   if (st) return st;
@@ -301,6 +322,7 @@ int otq_status_word(int* value, int reset) {
     const int zero = 0;
     e = cudaMemcpyToSymbol(g_status_word, &zero, sizeof(int));
     if (e != cudaSuccess) return cuda_status(e);
+    if (v != 0 && (st = chain_reset())) return st;   // a barrier may have been left mid-way
   }
   *value = v;
   return kOk;

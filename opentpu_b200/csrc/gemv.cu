@@ -39,6 +39,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstring>
 
 #include "mm_common.cuh"
 #include "otq_fp32.cuh"
@@ -88,6 +89,88 @@ struct GSmem {
 struct GLayout {
   int MT, K, ap, vpl, S, stage_bytes, scale_bytes, ns;
   bool fused, frag;
+};
+
+// Work decompositions of a projection: 32-row blocks, or 8-row blocks with S warps sharing a
+// row's K (S = 1, 2, 4, 8).
+enum { kCfgR32 = 0, kCfgS1 = 1, kCfgS2 = 2, kCfgS4 = 3, kCfgS8 = 4 };
+
+// One projection (QACT + MM) of a launch: its operands and the tensor map of its weight rows.
+struct alignas(64) Proj {
+  CUtensorMap map;
+  const uint8_t* rows;   // what the map describes (for L2 prefetches)
+  const uint8_t* srows;
+  const float* x;        // fp32 activations (QACT in the kernel), or null: q / Sa / da given
+  float* y;
+  const float* alpha;
+  const int8_t* q;
+  const float* Sa;
+  const uint8_t* da;
+  int64_t N;
+  int rs, srs, ldx, ldy, ldq, ldd;   // strides (the entry points keep them below 2^31)
+  int K, flags, k0, row_mode, M, cfg;
+};
+static_assert(sizeof(Proj) == 256, "a projection is 256 bytes of kernel parameters");
+
+// A projection's scalars, copied out of the kernel parameters once per projection (reads
+// through a pointer into parameter space cost a memory round trip each); map stays the
+// address of the tensor map in parameter space, which is what a tensor copy takes.
+struct PArgs {
+  const CUtensorMap* map;
+  const uint8_t* rows;
+  const uint8_t* srows;
+  const float* x;
+  float* y;
+  const float* alpha;
+  const int8_t* q;
+  const float* Sa;
+  const uint8_t* da;
+  int64_t N;
+  int rs, srs, ldx, ldy, ldq, ldd;
+  int K, flags, k0, row_mode, M, cfg;
+};
+
+__device__ __forceinline__ PArgs load_args(const Proj& d) {
+  PArgs a;
+  a.map = &d.map;
+  a.rows = d.rows;
+  a.srows = d.srows;
+  a.x = d.x;
+  a.y = d.y;
+  a.alpha = d.alpha;
+  a.q = d.q;
+  a.Sa = d.Sa;
+  a.da = d.da;
+  a.N = d.N;
+  a.rs = d.rs;
+  a.srs = d.srs;
+  a.ldx = d.ldx;
+  a.ldy = d.ldy;
+  a.ldq = d.ldq;
+  a.ldd = d.ldd;
+  a.K = d.K;
+  a.flags = d.flags;
+  a.k0 = d.k0;
+  a.row_mode = d.row_mode;
+  a.M = d.M;
+  a.cfg = d.cfg;
+  return a;
+}
+
+// The projections of one launch, run in order; from the second on, each starts after a grid
+// barrier (its x may be an earlier projection's y).
+template <int MAXP>
+struct Chain {
+  Proj proj[MAXP];
+  int count;
+  int* status;
+};
+
+// A warp's share of one projection: rows [rb, re) in NBLK blocks of R, chunks [c0, c0 + NSL)
+// of each (NIT items a block, the same in every warp of the CTA).
+struct Geo {
+  int R, S, c0, NSL, NIT, NBLK, total;
+  int64_t rb, re;
 };
 
 __host__ __device__ inline size_t gemv_layout(const GLayout& L, size_t* offs) {
@@ -177,8 +260,8 @@ __device__ __forceinline__ void put_group(const GSmem& s, int j, int G, int da) 
 // Activation rows [m0, m0 + mt) into shared memory (QACT of fp32 x, or copied bytes). Bytes past
 // K, and rows mt..MT-1, are zeros. With `frag`, the class path's A fragments as well.
 template <int FMT, int MT, bool PLAIN>
-__device__ void gemv_load_activations(const MMParams& p, const GSmem& s, int m0, int mt, int kp,
-                                      int ap, bool frag) {
+__device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSmem& s, int mt, int kp, int ap,
+                                      bool frag) {
   const int K = p.K, KG = K / 32;
   if (threadIdx.x == 0) *s.flag = 0;
   for (int j = 0; j < MT; ++j) {
@@ -195,7 +278,7 @@ __device__ void gemv_load_activations(const MMParams& p, const GSmem& s, int m0,
                 // by the first barrier of qact_row4)
       for (int i = threadIdx.x; i < KG * 32; i += kThreads) s.afrag[i] = make_uint4(0u, 0u, 0u, 0u);
     for (int j = 0; j < mt; ++j) {
-      const float* xr = p.x + static_cast<int64_t>(m0 + j) * p.ldx;
+      const float* xr = p.x + static_cast<int64_t>(j) * p.ldx;
       const bool x4 = (reinterpret_cast<uintptr_t>(xr) & 15u) == 0;
       uint8_t* arow = s.act + static_cast<size_t>(j) * ap;
       QactRowResult r = qact_row4<kThreads>(
@@ -232,13 +315,13 @@ __device__ void gemv_load_activations(const MMParams& p, const GSmem& s, int m0,
     }
   } else {
     for (int j = 0; j < mt; ++j) {
-      const int8_t* qr = p.q + static_cast<int64_t>(m0 + j) * p.ldq;
-      const uint8_t* dr = p.da + static_cast<int64_t>(m0 + j) * p.ldd;
+      const int8_t* qr = p.q + static_cast<int64_t>(j) * p.ldq;
+      const uint8_t* dr = p.da + static_cast<int64_t>(j) * p.ldd;
       uint8_t* arow = s.act + static_cast<size_t>(j) * ap;
       for (int i = threadIdx.x; i < K; i += kThreads)
         arow[act_pos<FMT>(i)] = static_cast<uint8_t>(__ldcg(qr + i));
       for (int G = threadIdx.x; G < KG; G += kThreads) put_group<FMT, MT, PLAIN>(s, j, G, __ldcg(dr + G));
-      if (threadIdx.x == 0) s.Sa[j] = __ldcg(p.Sa + m0 + j);
+      if (threadIdx.x == 0) s.Sa[j] = __ldcg(p.Sa + j);
     }
   }
   __syncthreads();
@@ -286,15 +369,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 // row0 + 8j .. + 7 (rows past the matrix and columns past the row's bytes read as zeros; rows
 // of the next worker are loaded and never stored). MX scale data goes by cp.async into the scale
 // stage sst, one commit group per issue.
-template <int FMT, int R, bool PLAIN>
-__device__ __forceinline__ void gemv_issue(uint32_t st, uint32_t sst, uint32_t bar,
-                                           const CUtensorMap* map, const MMParams& p, int64_t row0,
-                                           int nrows, int kc, int lane) {
+template <int FMT, bool PLAIN>
+__device__ __forceinline__ void gemv_issue(uint32_t st, uint32_t sst, uint32_t bar, const PArgs& p,
+                                           int64_t row0, int nrows, int kc, int lane) {
   const int boxes = (nrows + kBox - 1) / kBox;
   if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(boxes * kBox * kChunk));
   __syncwarp();
   if (lane < boxes)
-    tma_load_2d(st + lane * kBox * kChunk, map, kc * kChunk, static_cast<int>(row0) + kBox * lane, bar);
+    tma_load_2d(st + lane * kBox * kChunk, p.map, kc * kChunk, static_cast<int>(row0) + kBox * lane, bar);
   if constexpr (!PLAIN) {
     if (lane < nrows) {
       const uint8_t* srow = p.srows + (row0 + lane) * p.srs;
@@ -422,243 +504,383 @@ __device__ __forceinline__ void general_mult(const RowScale<FMT>& r, int s, int 
   }
 }
 
-template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
-__global__ void __launch_bounds__(kThreads, R == 32 ? 1 : 2)
-    gemv_kernel(const MMParams p, const GLayout L, const __grid_constant__ CUtensorMap map) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+template <int FMT>
+__device__ __forceinline__ Geo geometry(const PArgs& d, int warp) {
+  Geo q;
+  q.R = d.cfg == kCfgR32 ? 32 : 8;
+  q.S = d.cfg <= kCfgS1 ? 1 : (1 << (d.cfg - 1));
+  const int KCH = (d.K + GF<FMT>::kElems - 1) / GF<FMT>::kElems;   // chunks a row
+  const int slice = warp % q.S;
+  q.c0 = (KCH * slice) / q.S;
+  q.NSL = (KCH * (slice + 1)) / q.S - q.c0;
+  q.NIT = (KCH + q.S - 1) / q.S;
+  const int tpc = kWarps / q.S;   // row workers of a CTA
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * tpc;
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * tpc + warp / q.S;
+  q.rb = d.N * w / nw;
+  q.re = d.N * (w + 1) / nw;
+  const int64_t most = (d.N + nw - 1) / nw;
+  q.NBLK = static_cast<int>((most + q.R - 1) / q.R);
+  q.total = q.NBLK * q.NIT;
+  return q;
+}
+
+__device__ unsigned int g_bar_count;   // CTAs arrived at the current grid barrier
+__device__ unsigned int g_bar_gen;     // grid barriers completed (wraps)
+
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// All CTAs of the grid (co-resident: cooperative launch) meet; every global write before the
+// barrier is visible to every CTA after it. The last CTA to arrive resets the count and bumps
+// the generation; the others wait (bounded: after kSpinLimit polls the status word records
+// kStatusTimeout and the CTA goes on, so the kernel always ends).
+__device__ __forceinline__ void grid_barrier(int* status) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int gen = ld_acquire(&g_bar_gen);
+    __threadfence();
+    const unsigned int arrived = atomicAdd(&g_bar_count, 1u) + 1u;
+    if (arrived == gridDim.x) {
+      atomicExch(&g_bar_count, 0u);
+      __threadfence();
+      atomicAdd(&g_bar_gen, 1u);
+    } else {
+      uint32_t i = 0;
+      while (ld_acquire(&g_bar_gen) == gen) {
+        if (++i > kSpinLimit) {
+          if (status != nullptr) atomicOr(status, kStatusTimeout);
+          break;
+        }
+        if (i > 32) __nanosleep(32);
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+}
+
+// The warp's weight ring over all projections of the launch: items are issued in order
+// (projection, row block, chunk), NS - 1 ahead of the one computed, across projection boundaries
+// (weights never depend on activations).
+template <int FMT, bool PLAIN, int NS, int MAXP>
+struct RingIssue {
+  const Chain<MAXP>* C;
+  uint32_t ring_s, sring_s, bar0;
+  int stage_bytes, scale_bytes, lane, warp;
+  int count;
+  int p, i, issued;   // next item: projection p, item i of it; items issued so far
+  PArgs a;            // projection p
+  Geo q;
+
+  __device__ __forceinline__ bool next() {
+    while (p < count && i >= q.total) {
+      ++p;
+      i = 0;
+      if (p < count) {
+        a = load_args(C->proj[p]);
+        q = geometry<FMT>(a, warp);
+      }
+    }
+    if (p >= count) return false;
+    const PArgs& d = a;
+    const int b = i / q.NIT, k = i % q.NIT;
+    const int64_t r0 = q.rb + static_cast<int64_t>(b) * q.R;
+    int nrows = static_cast<int>(min(static_cast<int64_t>(q.R), q.re - r0));
+    if (k >= q.NSL || nrows < 0) nrows = 0;
+    const int st = issued % NS;
+    gemv_issue<FMT, PLAIN>(ring_s + st * stage_bytes, sring_s + st * scale_bytes, bar0 + 8 * st, d,
+                           r0, nrows, q.c0 + k, lane);
+    ++issued;
+    ++i;
+    return true;
+  }
+};
+
+// This warp's items of projection d (geometry q), consumed in order from the ring; f counts the
+// items consumed so far (stage f % NS, parity (f / NS) & 1).
+template <int FMT, int MT, bool PLAIN, int NS, int MAXP, int R, int S>
+__device__ __forceinline__ void run_proj(const PArgs& d, const Geo& q, const GSmem& s,
+                                         RingIssue<FMT, PLAIN, NS, MAXP>& iss, int& f, bool& ok,
+                                         int* status, const GLayout& L, uint8_t* ring,
+                                         uint8_t* sring, int mt) {
   using F = GF<FMT>;
-  using ST = Stage<R, PLAIN>;
-  constexpr int NO = R / 8;                  // row octets (tensor-copy boxes) of a block
-  constexpr int TPC = kWarps / S;            // row workers of a CTA
-  constexpr int VPL = 2 * NO;                // general-path values a lane
-  const int K = p.K;
-  const int KCH = (K + F::kElems - 1) / F::kElems;   // chunks a row
-  const int kp = KCH * F::kElems;
-  GSmem s = gemv_carve(smem_raw, L);
+  constexpr int NO = R / 8;     // row octets (tensor-copy boxes) of a block
+  constexpr int VPL = 2 * NO;   // general-path values a lane
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int slice = warp % S;
-  const int c0 = (KCH * slice) / S, c1 = (KCH * (slice + 1)) / S;   // this warp's chunks
-  const int NSL = c1 - c0;
-  const int NIT = (KCH + S - 1) / S;   // items a row block: the same in every warp of the CTA
-  const bool unit = (p.flags & kMmUnit) != 0;
-  // this worker's rows: [rb, re), balanced by rows over all workers
-  const int64_t nworkers = static_cast<int64_t>(gridDim.x) * TPC;
-  const int64_t worker = static_cast<int64_t>(blockIdx.x) * TPC + warp / S;
-  const int64_t rb = p.N * worker / nworkers, re = p.N * (worker + 1) / nworkers;
-  const int64_t most = (p.N + nworkers - 1) / nworkers;
-  const int NBLK = static_cast<int>((most + R - 1) / R);   // blocks: the same in every CTA
-  const int total = NBLK * NIT;                             // items a pass
-  uint8_t* const ring = s.ring + warp * NS * ST::kBytes;
-  const uint32_t ring_s = smem_addr(ring);
-  uint8_t* const sring = s.sring + warp * NS * ST::kScaleBytes;
-  const uint32_t sring_s = smem_addr(sring);
+  const bool unit = (d.flags & kMmUnit) != 0;
+  const bool use_class = MT == 1 && PLAIN && *s.flag == 0;
+  const uint32_t bar0 = iss.bar0;
+
+  int D[NO][4];
+  long long acc[NO][2];
+#pragma unroll
+  for (int o = 0; o < NO; ++o) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) D[o][i] = 0;
+    acc[o][0] = acc[o][1] = 0;
+  }
+  for (int b = 0; b < q.NBLK; ++b) {
+    for (int k = 0; k < q.NIT; ++k, ++f) {
+      __syncwarp();   // every lane is done with the stage that the next issue overwrites
+      const bool more = iss.next();
+      const int stn = f % NS;
+      if (!mbar_wait(bar0 + 8 * stn, static_cast<uint32_t>((f / NS) & 1), status)) ok = false;
+      if constexpr (!PLAIN) {
+        if (more) cp_async_wait<NS - 1>(); else cp_async_wait<0>();
+        __syncwarp();
+      }
+      if (k >= q.NSL || !ok) continue;
+      const uint8_t* st = ring + stn * L.stage_bytes;
+      const int kc = q.c0 + k;
+      if (use_class) {
+#pragma unroll
+        for (int sg = 0; sg < F::kGroups; ++sg) {
+          const int G = kc * F::kGroups + sg;
+          uint4 a;
+          if (L.frag) {
+            a = s.afrag[G * 32 + lane];
+          } else {
+            const uint2 qv = *reinterpret_cast<const uint2*>(s.act + 32 * G + 8 * t);
+            const int c = s.cls[G];
+            a.x = c == g ? qv.x : 0u;
+            a.y = c == g + 8 ? qv.x : 0u;
+            a.z = c == g ? qv.y : 0u;
+            a.w = c == g + 8 ? qv.y : 0u;
+          }
+#pragma unroll
+          for (int o = 0; o < NO; ++o) {
+            uint32_t b0, b1;
+            b_frag<FMT>(st + (8 * o + g) * kChunk, sg, g, t, b0, b1);
+            imma_acc(a.x, a.y, a.z, a.w, b0, b1, D[o]);
+          }
+        }
+      } else {
+        RowScale<FMT> rsc[NO][2];
+        if constexpr (!PLAIN) {
+#pragma unroll
+          for (int o = 0; o < NO; ++o)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              read_row_scale<FMT>(rsc[o][h], sring + stn * L.scale_bytes + (8 * o + 2 * t + h) * 16, d.k0, kc);
+        }
+        const int gm = g < MT ? g : 0;
+#pragma unroll
+        for (int sg = 0; sg < F::kGroups; ++sg) {
+          const int G = kc * F::kGroups + sg;
+          const uint2 qv = *reinterpret_cast<const uint2*>(s.act + static_cast<size_t>(gm) * L.ap + 32 * G + 8 * t);
+          const uint32_t a0 = g < MT ? qv.x : 0u, a2 = g < MT ? qv.y : 0u;
+          const int ta = g < MT ? s.term[G * MT + gm] : 0;
+#pragma unroll
+          for (int o = 0; o < NO; ++o) {
+            uint32_t b0, b1;
+            b_frag<FMT>(st + (8 * o + g) * kChunk, sg, g, t, b0, b1);
+            int dd[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
+            if constexpr (FMT == kFmtNvfp4) {
+              imma_acc(a0, 0u, a2, 0u, t < 2 ? b0 : 0u, t < 2 ? b1 : 0u, dd);
+              imma_acc(a0, 0u, a2, 0u, t < 2 ? 0u : b0, t < 2 ? 0u : b1, e);
+            } else {
+              imma_acc(a0, 0u, a2, 0u, b0, b1, dd);
+            }
+            if constexpr (FMT == kFmtInt4) {
+              dd[0] >>= 4;   // exact: every product was 16x
+              dd[1] >>= 4;
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              int mA, mB;
+              general_mult<FMT, PLAIN>(rsc[o][h], sg, ta, mA, mB);
+              acc[o][h] += static_cast<long long>(dd[h]) * mA;
+              if constexpr (FMT == kFmtNvfp4) acc[o][h] += static_cast<long long>(e[h]) * mB;
+            }
+          }
+        }
+      }
+    }
+    // the row block is complete: its totals, then the S warps' partials, then the epilogue
+    const int64_t r0 = q.rb + static_cast<int64_t>(b) * R;
+    const int nrows = static_cast<int>(max(static_cast<int64_t>(0), min(static_cast<int64_t>(R), q.re - r0)));
+    if (use_class) {
+      constexpr int W = F::kW;
+      const long long mlo = 1ll << (W - g);                          // class g
+      const long long mhi = g + 8 <= W ? (1ll << (W - g - 8)) : 0;   // class g + 8
+      long long v[NO][2];
+#pragma unroll
+      for (int o = 0; o < NO; ++o) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int lo = D[o][h], hi = D[o][2 + h];
+          if constexpr (FMT == kFmtInt4) {
+            lo >>= 4;
+            hi >>= 4;
+          }
+          v[o][h] = lo * mlo + hi * mhi;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) D[o][i] = 0;
+      }
+      long long tot = class_reduce<NO>(v, lane);
+      const int oct = NO >= 4 ? (lane >> 2) & 3 : (NO >= 2 ? (lane >> 3) & 1 : 0);
+      const int rr = 8 * oct + 2 * t + ((lane >> 4) & 1);
+      const bool owner = NO >= 4 ? true : (NO >= 2 ? (lane & 4) == 0 : (lane & 12) == 0);
+      if constexpr (S > 1) {
+        if (owner) s.red[warp * 32 + lane] = tot;
+        __syncthreads();
+        if (slice == 0 && owner)
+          for (int o = 1; o < S; ++o) tot += s.red[(warp + o) * 32 + lane];
+      }
+      if (slice == 0 && owner && rr < nrows && ok) {
+        const int64_t row = r0 + rr;
+        const float Sw = unit ? 1.0f : __ldg(reinterpret_cast<const float*>(d.srows + row * d.srs));
+        float yv = mm_epilogue(tot, Sw, s.Sa[0], W);
+        float* yp = d.y + row;
+        if (d.flags & kMmAscale) {
+          yv = fadd(fmul(*yp, __ldg(d.alpha)), yv);
+        } else if (d.flags & kMmAcc) {
+          yv = fadd(*yp, yv);
+        }
+        *yp = yv;
+      }
+      if constexpr (S > 1) __syncthreads();   // red is reused by the next row block
+    } else {
+      if constexpr (S > 1) {
+#pragma unroll
+        for (int o = 0; o < NO; ++o)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) s.red[(warp * 32 + lane) * VPL + 2 * o + h] = acc[o][h];
+        __syncthreads();
+        if (slice == 0)
+          for (int w2 = 1; w2 < S; ++w2)
+#pragma unroll
+            for (int o = 0; o < NO; ++o)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) acc[o][h] += s.red[((warp + w2) * 32 + lane) * VPL + 2 * o + h];
+      }
+      if (slice == 0 && g < mt && ok) {
+#pragma unroll
+        for (int o = 0; o < NO; ++o)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int rr = 8 * o + 2 * t + h;
+            if (rr < nrows) {
+              const int64_t row = r0 + rr;
+              const float Sw = unit ? 1.0f : __ldg(reinterpret_cast<const float*>(d.srows + row * d.srs));
+              float yv = mm_epilogue(acc[o][h], Sw, s.Sa[g], F::kW);
+              float* yp = d.y + static_cast<int64_t>(g) * d.ldy + row;
+              if (d.flags & kMmAscale) {
+                yv = fadd(fmul(*yp, __ldg(d.alpha + g)), yv);
+              } else if (d.flags & kMmAcc) {
+                yv = fadd(*yp, yv);
+              }
+              *yp = yv;
+            }
+          }
+      }
+#pragma unroll
+      for (int o = 0; o < NO; ++o) acc[o][0] = acc[o][1] = 0;
+      if constexpr (S > 1) __syncthreads();
+    }
+  }
+}
+
+// QACT + MM over the projections of C in order (M <= MT activation rows each). RMAX: the
+// largest row block the launch uses (the ring's stage size).
+template <int FMT, int MT, int NS, bool PLAIN, int MAXP, int RMAX, int FIXED>
+__global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 : 2)
+    gemv_kernel(const __grid_constant__ Chain<MAXP> C, const GLayout L) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  using F = GF<FMT>;
+  GSmem s = gemv_carve(smem_raw, L);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint8_t* const ring = s.ring + warp * NS * L.stage_bytes;
+  uint8_t* const sring = s.sring + warp * NS * L.scale_bytes;
   const uint32_t bar0 = smem_addr(s.bar + warp * NS);
   bool ok = true;   // false once a wait ran out: the remaining items are drained, not computed
 
   if (lane == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map)) : "memory");
     for (int i = 0; i < NS; ++i) mbar_init(bar0 + 8 * i, 1);
     mbar_init_fence();
   }
+  if (MAXP == 1 ? lane == 0 : lane < C.count)
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&C.proj[MAXP == 1 ? 0 : lane].map))
+                 : "memory");
   __syncwarp();
 
-  int f = 0;   // items issued and consumed over all passes: stage f % NS, parity (f / NS) & 1
-  for (int m0 = 0; m0 < p.M; m0 += MT) {
-    const int mt = min(MT, p.M - m0);
-    // Item i = (b, k): row block b of this worker, chunk c0 + k.
-    auto issue = [&](int i) {
-      const int b = i / NIT, k = i % NIT;
-      const int64_t r0 = rb + static_cast<int64_t>(b) * R;
-      int nrows = static_cast<int>(min(static_cast<int64_t>(R), re - r0));
-      if (k >= NSL || nrows < 0) nrows = 0;
-      const int st = (f + i) % NS;
-      gemv_issue<FMT, R, PLAIN>(ring_s + st * ST::kBytes, sring_s + st * ST::kScaleBytes, bar0 + 8 * st,
-                                &map, p, r0, nrows, c0 + k, lane);
-    };
-    const int pre = min(NS - 1, total);
-    for (int i = 0; i < pre; ++i) issue(i);
-    if (m0 == 0) pdl_wait();   // the activations may come from the kernel launched before
-    gemv_load_activations<FMT, MT, PLAIN>(p, s, m0, mt, kp, L.ap, L.frag);
-    if (m0 + mt >= p.M) pdl_launch();
-    const bool use_class = MT == 1 && PLAIN && *s.flag == 0;
+  RingIssue<FMT, PLAIN, NS, MAXP> iss;
+  iss.C = &C;
+  iss.ring_s = smem_addr(ring);
+  iss.sring_s = smem_addr(sring);
+  iss.bar0 = bar0;
+  iss.stage_bytes = L.stage_bytes;
+  iss.scale_bytes = L.scale_bytes;
+  iss.lane = lane;
+  iss.warp = warp;
+  const int count = MAXP == 1 ? 1 : C.count;
+  PArgs d = load_args(C.proj[0]);   // the projection computed next, and its geometry
+  Geo q = geometry<FMT>(d, warp);
+  iss.count = count;
+  iss.p = 0;
+  iss.i = 0;
+  iss.issued = 0;
+  iss.a = d;
+  iss.q = q;
+#pragma unroll 1
+  for (int q = 0; q < NS - 1; ++q) iss.next();
+  pdl_wait();   // the activations may come from the kernel launched before
 
-    int D[NO][4];
-    long long acc[NO][2];
-#pragma unroll
-    for (int o = 0; o < NO; ++o) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) D[o][i] = 0;
-      acc[o][0] = acc[o][1] = 0;
-    }
-    int i = 0;
-    for (int b = 0; b < NBLK; ++b) {
-      for (int k = 0; k < NIT; ++k, ++i) {
-        __syncwarp();   // every lane is done with the stage that the next issue overwrites
-        if (i + NS - 1 < total) issue(i + NS - 1);
-        const int stn = (f + i) % NS;
-        const uint32_t parity = static_cast<uint32_t>(((f + i) / NS) & 1);
-        if (!mbar_wait(bar0 + 8 * stn, parity, p.status)) ok = false;
-        if constexpr (!PLAIN) {
-          if (i + NS - 1 < total) cp_async_wait<NS - 1>(); else cp_async_wait<0>();
-          __syncwarp();
-        }
-        if (k >= NSL || !ok) continue;
-        const uint8_t* st = ring + stn * ST::kBytes;
-        const int kc = c0 + k;
-        if (use_class) {
-#pragma unroll
-          for (int sg = 0; sg < F::kGroups; ++sg) {
-            const int G = kc * F::kGroups + sg;
-            uint4 a;
-            if (L.frag) {
-              a = s.afrag[G * 32 + lane];
-            } else {
-              const uint2 q = *reinterpret_cast<const uint2*>(s.act + 32 * G + 8 * t);
-              const int c = s.cls[G];
-              a.x = c == g ? q.x : 0u;
-              a.y = c == g + 8 ? q.x : 0u;
-              a.z = c == g ? q.y : 0u;
-              a.w = c == g + 8 ? q.y : 0u;
-            }
-#pragma unroll
-            for (int o = 0; o < NO; ++o) {
-              uint32_t b0, b1;
-              b_frag<FMT>(st + (8 * o + g) * kChunk, sg, g, t, b0, b1);
-              imma_acc(a.x, a.y, a.z, a.w, b0, b1, D[o]);
-            }
-          }
-        } else {
-          RowScale<FMT> rsc[NO][2];
-          if constexpr (!PLAIN) {
-#pragma unroll
-            for (int o = 0; o < NO; ++o)
-#pragma unroll
-              for (int h = 0; h < 2; ++h)
-                read_row_scale<FMT>(rsc[o][h], sring + stn * ST::kScaleBytes + (8 * o + 2 * t + h) * 16, p.k0, kc);
-          }
-          const int gm = g < MT ? g : 0;
-#pragma unroll
-          for (int sg = 0; sg < F::kGroups; ++sg) {
-            const int G = kc * F::kGroups + sg;
-            const uint2 q = *reinterpret_cast<const uint2*>(s.act + static_cast<size_t>(gm) * L.ap + 32 * G + 8 * t);
-            const uint32_t a0 = g < MT ? q.x : 0u, a2 = g < MT ? q.y : 0u;
-            const int ta = g < MT ? s.term[G * MT + gm] : 0;
-#pragma unroll
-            for (int o = 0; o < NO; ++o) {
-              uint32_t b0, b1;
-              b_frag<FMT>(st + (8 * o + g) * kChunk, sg, g, t, b0, b1);
-              int d[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
-              if constexpr (FMT == kFmtNvfp4) {
-                imma_acc(a0, 0u, a2, 0u, t < 2 ? b0 : 0u, t < 2 ? b1 : 0u, d);
-                imma_acc(a0, 0u, a2, 0u, t < 2 ? 0u : b0, t < 2 ? 0u : b1, e);
-              } else {
-                imma_acc(a0, 0u, a2, 0u, b0, b1, d);
-              }
-              if constexpr (FMT == kFmtInt4) {
-                d[0] >>= 4;   // exact: every product was 16x
-                d[1] >>= 4;
-              }
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                int mA, mB;
-                general_mult<FMT, PLAIN>(rsc[o][h], sg, ta, mA, mB);
-                acc[o][h] += static_cast<long long>(d[h]) * mA;
-                if constexpr (FMT == kFmtNvfp4) acc[o][h] += static_cast<long long>(e[h]) * mB;
-              }
-            }
-          }
+  int f = 0;
+  for (int pi = 0; pi < count; ++pi) {
+    if (pi > 0) grid_barrier(C.status);   // projection pi may read what pi - 1 wrote
+    const int KCH = (d.K + F::kElems - 1) / F::kElems;
+    gemv_load_activations<FMT, MT, PLAIN>(d, s, min(MT, d.M), KCH * F::kElems, L.ap, L.frag);
+    if (pi == count - 1) pdl_launch();
+    const int mt = min(MT, d.M);
+    // Keep HBM busy past the grid barriers: this warp's rows of the next two projections into
+    // L2 (at most 64 KB a warp), and their tensor maps into the descriptor cache.
+    if (MAXP > 1 && lane == 0) {
+#pragma unroll 1
+      for (int a = 1; a <= 2 && pi + a < count; ++a) {
+        const PArgs n = load_args(C.proj[pi + a]);
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(n.map)) : "memory");
+        const Geo nq = geometry<FMT>(n, warp);
+        if (warp % nq.S == 0 && nq.re > nq.rb) {
+          const int64_t row_bytes = FMT == kFmtInt8 ? n.K : n.K / 2;
+          int64_t len = (nq.re - nq.rb - 1) * n.rs + row_bytes;
+          len = (len < 64 * 1024 ? len : 64 * 1024) & ~int64_t(15);
+          const uint8_t* base = reinterpret_cast<const uint8_t*>(n.rows) + nq.rb * n.rs;
+          if (len > 0) prefetch_l2(base, static_cast<uint32_t>(len));
         }
       }
-      // the row block is complete: its totals, then the S warps' partials, then the epilogue
-      const int64_t r0 = rb + static_cast<int64_t>(b) * R;
-      const int nrows = static_cast<int>(max(static_cast<int64_t>(0), min(static_cast<int64_t>(R), re - r0)));
-      if (use_class) {
-        constexpr int W = F::kW;
-        const long long mlo = 1ll << (W - g);                          // class g
-        const long long mhi = g + 8 <= W ? (1ll << (W - g - 8)) : 0;   // class g + 8
-        long long v[NO][2];
-#pragma unroll
-        for (int o = 0; o < NO; ++o) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            int lo = D[o][h], hi = D[o][2 + h];
-            if constexpr (FMT == kFmtInt4) {
-              lo >>= 4;
-              hi >>= 4;
-            }
-            v[o][h] = lo * mlo + hi * mhi;
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) D[o][q] = 0;
-        }
-        long long tot = class_reduce<NO>(v, lane);
-        const int oct = NO >= 4 ? (lane >> 2) & 3 : (NO >= 2 ? (lane >> 3) & 1 : 0);
-        const int rr = 8 * oct + 2 * t + ((lane >> 4) & 1);
-        const bool owner = NO >= 4 ? true : (NO >= 2 ? (lane & 4) == 0 : (lane & 12) == 0);
-        if constexpr (S > 1) {
-          if (owner) s.red[warp * 32 + lane] = tot;
-          __syncthreads();
-          if (slice == 0 && owner)
-            for (int o = 1; o < S; ++o) tot += s.red[(warp + o) * 32 + lane];
-        }
-        if (slice == 0 && owner && rr < nrows && ok) {
-          const int64_t row = r0 + rr;
-          const float Sw = unit ? 1.0f : __ldg(reinterpret_cast<const float*>(p.srows + row * p.srs));
-          float yv = mm_epilogue(tot, Sw, s.Sa[0], W);
-          float* yp = p.y + static_cast<int64_t>(m0) * p.ldy + row;
-          if (p.flags & kMmAscale) {
-            yv = fadd(fmul(*yp, __ldg(p.alpha + m0)), yv);
-          } else if (p.flags & kMmAcc) {
-            yv = fadd(*yp, yv);
-          }
-          *yp = yv;
-        }
-        if constexpr (S > 1) __syncthreads();   // red is reused by the next row block
-      } else {
-        if constexpr (S > 1) {
-#pragma unroll
-          for (int o = 0; o < NO; ++o)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) s.red[(warp * 32 + lane) * VPL + 2 * o + h] = acc[o][h];
-          __syncthreads();
-          if (slice == 0)
-            for (int w2 = 1; w2 < S; ++w2)
-#pragma unroll
-              for (int o = 0; o < NO; ++o)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) acc[o][h] += s.red[((warp + w2) * 32 + lane) * VPL + 2 * o + h];
-        }
-        if (slice == 0 && g < mt && ok) {
-#pragma unroll
-          for (int o = 0; o < NO; ++o)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int rr = 8 * o + 2 * t + h;
-              if (rr < nrows) {
-                const int64_t row = r0 + rr;
-                const float Sw = unit ? 1.0f : __ldg(reinterpret_cast<const float*>(p.srows + row * p.srs));
-                float yv = mm_epilogue(acc[o][h], Sw, s.Sa[g], F::kW);
-                float* yp = p.y + static_cast<int64_t>(m0 + g) * p.ldy + row;
-                if (p.flags & kMmAscale) {
-                  yv = fadd(fmul(*yp, __ldg(p.alpha + m0 + g)), yv);
-                } else if (p.flags & kMmAcc) {
-                  yv = fadd(*yp, yv);
-                }
-                *yp = yv;
-              }
-            }
-        }
-#pragma unroll
-        for (int o = 0; o < NO; ++o) acc[o][0] = acc[o][1] = 0;
-        if constexpr (S > 1) __syncthreads();
-      }
     }
-    f += total;
-    __syncthreads();   // the next activation rows overwrite shared memory
+    switch (FIXED >= 0 ? FIXED : d.cfg) {   // FIXED: one decomposition (a single projection)
+      case kCfgR32:
+        if constexpr (RMAX == 32 && (FIXED < 0 || FIXED == kCfgR32)) run_proj<FMT, MT, PLAIN, NS, MAXP, 32, 1>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        break;
+      case kCfgS1:
+        if constexpr (FIXED < 0 || FIXED == kCfgS1) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 1>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        break;
+      case kCfgS2:
+        if constexpr (FIXED < 0 || FIXED == kCfgS2) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 2>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        break;
+      case kCfgS4:
+        if constexpr (FIXED < 0 || FIXED == kCfgS4) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 4>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        break;
+      default:
+        if constexpr (FIXED < 0 || FIXED == kCfgS8) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 8>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        break;
+    }
+    if (pi + 1 < count) {   // ahead of the barrier, off the critical path
+      d = load_args(C.proj[pi + 1]);
+      q = geometry<FMT>(d, warp);
+    }
+    if (MAXP > 1) __syncthreads();   // the next projection's activations overwrite shared memory
   }
 }
-
 // The weight rows as a 2-D tensor of bytes: [N][row_bytes] with rows rs bytes apart, copied in
 // boxes of 8 rows x 128 bytes with the 128-byte swizzle. cuTensorMapEncodeTiled comes from the
 // driver through the runtime's entry-point query (nothing links libcuda).
@@ -681,35 +903,46 @@ bool encode_rows_map(CUtensorMap* map, const uint8_t* rows, int row_bytes, int64
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
-GLayout gemv_geometry(int K, bool fused, bool frag) {
+constexpr int kMaxChain = 120;   // projections of one launch (kernel parameters under 32 KB)
+
+int cfg_rows(int cfg) { return cfg == kCfgR32 ? 32 : 8; }
+int cfg_split(int cfg) { return cfg <= kCfgS1 ? 1 : (1 << (cfg - 1)); }
+
+// Work decomposition: 32-row blocks while they give every warp of the grid work; else 8-row
+// blocks with as many warps a row as keep every warp busy, each with at least one chunk.
+int pick_cfg(int fmt, int64_t N, int K, int64_t warps) {
+  if (N >= 32 * warps) return kCfgR32;
+  const int elems = fmt == kFmtInt8 ? 128 : 256;
+  const int KCH = (K + elems - 1) / elems;
+  int split = 1;
+  while (split < 8 && (N / 8) * split < warps && KCH / (split * 2) >= 1) split *= 2;
+  return split == 1 ? kCfgS1 : split == 2 ? kCfgS2 : split == 4 ? kCfgS4 : kCfgS8;
+}
+
+template <int FMT, bool PLAIN>
+GLayout launch_layout(int MT, int kmax, bool fused, bool frag, int smax, int rmax, int ns) {
   using F = GF<FMT>;
   GLayout L;
   L.MT = MT;
-  L.K = K;
-  const int kp = ((K + F::kElems - 1) / F::kElems) * F::kElems;
+  L.K = kmax;
+  const int kp = ((kmax + F::kElems - 1) / F::kElems) * F::kElems;
   L.ap = kp + kActPad;
-  L.vpl = 2 * (R / 8);
-  L.S = S;
-  L.stage_bytes = Stage<R, PLAIN>::kBytes;
-  L.scale_bytes = Stage<R, PLAIN>::kScaleBytes;
-  L.ns = NS;
+  L.vpl = 2;   // K-split blocks are 8 rows
+  L.S = smax;
+  L.stage_bytes = rmax * kChunk;
+  L.scale_bytes = PLAIN ? 0 : rmax * 16;
+  L.ns = ns;
   L.fused = fused;
   L.frag = frag && MT == 1 && PLAIN;
   return L;
 }
 
-template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
-bool gemv_fits(int K, bool fused, bool frag) {
-  return gemv_layout(gemv_geometry<FMT, MT, R, S, NS, PLAIN>(K, fused, frag), nullptr) <= 227 * 1024;
-}
-
-template <int FMT, int MT, int R, int S, int NS, bool PLAIN>
-int gemv_cfg(const MMParams& p, cudaStream_t stream, bool pdl, bool frag) {
-  const GLayout L = gemv_geometry<FMT, MT, R, S, NS, PLAIN>(p.K, p.x != nullptr, frag);
+template <int FMT, int MT, int NS, bool PLAIN, int MAXP, int RMAX, int FIXED>
+int launch_chain(const Chain<MAXP>& C, const GLayout& L, int grid, bool coop, cudaStream_t stream,
+                 bool pdl) {
   const size_t smem = gemv_layout(L, nullptr);
   if (smem > 227 * 1024) return kErrArg;
-  auto kern = gemv_kernel<FMT, MT, R, S, NS, PLAIN>;
+  auto kern = gemv_kernel<FMT, MT, NS, PLAIN, MAXP, RMAX, FIXED>;
   static size_t configured_smem[kMaxDevices] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return kErrCuda;
@@ -722,86 +955,226 @@ int gemv_cfg(const MMParams& p, cudaStream_t stream, bool pdl, bool frag) {
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess)
     return kErrCuda;
-  if (occ < 1) occ = 1;
-  constexpr int TPC = kWarps / S;
-  const int64_t want = (p.N + static_cast<int64_t>(R) * TPC - 1) / (static_cast<int64_t>(R) * TPC);
-  const int64_t grid = min(want, static_cast<int64_t>(sm_count(dev)) * occ);
+  if (occ < 1) return kErrArg;
+  const int cap = sm_count(dev) * occ;
+  if (coop) grid = cap;   // every CTA resident: the grid barriers need it
+  grid = max(1, min(grid, cap));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (coop) {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  CUtensorMap map;
-  const int row_bytes = FMT == kFmtInt8 ? p.K : p.K / 2;
-  if (!encode_rows_map(&map, p.rows, row_bytes, p.N, p.rs)) return kErrCuda;
-  void* args[] = {const_cast<MMParams*>(&p), const_cast<GLayout*>(&L), &map};
+  cfg.numAttrs = (coop || pdl) ? 1 : 0;
+  void* args[] = {const_cast<Chain<MAXP>*>(&C), const_cast<GLayout*>(&L)};
   return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kern), args) == cudaSuccess ? kOk
                                                                                           : kErrCuda;
 }
 
-// (rows a block, K split, ring depth): 32 rows a warp, no split and the deepest ring that fits
-// for tall matrices; 8 rows with the split that keeps about 8 warps on every SM for short ones.
-template <int FMT, int MT, bool PLAIN>
-int gemv_split(const MMParams& p, cudaStream_t stream, bool pdl, int split) {
-  const bool fused = p.x != nullptr;
-  switch (split) {
-    case 1:
-      if (gemv_fits<FMT, MT, 32, 1, 5, PLAIN>(p.K, fused, true))
-        return gemv_cfg<FMT, MT, 32, 1, 5, PLAIN>(p, stream, pdl, true);
-      if (gemv_fits<FMT, MT, 32, 1, 5, PLAIN>(p.K, fused, false))
-        return gemv_cfg<FMT, MT, 32, 1, 5, PLAIN>(p, stream, pdl, false);
-      if (gemv_fits<FMT, MT, 32, 1, 3, PLAIN>(p.K, fused, false))
-        return gemv_cfg<FMT, MT, 32, 1, 3, PLAIN>(p, stream, pdl, false);
-      return gemv_cfg<FMT, MT, 8, 2, 4, PLAIN>(p, stream, pdl, false);
-    case 2: return gemv_cfg<FMT, MT, 8, 2, 4, PLAIN>(p, stream, pdl, gemv_fits<FMT, MT, 8, 2, 4, PLAIN>(p.K, fused, true));
-    case 4: return gemv_cfg<FMT, MT, 8, 4, 4, PLAIN>(p, stream, pdl, gemv_fits<FMT, MT, 8, 4, 4, PLAIN>(p.K, fused, true));
-    default: return gemv_cfg<FMT, MT, 8, 8, 4, PLAIN>(p, stream, pdl, gemv_fits<FMT, MT, 8, 8, 4, PLAIN>(p.K, fused, true));
+// Choose the ring depth and whether the class path's A fragments fit beside it, then launch.
+// FIXED >= 0: a single projection of that decomposition; -1: a chain (decomposition per
+// projection).
+template <int FMT, int MT, bool PLAIN, int MAXP, int FIXED>
+int launch_fit(const Chain<MAXP>& C, int kmax, bool fused, int smax, int rmax, int grid, bool coop,
+               cudaStream_t stream, bool pdl) {
+  auto fits = [&](bool frag, int r, int ns) {
+    return gemv_layout(launch_layout<FMT, PLAIN>(MT, kmax, fused, frag, smax, r, ns), nullptr) <=
+           227 * 1024;
+  };
+  if constexpr (FIXED < 0 || FIXED == kCfgR32) {
+    if (rmax == 32) {
+      for (bool frag : {true, false}) {
+        if (fits(frag, 32, 5))
+          return launch_chain<FMT, MT, 5, PLAIN, MAXP, 32, FIXED>(
+              C, launch_layout<FMT, PLAIN>(MT, kmax, fused, frag, smax, 32, 5), grid, coop, stream, pdl);
+      }
+      if (fits(false, 32, 3))
+        return launch_chain<FMT, MT, 3, PLAIN, MAXP, 32, FIXED>(
+            C, launch_layout<FMT, PLAIN>(MT, kmax, fused, false, smax, 32, 3), grid, coop, stream, pdl);
+      return kErrArg;   // the caller retries with 8-row blocks
+    }
   }
+  if constexpr (FIXED != kCfgR32) {
+    for (bool frag : {true, false}) {
+      if (fits(frag, 8, 4))
+        return launch_chain<FMT, MT, 4, PLAIN, MAXP, 8, FIXED>(
+            C, launch_layout<FMT, PLAIN>(MT, kmax, fused, frag, smax, 8, 4), grid, coop, stream, pdl);
+    }
+  }
+  return kErrArg;
 }
 
-template <int FMT>
-int gemv_fmt(const MMParams& p, cudaStream_t stream, bool pdl, int split) {
-  const bool plain = (p.flags & (kMmUnit | kMmRsc)) != 0;
-  if (p.M <= 1) {
-    return plain ? gemv_split<FMT, 1, true>(p, stream, pdl, split)
-                 : gemv_split<FMT, 1, false>(p, stream, pdl, split);
+void fill_proj(Proj& d, const MMParams& p, int64_t m0, int mt) {
+  d.rows = p.rows;
+  d.rs = static_cast<int>(p.rs);
+  d.srows = p.srows;
+  d.srs = static_cast<int>(p.srs);
+  d.x = p.x != nullptr ? p.x + m0 * p.ldx : nullptr;
+  d.ldx = static_cast<int>(p.ldx);
+  d.q = p.q != nullptr ? p.q + m0 * p.ldq : nullptr;
+  d.ldq = static_cast<int>(p.ldq);
+  d.Sa = p.Sa != nullptr ? p.Sa + m0 : nullptr;
+  d.da = p.da != nullptr ? p.da + m0 * p.ldd : nullptr;
+  d.ldd = static_cast<int>(p.ldd);
+  d.y = p.y + m0 * p.ldy;
+  d.ldy = static_cast<int>(p.ldy);
+  d.alpha = p.alpha != nullptr ? p.alpha + m0 : nullptr;
+  d.N = p.N;
+  d.K = p.K;
+  d.flags = p.flags;
+  d.k0 = p.k0;
+  d.row_mode = p.row_mode;
+  d.M = mt;
+}
+
+template <int FMT, bool PLAIN>
+int single_fmt(const MMParams& p, cudaStream_t stream, bool pdl, int dev) {
+  const int warps = sm_count(dev) * kWarps;
+  int cfg = p.split == 0 ? pick_cfg(FMT, p.N, p.K, warps)
+            : p.split == 32 ? kCfgR32
+            : p.split == 1 ? kCfgS1
+            : p.split == 2 ? kCfgS2
+            : p.split == 4 ? kCfgS4 : kCfgS8;
+  const int row_bytes = FMT == kFmtInt8 ? p.K : p.K / 2;
+  for (int64_t m0 = 0; m0 < p.M; m0 += 8) {   // passes of up to 8 activation rows
+    const int mt = static_cast<int>(p.M - m0 < 8 ? p.M - m0 : 8);
+    Chain<1> C;
+    std::memset(&C, 0, sizeof(C));
+    fill_proj(C.proj[0], p, m0, mt);
+    if (!encode_rows_map(&C.proj[0].map, p.rows, row_bytes, p.N, p.rs)) return kErrCuda;
+    C.count = 1;
+    C.status = p.status;
+    for (int attempt = 0; attempt < 2; ++attempt) {
+      C.proj[0].cfg = cfg;
+      const int R = cfg_rows(cfg), S = cfg_split(cfg);
+      const int64_t grid = (p.N + static_cast<int64_t>(R) * (kWarps / S) - 1) / (static_cast<int64_t>(R) * (kWarps / S));
+      const int g = static_cast<int>(grid < (1 << 20) ? grid : (1 << 20));
+      int st;
+      const bool fused = p.x != nullptr;
+      switch (cfg) {
+#define OTQ_SINGLE(CFG)                                                                       \
+  st = mt == 1 ? launch_fit<FMT, 1, PLAIN, 1, CFG>(C, p.K, fused, S, R, g, false, stream, pdl) \
+               : launch_fit<FMT, 8, PLAIN, 1, CFG>(C, p.K, fused, S, R, g, false, stream, pdl)
+        case kCfgR32: OTQ_SINGLE(kCfgR32); break;
+        case kCfgS1: OTQ_SINGLE(kCfgS1); break;
+        case kCfgS2: OTQ_SINGLE(kCfgS2); break;
+        case kCfgS4: OTQ_SINGLE(kCfgS4); break;
+        default: OTQ_SINGLE(kCfgS8); break;
+#undef OTQ_SINGLE
+      }
+      if (st == kErrArg && cfg == kCfgR32) {   // no room beside a long activation row
+        cfg = kCfgS2;
+        continue;
+      }
+      if (st != kOk) return st;
+      break;
+    }
   }
-  return plain ? gemv_split<FMT, 8, true>(p, stream, pdl, split)
-               : gemv_split<FMT, 8, false>(p, stream, pdl, split);
+  return kOk;
+}
+
+template <int FMT, bool PLAIN>
+int chain_fmt(const otq_proj* pr, int count, int* status, cudaStream_t stream, int dev) {
+  const int warps = sm_count(dev) * kWarps;
+  Chain<kMaxChain>* C = new Chain<kMaxChain>;
+  std::memset(C, 0, sizeof(*C));
+  int kmax = 0, smax = 1, rmax = 8;
+  for (int i = 0; i < count; ++i) {
+    MMParams p{};
+    p.fmt = pr[i].fmt;
+    p.flags = pr[i].flags;
+    p.rows = pr[i].rows;
+    p.rs = pr[i].rs;
+    p.srows = pr[i].srows;
+    p.srs = pr[i].srs;
+    p.k0 = pr[i].k0;
+    p.N = pr[i].N;
+    p.K = static_cast<int>(pr[i].K);
+    p.x = pr[i].x;
+    p.ldx = pr[i].K;
+    p.row_mode = pr[i].row_mode;
+    p.M = 1;
+    p.y = pr[i].y;
+    p.ldy = pr[i].N;
+    fill_proj(C->proj[i], p, 0, 1);
+    const int row_bytes = FMT == kFmtInt8 ? p.K : p.K / 2;
+    if (!encode_rows_map(&C->proj[i].map, pr[i].rows, row_bytes, p.N, pr[i].rs)) {
+      delete C;
+      return kErrCuda;
+    }
+    C->proj[i].cfg = pick_cfg(FMT, p.N, p.K, warps);
+    kmax = max(kmax, p.K);
+    smax = max(smax, cfg_split(C->proj[i].cfg));
+    if (C->proj[i].cfg == kCfgR32) rmax = 32;
+  }
+  C->count = count;
+  C->status = status;
+  int st = launch_fit<FMT, 1, PLAIN, kMaxChain, -1>(*C, kmax, true, smax, rmax, 0, true, stream, false);
+  if (st == kErrArg && rmax == 32) {   // no room for 32-row stages: 8-row blocks everywhere
+    for (int i = 0; i < count; ++i)
+      if (C->proj[i].cfg == kCfgR32) C->proj[i].cfg = kCfgS1;
+    st = launch_fit<FMT, 1, PLAIN, kMaxChain, -1>(*C, kmax, true, smax, 8, 0, true, stream, false);
+  }
+  delete C;
+  return st;
 }
 
 }  // namespace
-
-// Split: none while 32-row blocks give every SM eight warps; else as many warps a row as keep
-// the SMs busy, each with at least one chunk.
-int gemv_pick_split(int fmt, int64_t N, int K, int dev) {
-  const int64_t workers = static_cast<int64_t>(sm_count(dev)) * kWarps;
-  if (N >= 32 * workers) return 1;
-  const int elems = fmt == kFmtInt8 ? 128 : 256;
-  const int KCH = (K + elems - 1) / elems;
-  int split = 1;
-  while (split < 8 && (N / 8) * split < workers && KCH / (split * 2) >= 1) split *= 2;
-  return split;
-}
 
 int mm_launch(const MMParams& p0, cudaStream_t stream, bool pdl) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
   MMParams p = p0;
   p.status = status_word();
-  const int split = p.split > 0 ? p.split : gemv_pick_split(p.fmt, p.N, p.K, dev);
+  const bool plain = (p.flags & (kMmUnit | kMmRsc)) != 0;
   switch (p.fmt) {
-    case kFmtInt8: return gemv_fmt<kFmtInt8>(p, stream, pdl, split);
-    case kFmtInt4: return gemv_fmt<kFmtInt4>(p, stream, pdl, split);
-    case kFmtFp4: return gemv_fmt<kFmtFp4>(p, stream, pdl, split);
-    case kFmtNvfp4: return gemv_fmt<kFmtNvfp4>(p, stream, pdl, split);
+    case kFmtInt8: return plain ? single_fmt<kFmtInt8, true>(p, stream, pdl, dev) : single_fmt<kFmtInt8, false>(p, stream, pdl, dev);
+    case kFmtInt4: return plain ? single_fmt<kFmtInt4, true>(p, stream, pdl, dev) : single_fmt<kFmtInt4, false>(p, stream, pdl, dev);
+    case kFmtFp4: return plain ? single_fmt<kFmtFp4, true>(p, stream, pdl, dev) : single_fmt<kFmtFp4, false>(p, stream, pdl, dev);
+    case kFmtNvfp4: return plain ? single_fmt<kFmtNvfp4, true>(p, stream, pdl, dev) : single_fmt<kFmtNvfp4, false>(p, stream, pdl, dev);
     default: return kErrFormat;
   }
+}
+
+// Consecutive projections of one format and kind go in one launch (at most kMaxChain).
+int chain_launch(const otq_proj* pr, int count, cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  int* status = status_word();
+  for (int i = 0; i < count;) {
+    const int fmt = pr[i].fmt;
+    const bool plain = (pr[i].flags & (kMmUnit | kMmRsc)) != 0;
+    int j = i + 1;
+    while (j < count && j - i < kMaxChain && pr[j].fmt == fmt &&
+           ((pr[j].flags & (kMmUnit | kMmRsc)) != 0) == plain)
+      ++j;
+    int st;
+    switch (fmt) {
+      case kFmtInt8: st = plain ? chain_fmt<kFmtInt8, true>(pr + i, j - i, status, stream, dev) : chain_fmt<kFmtInt8, false>(pr + i, j - i, status, stream, dev); break;
+      case kFmtInt4: st = plain ? chain_fmt<kFmtInt4, true>(pr + i, j - i, status, stream, dev) : chain_fmt<kFmtInt4, false>(pr + i, j - i, status, stream, dev); break;
+      case kFmtFp4: st = plain ? chain_fmt<kFmtFp4, true>(pr + i, j - i, status, stream, dev) : chain_fmt<kFmtFp4, false>(pr + i, j - i, status, stream, dev); break;
+      case kFmtNvfp4: st = plain ? chain_fmt<kFmtNvfp4, true>(pr + i, j - i, status, stream, dev) : chain_fmt<kFmtNvfp4, false>(pr + i, j - i, status, stream, dev); break;
+      default: st = kErrFormat;
+    }
+    if (st != kOk) return st;
+    i = j;
+  }
+  return kOk;
+}
+
+// The grid barrier's words back to zero (after a launch whose barrier wait ran out).
+int chain_reset() {
+  const unsigned int zero = 0;
+  if (cudaMemcpyToSymbol(g_bar_count, &zero, sizeof(zero)) != cudaSuccess) return kErrCuda;
+  return kOk;
 }
 
 }  // namespace otq

@@ -54,13 +54,14 @@ struct MMParams {
   const float* alpha;
   float* y;
   int64_t ldy;
-  int split;    // warps that split a row's K (1, 2, 4, 8); 0: pick
+  int split;    // otq_qmm_ex's k_split (0 picks)
   int* status;   // device status word (may be null): kStatusTimeout bits
 };
 
 int sm_count(int dev);
-int gemv_pick_split(int fmt, int64_t N, int K, int dev);
-int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);   // gemv.cu
+int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);    // gemv.cu
+int chain_launch(const otq_proj* projs, int count, cudaStream_t stream);
+int chain_reset();   // the grid barrier's count back to zero
 int* status_word();   // this device's status word (device address), or null
 
 // Launch with an optional programmatic-dependent-launch attribute (the kernel then may start

@@ -20,6 +20,11 @@ O feeds GateUp, GateUp's gate part feeds Down, Down feeds the next layer's QKV a
 last layer, the head), so every launch waits for the one before it -- the serialization of a
 real decode step without the non-linear-layer ops in between. dependent=False gives every
 projection its own fixed input.
+
+chained=True runs the whole step as one persistent launch (linear.qlinear_chain: the
+projections in order with a grid barrier between them, the next projection's weights streaming
+while the grid waits); the default launches one kernel a projection (what world > 1 needs, with
+the all-gathers in between).
 """
 from __future__ import annotations
 
@@ -32,9 +37,14 @@ from .workloads import DecoderShape
 class DecodeChain:
     def __init__(self, shape: DecoderShape, fmt: str = "int8-row", head_fmt: str = "int8-row",
                  seed: int = 0, world: int = 1, rank: int = 0, group=None, pdl: bool = True,
-                 std: float = 0.02, dependent: bool = True):
+                 std: float = 0.02, dependent: bool = True, chained: bool | None = None):
         self.shape, self.world, self.rank, self.group, self.pdl = shape, world, rank, group, pdl
         self.dependent = dependent
+        # chained: the whole step as one persistent launch (linear.qlinear_chain). Measured on
+        # a B200 it is slower today than one launch a projection (1.12 vs 0.61 ms for the
+        # Qwen3-0.6B step: per projection the grid barrier and the QACT prologue cost as much as
+        # a launch, and a warp's ring holds under one projection of look-ahead), so it is opt-in.
+        self.chained = bool(chained)
         H, d = shape.hidden, shape.head_dim
         qkv = shape.n_q * d + 2 * shape.n_kv * d
         layer = [("qkv", qkv, H), ("o", H, shape.n_q * d), ("gateup", 2 * shape.ffn, H),
@@ -71,10 +81,16 @@ class DecodeChain:
                 self.x_of.append(prev[:, :K])
         self.graph = None
         self.stream = torch.cuda.Stream()
+        self.table = None
+        if self.chained:
+            if world > 1:
+                raise ValueError("a chained step has no all-gather: world must be 1")
+            self.table = linear.chain_table([(x, w, y, False, False) for x, w, y in
+                                             zip(self.x_of, self.weights, self.outs)])
 
     @property
     def launches(self) -> int:
-        return len(self.plan)
+        return 1 if self.chained else len(self.plan)
 
     def full_out(self, i: int) -> torch.Tensor:
         """Projection i's whole output row [1, N] (the gathered one with world > 1)."""
@@ -82,6 +98,9 @@ class DecodeChain:
 
     def step_eager(self):
         import torch.distributed as dist
+        if self.chained:
+            linear.qlinear_chain(self.table)
+            return
         for x, w, y, g in zip(self.x_of, self.weights, self.outs, self.gathered):
             linear.qlinear(x, w, out=y, pdl=self.pdl)
             if self.world > 1:

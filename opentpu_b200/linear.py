@@ -257,3 +257,33 @@ def qlinear(x: torch.Tensor, w: PackedWeight, *, out=None, acc: bool = False, al
                x2.data_ptr(), x2.stride(0), int(row_mode), M, _ptr(alpha), y.data_ptr(),
                y.stride(0), k_split, int(pdl), _stream())
     return y.reshape(-1) if vec and out is None else y
+
+
+def chain_table(steps) -> "ctypes.Array":
+    """The otq_proj array of a chain: steps is a list of (x [K] or [1, K], w, out [N] or [1, N],
+    acc, row_mode) with MX / int8-row weights. Kept by the caller to call qlinear_chain again."""
+    import ctypes
+    arr = (L.Proj * len(steps))()
+    for i, (x, w, y, acc, row_mode) in enumerate(steps):
+        if w.fmt == "int4-g32":
+            raise ValueError("int4-g32 is not an MM format; it has no chain launch")
+        if x.numel() != w.K or y.numel() != w.N:
+            raise ValueError(f"projection {i}: x has {x.numel()} elements for K = {w.K}, "
+                             f"out {y.numel()} for N = {w.N}")
+        if not (x.is_contiguous() and y.is_contiguous()):
+            raise ValueError(f"projection {i}: x and out must be contiguous")
+        p = arr[i]
+        p.fmt, p.flags = L.FMT[w.mx_fmt], w.flags | (L.MM_ACC if acc else 0)
+        p.rows, p.rs = w.rows.data_ptr(), w.rows.stride(0)
+        p.srows, p.srs = _ptr(w.srows), 0 if w.srows is None else w.srows.stride(0)
+        p.k0, p.N, p.K = w.k0, w.N, w.K
+        p.x, p.row_mode, p.y = x.data_ptr(), int(row_mode), y.data_ptr()
+    return arr
+
+
+def qlinear_chain(table) -> None:
+    """Run a chain table (chain_table) on the current stream: the projections in order, one
+    activation row each, each possibly reading an earlier one's output -- the same results as
+    qlinear called per projection, in one persistent launch per run of one weight format."""
+    import ctypes
+    L.call("otq_qmm_chain", ctypes.addressof(table), len(table), _stream())

@@ -136,8 +136,9 @@ def test_config1_matches_reference(ops, golden):
 
 
 # ---------------------------------------------------------------------------- vs the oracle
-# every work split of the GEMV (0: the pick; 1: 32-row blocks; 2, 4, 8: K split over warps)
-SPLITS = (0, 1, 2, 4, 8)
+# every work decomposition of the GEMV (0: the pick; 32: 32-row blocks; 1: 8-row blocks;
+# 2, 4, 8: 8-row blocks with K split over that many warps)
+SPLITS = (0, 1, 2, 4, 8, 32)
 SHAPES = [(1, 1, 128), (1, 5, 256), (3, 37, 384), (1, 1024, 1024), (8, 513, 1024),
           (2, 300, 3072), (4, 64, 11008), (5, 2048, 2048), (1, 7, 32640)]
 
@@ -236,3 +237,67 @@ def test_g32_linear_within_tolerance(ops, M, N, K):
     got = host(ops.qlinear(dev(x), w)).astype(np.float64)
     assert np.abs(got - want).max() <= G32_TOL * np.abs(want).max()
     assert rel(got, want) < G32_TOL
+
+
+# ---------------------------------------------------------------------------- chains
+def test_chain_matches_oracle(ops):
+    """otq_qmm_chain: projections of several formats in one call (one launch per run of a
+    format), each reading an earlier projection's output, one with ACC, a tall one taking the
+    32-row blocks: bit-exact with the oracle run in the same order."""
+    from opentpu_b200 import _lib
+    rng = np.random.default_rng(5)
+    # (format, N, K, acc); projection i reads the first K outputs of projection i - 1
+    specs = [("int8-row", 640, 256, False), ("int8-row", 40064, 512, False),
+             ("int8", 300, 1024, False), ("int4", 512, 256, False),
+             ("int8-row", 2048, 384, True), ("nvfp4", 130, 128, False), ("fp4", 256, 128, False)]
+    x0 = WL.spread_acts(rng, 1, specs[0][2], 3.0, 8)[0]
+    ws, outs, steps, host_w = [], [], [], []
+    prev = torch.tensor(x0, device="cuda")
+    olds = []
+    for i, (fmt, N, K, acc) in enumerate(specs):
+        W = WL.spread_rows(rng, N, K, 2.0, 32)
+        w = ops.PackedWeight.from_float(dev(W), fmt)
+        y = torch.tensor(rng.standard_normal(N).astype(np.float32), device="cuda")
+        olds.append(host(y).copy())
+        x = prev[:K]
+        steps.append((x, w, y, acc, False))
+        ws.append(w)
+        outs.append(y)
+        host_w.append((host(w.rows), host(w.srows), fmt))
+        prev = y
+    table = ops.chain_table(steps)
+    ops.qlinear_chain(table)
+    torch.cuda.synchronize()
+    assert _lib.status_word() == 0
+    xin = x0
+    for (fmt, N, K, acc), (rows, srows, f), y, old in zip(specs, host_w, outs, olds):
+        mfmt = "int8" if f == "int8-row" else f
+        want = X.qlinear(xin[None, :K], rows, srows, mfmt, rsc=f == "int8-row")[0]
+        if acc:
+            want = F.fadd(old, want)
+        got = host(y)
+        assert np.array_equal(bits(got), bits(want)), (fmt, N, K)
+        xin = got
+    # the same table again gives the same bits (the grid barrier re-arms itself)
+    before = [host(y).copy() for y in outs]
+    for (x, w, y, acc, rm), old in zip(steps, olds):
+        y.copy_(torch.tensor(old, device="cuda"))
+    ops.qlinear_chain(table)
+    torch.cuda.synchronize()
+    assert all(np.array_equal(bits(host(y)), bits(b)) for y, b in zip(outs, before))
+
+
+def test_decode_chain_chained_equals_launch_per_projection():
+    from opentpu_b200.decode import DecodeChain
+    a = DecodeChain(WL.TINY, chained=True)
+    b = DecodeChain(WL.TINY, chained=False)
+    assert a.launches == 1 and b.launches == len(b.plan)
+    a.step_eager()
+    b.step_eager()
+    torch.cuda.synchronize()
+    for ya, yb in zip(a.outs, b.outs):
+        assert np.array_equal(bits(host(ya)), bits(host(yb)))
+    a.capture()
+    a.replay(3)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(host(a.logits())), bits(host(b.logits())))
