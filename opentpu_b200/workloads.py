@@ -62,3 +62,49 @@ PHI4_MINI = DecoderShape("Phi-4-mini", hidden=3072, layers=32, n_q=24, n_kv=8, h
 # the reference's tiny test model (tests/test_qwen3.py:22-35): hidden 256, 2 layers, vocab 1000
 TINY = DecoderShape("tiny-qwen3", hidden=256, layers=2, n_q=4, n_kv=2, head_dim=128, ffn=512,
                     vocab=1000)
+
+
+def decoder_weights(shape: DecoderShape, seed: int = 0) -> dict:
+    """Random-init float32 weights of a Qwen3-shaped decoder (the configurations' N(0, 0.02)
+    projections and embedding, norm gains 1 as a fresh HF model has them), named as the
+    reference's checkpoints are (qwen3.reference_logits): model.embed_tokens.weight (tied to the
+    LM head, as Qwen3-0.6B is), model.layers.{i}.self_attn.{q,k,v,o}_proj.weight,
+    ...q_norm / k_norm, mlp.{gate,up,down}_proj.weight, input / post_attention layernorms,
+    model.norm.weight."""
+    rng = np.random.default_rng(seed)
+    H, d = shape.hidden, shape.head_dim
+
+    def w(N, K):
+        return rng.normal(0.0, 0.02, (N, K)).astype(np.float32)
+
+    W = {"model.embed_tokens.weight": w(shape.vocab, H),
+         "model.norm.weight": np.ones(H, np.float32)}
+    for i in range(shape.layers):
+        p = f"model.layers.{i}."
+        W[p + "input_layernorm.weight"] = np.ones(H, np.float32)
+        W[p + "post_attention_layernorm.weight"] = np.ones(H, np.float32)
+        W[p + "self_attn.q_proj.weight"] = w(shape.n_q * d, H)
+        W[p + "self_attn.k_proj.weight"] = w(shape.n_kv * d, H)
+        W[p + "self_attn.v_proj.weight"] = w(shape.n_kv * d, H)
+        W[p + "self_attn.o_proj.weight"] = w(H, shape.n_q * d)
+        if shape.qk_norm:
+            W[p + "self_attn.q_norm.weight"] = np.ones(d, np.float32)
+            W[p + "self_attn.k_norm.weight"] = np.ones(d, np.float32)
+        W[p + "mlp.gate_proj.weight"] = w(shape.ffn, H)
+        W[p + "mlp.up_proj.weight"] = w(shape.ffn, H)
+        W[p + "mlp.down_proj.weight"] = w(H, shape.ffn)
+    return W
+
+
+def rope_tables(shape: DecoderShape, pos: int):
+    """cos, sin [head_dim / 2] float32 of one position, rotate-half convention, computed in
+    float64 (reference opentpu/llm/qwen3.py:335-346 rope_tables, without LongRoPE factors)."""
+    half = shape.head_dim // 2
+    inv = 1.0 / (shape.theta ** (np.arange(half, dtype=np.float64) * 2 / shape.head_dim))
+    ang = pos * inv
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def prompt_ids(shape: DecoderShape, n: int, seed: int = 0) -> list:
+    """A random prompt: n token ids uniform in [0, vocab) (the configurations' random prompt)."""
+    return [int(t) for t in np.random.default_rng(seed).integers(0, shape.vocab, n)]

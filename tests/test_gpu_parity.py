@@ -301,3 +301,59 @@ def test_decode_chain_chained_equals_launch_per_projection():
     a.replay(3)
     torch.cuda.synchronize()
     assert np.array_equal(bits(host(a.logits())), bits(host(b.logits())))
+
+
+# ---------------------------------------------------------------------------- token level
+def _near_tie_check(dev_logits, ref_logits, tokens):
+    """The reference's rule for a greedy run against a golden, teacher forced on the device's
+    tokens (tests/test_validate.py:124-164 _top1_where_clear): at every step whose golden top-1
+    leads its runner-up by more than the noise (here: 8x the largest |device - golden| logit
+    difference of the run, itself bounded by the cosine check), the device's token is the
+    golden's first maximal logit. Returns the number of steps that were clear."""
+    diff = np.abs(dev_logits - ref_logits).max()
+    cos = [float(np.dot(a, b) / np.linalg.norm(a) / np.linalg.norm(b))
+           for a, b in zip(dev_logits, ref_logits)]
+    assert min(cos) > 0.99999, min(cos)
+    top2 = np.sort(ref_logits, -1)[:, -2:]
+    clear = top2[:, 1] - top2[:, 0] > 8 * diff
+    assert (np.array(tokens)[clear] == ref_logits.argmax(-1)[clear]).all()
+    return int(clear.sum())
+
+
+@pytest.mark.parametrize("fmt,head_fmt", [("int8-row", "int8-row"), ("int4-g32", "int8-row"),
+                                          ("int4", "int8-row")])
+def test_tiny_decode_tokens_match_oracle(fmt, head_fmt):
+    """Greedy decode of the tiny Qwen3 shape (the reference's test model geometry) through the
+    quantized linear layer: every clear step's token is the oracle's (the same model on the CPU
+    with the reference's quantized arithmetic); the logits agree to cos > 0.99999."""
+    from oracle.model import Qwen3Oracle
+    from opentpu_b200.model import Qwen3Decoder
+    shape = WL.TINY
+    W = WL.decoder_weights(shape, seed=1)
+    prompt = WL.prompt_ids(shape, 24, seed=2)
+    dec = Qwen3Decoder(shape, W, fmt=fmt, head_fmt=head_fmt, max_pos=64)
+    tokens, dev = dec.generate(prompt, 12)
+    ora = Qwen3Oracle(shape, W, fmt=fmt, head_fmt=head_fmt, rope=lambda p: WL.rope_tables(shape, p))
+    ref = ora.forced(prompt, tokens)
+    assert _near_tie_check(dev, ref, tokens) >= 10
+
+
+@pytest.mark.slow
+def test_qwen3_0_6b_4bit_decode_tokens_match_oracle():
+    """The seeded Qwen3-0.6B shape with 4-bit group-32 fp16-scale layers and the int8 per-row
+    LM head (configuration 3's formats), a random prompt then greedy tokens: every clear step's
+    token is the oracle's. (Prompt and generation shortened from 512 + 64 to keep the CPU
+    oracle to about a minute; the arithmetic per step is the configuration's.)"""
+    from oracle.model import Qwen3Oracle
+    from opentpu_b200.model import Qwen3Decoder
+    shape = WL.QWEN3_0_6B
+    W = WL.decoder_weights(shape, seed=0)
+    prompt = WL.prompt_ids(shape, 32, seed=0)
+    dec = Qwen3Decoder(shape, W, fmt="int4-g32", head_fmt="int8-row", max_pos=64)
+    tokens, dev = dec.generate(prompt, 16)
+    del dec
+    torch.cuda.empty_cache()
+    ora = Qwen3Oracle(shape, W, fmt="int4-g32", head_fmt="int8-row",
+                      rope=lambda p: WL.rope_tables(shape, p))
+    ref = ora.forced(prompt, tokens)
+    assert _near_tie_check(dev, ref, tokens) >= 12
