@@ -162,6 +162,41 @@ OTQ_API int otq_qmm_chain(const otq_proj* projs, int count, void* stream);
  * such failure). */
 OTQ_API int otq_status_word(int* value, int reset);
 
+/* ------------------------------------------------------------------ prefill GEMM */
+
+/* One projection of otq_gemm_w8a16_group. */
+typedef struct otq_gemm_proj {
+  int flags;             /* OTQ_MM_RSC (Sw = the first fp32 word of each scale row) or
+                            OTQ_MM_UNIT (Sw = 1), either one | OTQ_MM_ACC */
+  const uint8_t* rows;   /* int8 weight rows [N][rs] (16-byte aligned, rs a multiple of 16) */
+  int64_t rs;
+  const uint8_t* srows;  /* scale rows [N][srs] (4-byte aligned), or NULL with OTQ_MM_UNIT */
+  int64_t srs;
+  int64_t N;
+  int64_t K;
+  const uint16_t* x;     /* bf16 activations [M][ldx] (16-byte aligned, ldx a multiple of 8) */
+  int64_t ldx;
+  int64_t M;
+  float* y;              /* fp32 output [M][ldy] (4-byte aligned) */
+  int64_t ldy;
+} otq_gemm_proj;
+
+/* The int8 weight-only linear layer on bf16 activations, as a tensor-core GEMM (prefill):
+ * y [M, N] = x [M, K] @ (q * Sw)^T, q the int8-row bytes of otq_pack_int8(rsc = 1) --
+ * quant.quantize(W, "int8", g=K) (opentpu/quant.py:218-224) used as `deq @ x`
+ * (opentpu/reference.py:14-17). int8 and bf16 are exact in the products; sums are fp32 in
+ * tensor-core order, so results agree with a float64 evaluation to a relative tolerance
+ * (not bit-exact; otq_qmm is the bit-exact MM). ACC: y += . K % 8 == 0. The reference's own
+ * prefill quantizes activations first (QACT); a bf16 path has no single counterpart there. */
+OTQ_API int otq_gemm_w8a16(int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+                           int64_t srs, int64_t N, int64_t K, const uint16_t* x, int64_t ldx,
+                           int64_t M, float* y, int64_t ldy, void* stream);
+
+/* Up to 8 independent projections of otq_gemm_w8a16 in one launch (their tiles share the
+ * GPU's SMs: a layer's projections at prefill). The outputs must not overlap the inputs or
+ * each other. No counterpart in the reference (its projections are separate programs). */
+OTQ_API int otq_gemm_w8a16_group(const otq_gemm_proj* projs, int count, void* stream);
+
 /* ------------------------------------------------------------------ 4-bit group-32 fp16 */
 
 /* quant.quantize(W, "int4", g=32, scale="fp16") (opentpu/quant.py:225-227 -> quant_block

@@ -23,6 +23,13 @@ class Proj(ctypes.Structure):
                 ("K", c_int64), ("x", c_void_p), ("row_mode", c_int), ("y", c_void_p)]
 
 
+class GemmProj(ctypes.Structure):
+    """struct otq_gemm_proj of include/otq.h: one projection of otq_gemm_w8a16_group."""
+    _fields_ = [("flags", c_int), ("rows", c_void_p), ("rs", c_int64), ("srows", c_void_p),
+                ("srs", c_int64), ("N", c_int64), ("K", c_int64), ("x", c_void_p),
+                ("ldx", c_int64), ("M", c_int64), ("y", c_void_p), ("ldy", c_int64)]
+
+
 # name -> (restype, argtypes); every pointer is passed as an integer address
 _P, _I, _L = c_void_p, c_int, c_int64
 SIGNATURES = {
@@ -38,6 +45,8 @@ SIGNATURES = {
     "otq_qmm_ex": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _L, _P, _P, _L, _I, _I,
                         _P]),
     "otq_qmm_chain": (_I, [_P, _I, _P]),
+    "otq_gemm_w8a16": (_I, [_I, _P, _L, _P, _L, _L, _L, _P, _L, _L, _P, _L, _P]),
+    "otq_gemm_w8a16_group": (_I, [_P, _I, _P]),
     "otq_status_word": (_I, [_P, _I]),
     "otq_pack_g32": (_I, [_P, _L, _L, _L, _P, _P, _P]),
     "otq_linear_g32": (_I, [_P, _P, _L, _L, _P, _L, _L, _I, _P, _L, _P]),

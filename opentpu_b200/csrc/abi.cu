@@ -311,6 +311,39 @@ int otq_qmm_chain(const otq_proj* projs, int count, void* stream) {
   return finish(chain_launch(projs, count, static_cast<cudaStream_t>(stream)));
 }
 
+int otq_gemm_w8a16_group(const otq_gemm_proj* projs, int count, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (projs == nullptr || count < 0 || count > kW8A16MaxGroup) return kErrArg;
+  W8A16Proj w[kW8A16MaxGroup];
+  for (int i = 0; i < count; ++i) {
+    const otq_gemm_proj& p = projs[i];
+    if (p.flags & ~(kMmUnit | kMmRsc | kMmAcc)) return kErrArg;
+    if (!(p.flags & (kMmUnit | kMmRsc))) return kErrFormat;   // int8x block offsets: otq_qmm
+    if (p.N <= 0 || p.K <= 0 || p.M <= 0 || p.K % 8 || p.K > 0x7FFFFFFF || p.N > 0x7FFFFFFF ||
+        p.M > 0x7FFFFFFF)
+      return kErrArg;
+    if (p.rows == nullptr || p.x == nullptr || p.y == nullptr) return kErrArg;
+    if (!(p.flags & kMmUnit) && p.srows == nullptr) return kErrArg;
+    if (p.rs < p.K || p.ldx < p.K || p.ldy < p.N || p.rs >= kStrideLimit ||
+        p.ldx >= kStrideLimit || p.ldy >= kStrideLimit)
+      return kErrArg;
+    if (!aligned(p.rows, 16) || p.rs % 16 || !aligned(p.x, 16) || p.ldx % 8 || !aligned(p.y, 4))
+      return kErrAlign;
+    if (!(p.flags & kMmUnit) && (!aligned(p.srows, 4) || p.srs % 4 || p.srs < 4)) return kErrAlign;
+    w[i] = W8A16Proj{p.flags, p.rows, p.rs, p.srows, p.srs, p.N, p.K, p.x, p.ldx, p.M, p.y, p.ldy};
+  }
+  if (count == 0) return kOk;
+  return finish(w8a16_launch(w, count, static_cast<cudaStream_t>(stream)));
+}
+
+int otq_gemm_w8a16(int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+                   int64_t srs, int64_t N, int64_t K, const uint16_t* x, int64_t ldx, int64_t M,
+                   float* y, int64_t ldy, void* stream) {
+  const otq_gemm_proj p{flags, rows, rs, srows, srs, N, K, x, ldx, M, y, ldy};
+  return otq_gemm_w8a16_group(&p, 1, stream);
+}
+
 int otq_status_word(int* value, int reset) {
   int st = device_ok();
   if (st) return st;

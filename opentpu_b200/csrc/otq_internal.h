@@ -58,7 +58,25 @@ struct MMParams {
   int* status;   // device status word (may be null): kStatusTimeout bits
 };
 
+// One projection of the prefill GEMM (prefill.cu), checked by the caller: x bf16 [M, K] (ldx
+// elements, 16-byte aligned rows), rows int8 [N, K] (rs bytes), Sw the first fp32 word of each
+// scale row (srs bytes; srows unused with OTQ_MM_UNIT), y fp32 [M, N] (ldy floats).
+struct W8A16Proj {
+  int flags;
+  const uint8_t* rows;
+  int64_t rs;
+  const uint8_t* srows;
+  int64_t srs;
+  int64_t N, K;
+  const uint16_t* x;
+  int64_t ldx, M;
+  float* y;
+  int64_t ldy;
+};
+constexpr int kW8A16MaxGroup = 8;
+
 int sm_count(int dev);
+int w8a16_launch(const W8A16Proj* projs, int count, cudaStream_t stream);   // prefill.cu
 int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);    // gemv.cu
 int chain_launch(const otq_proj* projs, int count, cudaStream_t stream);
 int chain_reset();   // the grid barrier's count back to zero

@@ -259,6 +259,51 @@ def qlinear(x: torch.Tensor, w: PackedWeight, *, out=None, acc: bool = False, al
     return y.reshape(-1) if vec and out is None else y
 
 
+def _gemm_proj(x: torch.Tensor, w: PackedWeight, y: torch.Tensor | None, acc: bool):
+    """Checked operands of one prefill GEMM projection: (GemmProj, y)."""
+    if w.fmt != "int8-row" and not (w.fmt == "int8" and w.srows is None):
+        raise ValueError("the prefill GEMM takes int8-row weights (or UNIT int8)")
+    _cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.ndim != 2 or x.shape[1] != w.K:
+        raise ValueError(f"x must be bfloat16 [M, {w.K}]")
+    if x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    M = x.shape[0]
+    y = _out(y, M, w.N, x.device, acc)
+    p = L.GemmProj()
+    p.flags = w.flags | (L.MM_ACC if acc else 0)
+    p.rows, p.rs = w.rows.data_ptr(), w.rows.stride(0)
+    p.srows, p.srs = _ptr(w.srows), 0 if w.srows is None else w.srows.stride(0)
+    p.N, p.K, p.x, p.ldx, p.M = w.N, w.K, x.data_ptr(), x.stride(0), M
+    p.y, p.ldy = y.data_ptr(), y.stride(0)
+    return p, y, x
+
+
+def gemm_w8a16(x: torch.Tensor, w: PackedWeight, *, out=None, acc: bool = False) -> torch.Tensor:
+    """Prefill linear layer: y [M, N] fp32 = x [M, K] bf16 @ (q * Sw)^T on the tensor cores
+    (tcgen05), w an int8-row weight -- the reference's `deq @ x` with bf16 activations
+    (opentpu/reference.py:14-17 on quant.quantize(W, "int8", g=K), quant.py:218-224). fp32
+    accumulation: within a relative tolerance of float64, not bit-exact. acc: y = out + ."""
+    p, y, x = _gemm_proj(x, w, out, acc)
+    L.call("otq_gemm_w8a16", p.flags, p.rows, p.rs, p.srows, p.srs, p.N, p.K, p.x, p.ldx, p.M,
+           p.y, p.ldy, _stream())
+    return y
+
+
+def gemm_w8a16_group(items) -> list:
+    """Several independent prefill projections in one launch: items is a list of (x, w, out,
+    acc) as gemm_w8a16 takes them (at most 8). Returns the outputs in order."""
+    import ctypes
+    arr = (L.GemmProj * len(items))()
+    outs, keep = [], []
+    for i, (x, w, out, acc) in enumerate(items):
+        arr[i], y, xx = _gemm_proj(x, w, out, acc)
+        outs.append(y)
+        keep.append(xx)
+    L.call("otq_gemm_w8a16_group", ctypes.addressof(arr), len(items), _stream())
+    return outs
+
+
 def chain_table(steps) -> "ctypes.Array":
     """The otq_proj array of a chain: steps is a list of (x [K] or [1, K], w, out [N] or [1, N],
     acc, row_mode) with MX / int8-row weights. Kept by the caller to call qlinear_chain again."""

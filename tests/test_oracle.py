@@ -129,3 +129,21 @@ def test_emulation_matches_exact_mm(golden):
                            X.weight_offsets(srows, fmt, W.shape[1]), X.WINDOW[fmt])
         got = golden[f"dot_{fmt}_y"].view(np.float32)
         assert np.abs(got - want).max() < 1e-6 * np.abs(want).max(), fmt
+
+
+def test_prefill_oracle_bf16_and_deq(golden):
+    """oracle/prefill: bf16 rounding (ties to even) as torch rounds, and q * Sw as the MX
+    dequantizer gives it for RSC rows."""
+    import torch
+    from oracle import prefill as PF
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.normal(size=4096).astype(np.float32),
+                        np.array([1.00390625, 1.01171875, -3.0078125, 0.0, -0.0], np.float32)])
+    want = torch.from_numpy(x).to(torch.bfloat16).to(torch.float32).numpy()
+    assert np.array_equal(bits(PF.bf16_round(x)), bits(want))
+    rows, srows = golden["fmt_rsc_q"].view(np.uint8), golden["fmt_rsc_s"]
+    K = rows.shape[1]
+    d = PF.deq_rows(rows, srows, K)
+    assert np.array_equal(d, X.dequantize(rows, srows, "int8", K, rsc=True))
+    y, bound = PF.gemm_w8a16(want[:K][None], rows, srows, K)
+    assert y.shape == (1, rows.shape[0]) and np.all(bound >= np.abs(y))
