@@ -8,8 +8,13 @@ launch's output as a decode step does (opentpu_b200.decode.DecodeChain, dependen
 one CUDA graph. The weights (598 MB) exceed the 126 MB L2, so each step streams them from
 HBM.
 
---profile head|step runs a few launches and exits (the command the ncu summaries under
+--profile head|step|prefill runs a few launches and exits (the command the ncu summaries under
 profiles/ were captured with).
+
+The line's "prefill" object is BASELINE configuration 4 (prefill TFLOP/s): 36 SmolLM3-3B-shaped
+layers of int8-row weights (2.8 GB) against 512 bf16 tokens, one grouped tcgen05 GEMM launch
+(opentpu_b200.linear.gemm_w8a16_group) a layer, the 36 launches one CUDA graph a step; its
+roofline is against the measured bf16 tensor peak.
 
 metric: decode weight GB/s (whole job) with tok/s = steps / s beside it. With --gpus N each
 projection's output rows are split over the N ranks (the reference's Weight(shard=0)) and an
@@ -50,7 +55,8 @@ def peaks():
 
 
 def profile_run(what: str):
-    """A few launches for an ncu capture: the LM head GEMV alone, or two decode steps."""
+    """A few launches for an ncu capture: the LM head GEMV alone, two decode steps, or three
+    grouped prefill launches of one SmolLM3-3B layer."""
     import torch
     from opentpu_b200 import linear
     from opentpu_b200.decode import DecodeChain
@@ -64,12 +70,150 @@ def profile_run(what: str):
         y = torch.empty((1, shape.vocab), device="cuda")
         for _ in range(5):
             linear.qlinear(x, w, out=y)
+    elif what == "prefill":
+        items = prefill_layer(WL.SMOLLM3_3B, 1, 0, torch.Generator(device="cuda").manual_seed(0))
+        for _ in range(3):
+            linear.gemm_w8a16_group(items)
     else:
         chain = DecodeChain(shape)
         chain.capture()
         chain.replay(2)
         chain.release()
     torch.cuda.synchronize()
+
+
+PREFILL_TOKENS = 512
+
+
+def prefill_layer(shape, world, rank, gen, xs=None):
+    """One layer's seven projections for the prefill GEMM: int8-row
+    weights (uniform int8 rows, Sw ~ 1e-3: the GEMM's cost does not depend on the values) for
+    this rank's row shard, bf16 activations N(0, 1) [512, K] (shared across layers when xs is
+    given) and fp32 outputs. Returns gemm_w8a16_group items."""
+    import torch
+    from opentpu_b200 import linear
+    items = []
+    for i, (_, N, K) in enumerate(shape.projections()):
+        n = N // world
+        rows = torch.randint(-127, 128, (n, K), dtype=torch.int8, device="cuda",
+                             generator=gen).view(torch.uint8)
+        sw = (torch.rand(n, device="cuda", generator=gen) * 1e-3 + 1e-4)
+        w = linear.PackedWeight("int8-row", n, K, rows, sw.view(torch.uint8).reshape(n, 4))
+        x = xs[i] if xs is not None else torch.randn((PREFILL_TOKENS, K), device="cuda",
+                                                      generator=gen).to(torch.bfloat16)
+        y = torch.empty((PREFILL_TOKENS, n), device="cuda")
+        items.append((x, w, y, False))
+    return items
+
+
+def prefill_cpu_sample(budget_s: float = 6.0):
+    """The oracle's float64 `deq @ x` (oracle/prefill.py) on host cores over one 2048 x 2048
+    projection at 512 tokens: (TFLOP/s, description, threads)."""
+    from oracle import prefill as PF
+    rng = np.random.default_rng(0)
+    K = N = 2048
+    x = PF.bf16_round(rng.standard_normal((PREFILL_TOKENS, K)).astype(np.float32))
+    rows = rng.integers(-127, 128, (N, K), dtype=np.int8).view(np.uint8)
+    srows = (rng.random(N).astype(np.float32) * 1e-3).view(np.uint8).reshape(N, 4)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        PF.gemm_w8a16(x, rows, srows, K)
+        done += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or done >= 20:
+            break
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:
+        threads = 1
+    flops = 2.0 * PREFILL_TOKENS * N * K
+    desc = (f"{done} x one 2048x2048 projection at 512 tokens, float64 numpy (oracle, also "
+            "forms the error bound |x| @ |deq|^T)")
+    return done * flops / el / 1e12, desc, threads
+
+
+def prefill_bench(world, rank, local, steps, warmup, cpu_baseline: bool):
+    """BASELINE configuration 4 on this rank: 36 SmolLM3-3B layers, each one grouped launch of
+    its seven projections (row shard 1/world of each), captured in one CUDA graph a step.
+    Returns the prefill part of the bench line (rank 0) after a max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from opentpu_b200 import linear
+    shape = WL.SMOLLM3_3B
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    first = prefill_layer(shape, world, rank, gen)
+    xs = [it[0] for it in first]
+    layers = [first] + [prefill_layer(shape, world, rank, gen, xs) for _ in range(shape.layers - 1)]
+    flops_layer = sum(2.0 * PREFILL_TOKENS * it[1].N * it[1].K for it in first)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for items in layers[:2]:
+            linear.gemm_w8a16_group(items)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for items in layers:
+            linear.gemm_w8a16_group(items)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del g
+    total_flops = flops_layer * world * shape.layers
+    tflops = total_flops / (ms * 1e-3) / 1e12
+    launch_us = ms * 1e3 / shape.layers
+    achieved = flops_layer / (launch_us * 1e-6) / 1e12
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak, peak_kind = float(json.loads(pk.read_text())["bf16_tflops"]), "measured (burst)"
+    else:
+        peak, peak_kind = 1590.0, "fallback"
+    traffic = None
+    tp = ROOT / "profiles" / "w8a16_kernel_smollm3_layer_m512.md"
+    if tp.exists() and world == 1:
+        for line in tp.read_text().splitlines():
+            if line.startswith("| dram_bytes_per_launch |"):
+                traffic = int(line.split("|")[2])
+    cpu = None
+    if rank == 0 and world == 1 and cpu_baseline:
+        v, desc, threads = prefill_cpu_sample()
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}
+    return {
+        "metric": "prefill TFLOP/s", "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms,
+        "steps": steps, "warmup": warmup, "scaling": "strong", "dtype": "bf16 x int8 -> fp32",
+        "config": {"workload": "SmolLM3-3B-shaped prefill GEMMs: 36 layers x (q 2048x2048, k/v "
+                               "512x2048, o 2048x2048, gate/up 11008x2048, down 2048x11008) "
+                               "int8 per-row weights, 512 tokens bf16 N(0,1)",
+                   "flops_per_step": total_flops, "launch": "one grouped launch a layer "
+                   "(7 projections), 36 in one CUDA graph",
+                   "parallelism": f"row-shard x{world}",
+                   "l2": "weights 2.8 GB > 126 MB L2 (no flush needed)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "w8a16_kernel (one SmolLM3-3B layer, 7 projections, M=512)",
+                     "flops_per_launch": flops_layer, "us_per_launch": launch_us,
+                     "peak_kind": peak_kind},
+        "cpu_baseline": cpu,
+        "gpu_launches": shape.layers * steps,
+        "clocks": clocks.summary(),
+    }
 
 
 class Clocks:
@@ -184,7 +328,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["head", "step"])
+    ap.add_argument("--profile", choices=["head", "step", "prefill"])
+    ap.add_argument("--no-prefill", action="store_true")
     args = ap.parse_args()
     if args.profile:
         profile_run(args.profile)
@@ -289,6 +434,11 @@ def main():
         v, desc, threads = cpu_sample_seconds()
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
 
+    prefill = None
+    if not args.no_prefill:
+        prefill = prefill_bench(world, rank, local, max(3, min(100, args.steps // 20)),
+                                max(3, min(5, args.warmup)), not args.no_cpu_baseline)
+
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -315,6 +465,7 @@ def main():
                     "ms_per_step": e2e_ms, "api": "DecodeChain.run_host"},
             "gpu_launches": chain.launches * args.steps,
             "clocks": clocks.summary(),
+            "prefill": prefill,
         }), flush=True)
     chain.release()
     del hg
