@@ -34,6 +34,18 @@ from . import linear
 from .workloads import DecoderShape
 
 
+def shard_rows(N: int, world: int, rank: int) -> tuple[int, int]:
+    """Rank `rank`'s contiguous rows [n0, n1) of an N-row projection split over `world` ranks
+    (runtime.Weight(shard=0), runtime.py:138-142: equal contiguous row blocks); an all-gather of
+    the ranks' outputs in rank order is the whole output row."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world}")
+    if N % world:
+        raise ValueError(f"{N} rows do not split over {world} ranks")
+    n = N // world
+    return rank * n, (rank + 1) * n
+
+
 class DecodeChain:
     def __init__(self, shape: DecoderShape, fmt: str = "int8-row", head_fmt: str = "int8-row",
                  seed: int = 0, world: int = 1, rank: int = 0, group=None, pdl: bool = True,
@@ -57,10 +69,12 @@ class DecodeChain:
         self.inputs: dict[int, torch.Tensor] = {}
         self.weight_bytes = 0
         for name, N, K, f in self.plan:
-            if N % world:
-                raise ValueError(f"{name}: {N} rows do not split over {world} ranks")
-            n = N // world
-            W = torch.randn((N, K), generator=gen, device="cuda")[rank * n:(rank + 1) * n] * std
+            try:
+                n0, n1 = shard_rows(N, world, rank)
+            except ValueError as e:
+                raise ValueError(f"{name}: {e}") from None
+            n = n1 - n0
+            W = torch.randn((N, K), generator=gen, device="cuda")[n0:n1] * std
             w = linear.PackedWeight.from_float(W, f)
             del W
             self.weights.append(w)
