@@ -17,8 +17,10 @@ layers of int8-row weights (2.8 GB) against 512 bf16 tokens, one grouped tcgen05
 roofline is against the measured bf16 tensor peak.
 
 metric: decode weight GB/s (whole job) with tok/s = steps / s beside it. With --gpus N each
-projection's output rows are split over the N ranks (the reference's Weight(shard=0)) and an
-NCCL all-gather assembles every projection's output on every rank (the reference's GATHER).
+projection's output rows are split over the N ranks (the reference's Weight(shard=0)) and every
+projection's output is assembled on every rank (the reference's GATHER) inside the GEMV itself:
+each rank stores its rows into every rank's copy over NVLink and the next projection waits on
+per-rank flags (DecodeChain gather="fused").
 
 --impl reference times the reference's CPU algorithm (the numpy port under oracle/, the same
 arithmetic as the reference's MM) on a bounded sample of the same step.
@@ -378,7 +380,8 @@ def main():
     value = total_bytes / (ms * 1e-3) / 1e9
 
     # the dominant kernel alone: the LM head GEMV (this rank's rows), 20 launches in a graph
-    head, hx, hy = chain.weights[-1], chain.inputs[shape.hidden], chain.outs[-1]
+    head, hx = chain.weights[-1], chain.inputs[shape.hidden]
+    hy = torch.empty((1, head.N), device="cuda")
     hg = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -448,8 +451,11 @@ def main():
             "config": {"workload": "Qwen3-0.6B-shaped int8 per-row decode step: 28 layers x "
                                    "(QKV, O, GateUp, Down) + 151936x1024 LM head, M=1",
                        "weights_bytes_per_step": total_bytes, "format": fmt,
-                       "parallelism": f"row-shard x{world}" + (" + NCCL all-gather per "
-                                                              "projection" if world > 1 else ""),
+                       "parallelism": f"row-shard x{world}" + (" + all-gather per projection "
+                                                              "fused into the GEMV (tagged 8-byte "
+                                                              "words stored to every rank over "
+                                                              "NVLink)"
+                                                              if world > 1 else ""),
                        "l2": "weights 598 MB > 126 MB L2 (no flush needed)",
                        "graph": "one CUDA graph per step, PDL launches"},
             "tok_s": 1e3 / ms,

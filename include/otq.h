@@ -129,6 +129,38 @@ OTQ_API int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, cons
                int row_mode, int64_t M, const float* alpha, float* y, int64_t ldy,
                int k_split, int pdl, void* stream);
 
+/* The NVLink fan-out of a row-sharded decode projection (otq_qmm_peer). The ranks' output rows
+ * live in symmetric buffers (one allocation a rank, mapped into every rank's address space);
+ * delta[r] is the byte distance from this rank's buffer to rank r's as mapped here (delta[rank]
+ * = 0). seq, done: two words of this GPU's memory, both zero before this rank's first
+ * otq_qmm_peer launch; the launches keep done at zero between launches and seq equal to the
+ * number of otq_qmm_peer launches this rank has run. */
+typedef struct otq_peer {
+  int rank;
+  int world;             /* 2 .. 8 */
+  int wait;              /* != 0: x is the previous projection's tagged output row */
+  int pad;
+  int64_t delta[8];
+  int* seq;
+  int* done;
+} otq_peer;
+
+/* QACT + MM of one activation row against this rank's rows of a row-sharded projection
+ * (runtime.Weight(shard=0), opentpu/runtime.py:138-142), with the all-gather of the output
+ * (the reference's GATHER, opentpu/isasim.py:1413-1438) fused into the kernel. Output rows are
+ * tagged: element i is one 8-byte word, the fp32 value in the low 4 bytes and a tag in the high
+ * 4, and y is this rank's N words (16-byte aligned) of its symmetric copy of the output row.
+ * Each word is also stored at the same place in every other rank's copy over NVLink, with tag =
+ * seq + 1. With wait != 0, x is such a tagged row (K words, 16-byte aligned) and the kernel
+ * reads each element until its tag reaches seq: every rank's previous output has arrived. With
+ * wait == 0, x is plain fp32. Every rank must run the same sequence of launches. The values are
+ * otq_qmm's bit for bit; a read that waits too long sets the status word (the launch's outputs
+ * are then not valid). No ACC or ASCALE. No counterpart in the reference (its GATHER is a
+ * separate instruction). */
+OTQ_API int otq_qmm_peer(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+                         int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx,
+                         int row_mode, float* y, const otq_peer* peer, int pdl, void* stream);
+
 /* One projection of a chain (otq_qmm_chain): the operands of otq_qmm for one activation row. */
 typedef struct otq_proj {
   int fmt;               /* OTQ_FMT_* */

@@ -23,6 +23,12 @@ class Proj(ctypes.Structure):
                 ("K", c_int64), ("x", c_void_p), ("row_mode", c_int), ("y", c_void_p)]
 
 
+class Peer(ctypes.Structure):
+    """struct otq_peer of include/otq.h: the NVLink fan-out of otq_qmm_peer."""
+    _fields_ = [("rank", c_int), ("world", c_int), ("wait", c_int), ("pad", c_int),
+                ("delta", c_int64 * 8), ("seq", c_void_p), ("done", c_void_p)]
+
+
 class GemmProj(ctypes.Structure):
     """struct otq_gemm_proj of include/otq.h: one projection of otq_gemm_w8a16_group."""
     _fields_ = [("flags", c_int), ("rows", c_void_p), ("rs", c_int64), ("srows", c_void_p),
@@ -45,6 +51,7 @@ SIGNATURES = {
     "otq_qmm_ex": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _L, _P, _P, _L, _I, _I,
                         _P]),
     "otq_qmm_chain": (_I, [_P, _I, _P]),
+    "otq_qmm_peer": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _P, _P, _I, _P]),
     "otq_gemm_w8a16": (_I, [_I, _P, _L, _P, _L, _L, _L, _P, _L, _L, _P, _L, _P]),
     "otq_gemm_w8a16_group": (_I, [_P, _I, _P]),
     "otq_status_word": (_I, [_P, _I]),

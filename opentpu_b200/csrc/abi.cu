@@ -289,6 +289,42 @@ int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_
   return finish(mm_launch(p, static_cast<cudaStream_t>(stream), pdl != 0));
 }
 
+int otq_qmm_peer(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+                 int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx,
+                 int row_mode, float* y, const otq_peer* peer, int pdl, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if ((st = check_weights(fmt, flags, rows, rs, srows, srs, k0, N, K))) return st;
+  if ((st = check_out(1, N, y, N, flags, nullptr))) return st;
+  if (flags & (kMmAscale | kMmAcc)) return kErrArg;
+  if (x == nullptr || ldx < K || ldx >= kStrideLimit) return kErrArg;
+  if (peer == nullptr || peer->world < 2 || peer->world > 8 || peer->rank < 0 ||
+      peer->rank >= peer->world || peer->seq == nullptr || peer->done == nullptr)
+    return kErrArg;
+  if (!aligned(y, 16) || !aligned(x, peer->wait ? 16 : 4)) return kErrAlign;
+  if (!aligned(peer->seq, 4) || !aligned(peer->done, 4)) return kErrAlign;
+  for (int r = 0; r < peer->world; ++r)
+    if (peer->delta[r] % 16) return kErrAlign;
+  MMParams p{};
+  p.fmt = fmt;
+  p.flags = flags;
+  p.rows = rows;
+  p.rs = rs;
+  p.srows = srows;
+  p.srs = srs;
+  p.k0 = k0;
+  p.N = N;
+  p.K = static_cast<int>(K);
+  p.x = x;
+  p.ldx = ldx;
+  p.row_mode = row_mode ? 1 : 0;
+  p.M = 1;
+  p.y = y;
+  p.ldy = N;
+  p.peer = peer;
+  return finish(mm_launch(p, static_cast<cudaStream_t>(stream), pdl != 0));
+}
+
 int otq_qmm(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
             int64_t srs, int k0, int64_t N, int64_t K, const float* x, int64_t ldx, int row_mode,
             int64_t M, const float* alpha, float* y, int64_t ldy, void* stream) {

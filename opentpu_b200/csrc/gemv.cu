@@ -159,12 +159,52 @@ __device__ __forceinline__ PArgs load_args(const Proj& d) {
 
 // The projections of one launch, run in order; from the second on, each starts after a grid
 // barrier (its x may be an earlier projection's y).
+// A row-sharded projection's output fan-out over NVLink (world > 0, single-projection launches).
+// Output rows are tagged: element i is one 8-byte word, the fp32 value in the low half and a tag
+// in the high half, stored single-copy atomically. The rank that owns a row stores its word into
+// every rank's copy of the output row (symmetric buffers, delta[r] bytes from this rank's) with
+// tag = this rank's projection count + 1; a launch whose x is such a row (wait != 0) reads each
+// element until its tag has reached this rank's count, so it starts on every rank's previous
+// output without a fence or a flag. The launch's last CTA advances the count (device scope).
+constexpr int kMaxPeers = 8;
+struct PeerArgs {
+  int rank, world, wait, pad;
+  int64_t delta[kMaxPeers];
+  int* seq;     // projections this rank has completed (this GPU's memory)
+  int* done;    // CTAs of the current launch that have finished (zero between launches)
+};
+
 template <int MAXP>
 struct Chain {
   Proj proj[MAXP];
   int count;
   int* status;
+  PeerArgs peer;
 };
+
+struct Fan {
+  int world, rank;
+  uint32_t tag;            // 0: plain fp32 output; else the tag of this launch's output words
+  const int64_t* delta;    // shared-memory copy of PeerArgs::delta
+};
+
+__device__ __forceinline__ void st_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Output element idx of y: a plain store, or the tagged word here and on every other rank.
+__device__ __forceinline__ void put_out(float* y, int64_t idx, float v, const Fan& fan) {
+  if (fan.tag == 0) {
+    y[idx] = v;
+    return;
+  }
+  const unsigned long long w = __float_as_uint(v) | (static_cast<unsigned long long>(fan.tag) << 32);
+  unsigned long long* p = reinterpret_cast<unsigned long long*>(y) + idx;
+  st_sys_u64(p, w);
+  for (int r = 0; r < fan.world; ++r)
+    if (r != fan.rank)
+      st_sys_u64(reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(p) + fan.delta[r]), w);
+}
 
 // A warp's share of one projection: rows [rb, re) in NBLK blocks of R, chunks [c0, c0 + NSL)
 // of each (NIT items a block, the same in every warp of the CTA).
@@ -261,7 +301,7 @@ __device__ __forceinline__ void put_group(const GSmem& s, int j, int G, int da) 
 // K, and rows mt..MT-1, are zeros. With `frag`, the class path's A fragments as well.
 template <int FMT, int MT, bool PLAIN>
 __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSmem& s, int mt, int kp, int ap,
-                                      bool frag) {
+                                      bool frag, int expect = -1, int* status = nullptr) {
   const int K = p.K, KG = K / 32;
   if (threadIdx.x == 0) *s.flag = 0;
   for (int j = 0; j < MT; ++j) {
@@ -310,7 +350,8 @@ __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSme
                 *reinterpret_cast<uint32_t*>(fb + (cg + (e >> 3)) * 16 + ((e & 7) >= 4 ? 8 : 0) + ch) = packed;
               }
             }
-          });
+          },
+          expect >= 0 ? reinterpret_cast<const unsigned long long*>(xr) : nullptr, expect, status);
       if (threadIdx.x == 0) s.Sa[j] = r.S;
     }
   } else {
@@ -606,7 +647,7 @@ template <int FMT, int MT, bool PLAIN, int NS, int MAXP, int R, int S>
 __device__ __forceinline__ void run_proj(const PArgs& d, const Geo& q, const GSmem& s,
                                          RingIssue<FMT, PLAIN, NS, MAXP>& iss, int& f, bool& ok,
                                          int* status, const GLayout& L, uint8_t* ring,
-                                         uint8_t* sring, int mt) {
+                                         uint8_t* sring, int mt, const Fan& fan) {
   using F = GF<FMT>;
   constexpr int NO = R / 8;     // row octets (tensor-copy boxes) of a block
   constexpr int VPL = 2 * NO;   // general-path values a lane
@@ -738,13 +779,12 @@ __device__ __forceinline__ void run_proj(const PArgs& d, const Geo& q, const GSm
         const int64_t row = r0 + rr;
         const float Sw = unit ? 1.0f : __ldg(reinterpret_cast<const float*>(d.srows + row * d.srs));
         float yv = mm_epilogue(tot, Sw, s.Sa[0], W);
-        float* yp = d.y + row;
         if (d.flags & kMmAscale) {
-          yv = fadd(fmul(*yp, __ldg(d.alpha)), yv);
+          yv = fadd(fmul(d.y[row], __ldg(d.alpha)), yv);
         } else if (d.flags & kMmAcc) {
-          yv = fadd(*yp, yv);
+          yv = fadd(d.y[row], yv);
         }
-        *yp = yv;
+        put_out(d.y, row, yv, fan);
       }
       if constexpr (S > 1) __syncthreads();   // red is reused by the next row block
     } else {
@@ -771,13 +811,13 @@ __device__ __forceinline__ void run_proj(const PArgs& d, const Geo& q, const GSm
               const int64_t row = r0 + rr;
               const float Sw = unit ? 1.0f : __ldg(reinterpret_cast<const float*>(d.srows + row * d.srs));
               float yv = mm_epilogue(acc[o][h], Sw, s.Sa[g], F::kW);
-              float* yp = d.y + static_cast<int64_t>(g) * d.ldy + row;
+              const int64_t idx = static_cast<int64_t>(g) * d.ldy + row;
               if (d.flags & kMmAscale) {
-                yv = fadd(fmul(*yp, __ldg(d.alpha + g)), yv);
+                yv = fadd(fmul(d.y[idx], __ldg(d.alpha + g)), yv);
               } else if (d.flags & kMmAcc) {
-                yv = fadd(*yp, yv);
+                yv = fadd(d.y[idx], yv);
               }
-              *yp = yv;
+              put_out(d.y, idx, yv, fan);
             }
           }
       }
@@ -833,11 +873,28 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
   for (int q = 0; q < NS - 1; ++q) iss.next();
   pdl_wait();   // the activations may come from the kernel launched before
 
+  // output fan-out (single-projection launches of a row-sharded step): this rank's count of
+  // completed projections tags this launch's outputs and is the tag its tagged input must reach
+  __shared__ int64_t peer_delta[kMaxPeers];
+  __shared__ int peer_count;
+  Fan fan{0, 0, 0u, peer_delta};
+  int expect = -1;   // >= 0: x is a tagged row
+  if (MAXP == 1 && C.peer.world > 0) {
+    if (threadIdx.x < kMaxPeers) peer_delta[threadIdx.x] = C.peer.delta[threadIdx.x];
+    if (threadIdx.x == 0) peer_count = *reinterpret_cast<volatile int*>(C.peer.seq);
+    __syncthreads();
+    fan.world = C.peer.world;
+    fan.rank = C.peer.rank;
+    fan.tag = static_cast<uint32_t>(peer_count + 1);
+    if (C.peer.wait) expect = peer_count;
+  }
+
   int f = 0;
   for (int pi = 0; pi < count; ++pi) {
     if (pi > 0) grid_barrier(C.status);   // projection pi may read what pi - 1 wrote
     const int KCH = (d.K + F::kElems - 1) / F::kElems;
-    gemv_load_activations<FMT, MT, PLAIN>(d, s, min(MT, d.M), KCH * F::kElems, L.ap, L.frag);
+    gemv_load_activations<FMT, MT, PLAIN>(d, s, min(MT, d.M), KCH * F::kElems, L.ap, L.frag,
+                                          pi == 0 ? expect : -1, C.status);
     if (pi == count - 1) pdl_launch();
     const int mt = min(MT, d.M);
     // Keep HBM busy past the grid barriers: this warp's rows of the next two projections into
@@ -859,19 +916,19 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
     }
     switch (FIXED >= 0 ? FIXED : d.cfg) {   // FIXED: one decomposition (a single projection)
       case kCfgR32:
-        if constexpr (RMAX == 32 && (FIXED < 0 || FIXED == kCfgR32)) run_proj<FMT, MT, PLAIN, NS, MAXP, 32, 1>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        if constexpr (RMAX == 32 && (FIXED < 0 || FIXED == kCfgR32)) run_proj<FMT, MT, PLAIN, NS, MAXP, 32, 1>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt, fan);
         break;
       case kCfgS1:
-        if constexpr (FIXED < 0 || FIXED == kCfgS1) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 1>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        if constexpr (FIXED < 0 || FIXED == kCfgS1) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 1>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt, fan);
         break;
       case kCfgS2:
-        if constexpr (FIXED < 0 || FIXED == kCfgS2) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 2>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        if constexpr (FIXED < 0 || FIXED == kCfgS2) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 2>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt, fan);
         break;
       case kCfgS4:
-        if constexpr (FIXED < 0 || FIXED == kCfgS4) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 4>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        if constexpr (FIXED < 0 || FIXED == kCfgS4) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 4>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt, fan);
         break;
       default:
-        if constexpr (FIXED < 0 || FIXED == kCfgS8) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 8>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt);
+        if constexpr (FIXED < 0 || FIXED == kCfgS8) run_proj<FMT, MT, PLAIN, NS, MAXP, 8, 8>(d, q, s, iss, f, ok, C.status, L, ring, sring, mt, fan);
         break;
     }
     if (pi + 1 < count) {   // ahead of the barrier, off the critical path
@@ -879,6 +936,13 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
       q = geometry<FMT>(d, warp);
     }
     if (MAXP > 1) __syncthreads();   // the next projection's activations overwrite shared memory
+  }
+  if (MAXP == 1 && C.peer.world > 0) {   // the last CTA advances this rank's count
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(C.peer.done, 1) == static_cast<int>(gridDim.x) - 1) {
+      *C.peer.done = 0;
+      *reinterpret_cast<volatile int*>(C.peer.seq) = peer_count + 1;
+    }
   }
 }
 // The weight rows as a 2-D tensor of bytes: [N][row_bytes] with rows rs bytes apart, copied in
@@ -1052,6 +1116,14 @@ int single_fmt(const MMParams& p, cudaStream_t stream, bool pdl, int dev) {
     if (!encode_rows_map(&C.proj[0].map, p.rows, row_bytes, p.N, p.rs)) return kErrCuda;
     C.count = 1;
     C.status = p.status;
+    if (p.peer != nullptr) {   // a row-sharded decode projection (M = 1: one pass)
+      C.peer.rank = p.peer->rank;
+      C.peer.world = p.peer->world;
+      C.peer.wait = p.peer->wait;
+      for (int r = 0; r < kMaxPeers; ++r) C.peer.delta[r] = r < p.peer->world ? p.peer->delta[r] : 0;
+      C.peer.seq = p.peer->seq;
+      C.peer.done = p.peer->done;
+    }
     for (int attempt = 0; attempt < 2; ++attempt) {
       C.proj[0].cfg = cfg;
       const int R = cfg_rows(cfg), S = cfg_split(cfg);

@@ -56,6 +56,7 @@ struct MMParams {
   int64_t ldy;
   int split;    // otq_qmm_ex's k_split (0 picks)
   int* status;   // device status word (may be null): kStatusTimeout bits
+  const otq_peer* peer;   // otq_qmm_peer's output fan-out over NVLink, or null
 };
 
 // One projection of the prefill GEMM (prefill.cu), checked by the caller: x bf16 [M, K] (ldx

@@ -143,17 +143,45 @@ __device__ __forceinline__ uint32_t mag_bits(float v) {
 // n/32 words; red: of NT/32 + 3 words. emit(i, q0, q1, q2, q3, d) gets elements 4i..4i+3 and
 // their group's offset; the 8 threads of a group call it together (lanes 8k..8k+7 of a warp).
 // Ends with a barrier.
+// Two (value, tag) words of a tagged row: each 8-byte element is read single-copy atomically,
+// bypassing L1 (the row is written by other GPUs while this kernel runs).
+__device__ __forceinline__ void ld_tagged2(const unsigned long long* p, unsigned long long& a,
+                                           unsigned long long& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ int tag_of(unsigned long long w) {
+  return static_cast<int>(static_cast<uint32_t>(w >> 32));
+}
+
 template <int NT, class Emit4>
 __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, bool x4, float* xs,
                                                    int n, bool row_mode, uint32_t* segm,
-                                                   uint32_t* red, Emit4 emit) {
+                                                   uint32_t* red, Emit4 emit,
+                                                   const unsigned long long* xt = nullptr,
+                                                   int expect = 0, int* status = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NW = NT / 32;
   const int n4 = n >> 2;   // a multiple of 32: every lane of a warp runs the same iterations
   uint32_t tmax = 0u;
   for (int i = tid; i < n4; i += NT) {
     float4 v;
-    if (x4) {
+    if (xt != nullptr) {
+      // a tagged row (value in the low word, the writer's tag in the high word): wait, bounded,
+      // until the four elements carry at least the expected tag
+      unsigned long long a0, a1, a2, a3;
+      for (uint32_t spin = 0;; ++spin) {
+        ld_tagged2(xt + 4 * i, a0, a1);
+        ld_tagged2(xt + 4 * i + 2, a2, a3);
+        if (min(min(tag_of(a0), tag_of(a1)), min(tag_of(a2), tag_of(a3))) >= expect) break;
+        if (spin >= (1u << 22)) {
+          if (status != nullptr) atomicOr(status, 1);   // a writer never arrived: not valid
+          break;
+        }
+        if (spin >= 16) __nanosleep(32);
+      }
+      v = make_float4(__uint_as_float(static_cast<uint32_t>(a0)), __uint_as_float(static_cast<uint32_t>(a1)),
+                      __uint_as_float(static_cast<uint32_t>(a2)), __uint_as_float(static_cast<uint32_t>(a3)));
+    } else if (x4) {
       v = ld_cg4(x + 4 * i);
     } else {
       v.x = __ldcg(x + 4 * i);

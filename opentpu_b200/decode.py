@@ -12,7 +12,13 @@ and the LM head [vocab, H] after the last layer.
 
 With world > 1 every projection's rows are split over the ranks (runtime.Weight(shard=0),
 runtime.py:138-142) and an all-gather assembles each output on every rank (the reference's
-GATHER, isasim.py:1413-1438), captured in the same graph.
+GATHER, isasim.py:1413-1438), captured in the same graph. gather="fused" (the default) fuses it
+into the GEMV: every projection's full output row lives in one symmetric buffer (torch
+symmetric memory, mapped into every rank) as tagged 8-byte words (value, tag), each rank's
+kernel stores its rows' words into every rank's copy over NVLink, and the next projection's
+kernel reads its input words until their tags show every rank's output has arrived
+(linear.qlinear_peer): no fence, flag or extra launch. gather="nccl" runs an NCCL all-gather
+after each projection instead.
 
 dependent=True (the default) chains the projections through their outputs the way a decode
 step does: each projection reads the first K outputs of the previous one (QKV's q part feeds O,
@@ -49,8 +55,12 @@ def shard_rows(N: int, world: int, rank: int) -> tuple[int, int]:
 class DecodeChain:
     def __init__(self, shape: DecoderShape, fmt: str = "int8-row", head_fmt: str = "int8-row",
                  seed: int = 0, world: int = 1, rank: int = 0, group=None, pdl: bool = True,
-                 std: float = 0.02, dependent: bool = True, chained: bool | None = None):
+                 std: float = 0.02, dependent: bool = True, chained: bool | None = None,
+                 gather: str = "fused"):
         self.shape, self.world, self.rank, self.group, self.pdl = shape, world, rank, group, pdl
+        if gather not in ("fused", "nccl"):
+            raise ValueError("gather must be 'fused' or 'nccl'")
+        self.fused = world > 1 and gather == "fused"
         self.dependent = dependent
         # chained: the whole step as one persistent launch (linear.qlinear_chain). Measured on
         # a B200 it is slower today than one launch a projection (1.12 vs 0.61 ms for the
@@ -81,13 +91,20 @@ class DecodeChain:
             self.weight_bytes += w.stream_bytes * world
             if K not in self.inputs:
                 self.inputs[K] = torch.randn((1, K), generator=gen, device="cuda")
-            self.outs.append(torch.zeros((1, n), device="cuda"))
-            self.gathered.append(torch.zeros((world, n), device="cuda") if world > 1 else None)
+            if not self.fused:
+                self.outs.append(torch.zeros((1, n), device="cuda"))
+                self.gathered.append(torch.zeros((world, n), device="cuda") if world > 1 else None)
+        if self.fused:
+            self._symmetric_outputs()
         # the input each projection reads: a fixed vector, or the previous projection's output
         self.x_of = []
         for i, (name, N, K, f) in enumerate(self.plan):
             if not dependent or i == 0:
                 self.x_of.append(self.inputs[K])
+            elif self.fused:   # the previous projection's tagged words
+                if self.full[i - 1].shape[0] < K:
+                    raise ValueError(f"{name}: the previous output has {self.full[i - 1].shape[0]} < {K}")
+                self.x_of.append(self.full[i - 1][:K])
             else:
                 prev = self.full_out(i - 1)
                 if prev.shape[1] < K:
@@ -102,18 +119,64 @@ class DecodeChain:
             self.table = linear.chain_table([(x, w, y, False, False) for x, w, y in
                                              zip(self.x_of, self.weights, self.outs)])
 
+    def _symmetric_outputs(self):
+        """Every projection's full output row as tagged words ([N, 2] float32: value, tag bits)
+        in one symmetric buffer (16-byte aligned slots); this rank's projection count and the
+        launches' CTA count in ordinary device memory. All zero before the first launch."""
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        from . import _lib as L
+        offs, tot = [], 0
+        for _, N, _, _ in self.plan:
+            offs.append(tot)
+            tot += 2 * (-(-N // 2) * 2)   # N words of 8 bytes, rounded to 16 bytes
+        try:
+            symm.set_backend("CUDA")
+        except Exception:
+            pass   # already chosen by an earlier allocation
+        buf = symm.empty(tot, dtype=torch.float32, device="cuda")
+        buf.zero_()
+        group = self.group if self.group is not None else dist.group.WORLD
+        handle = symm.rendezvous(buf, group)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        ptrs = handle.buffer_ptrs
+        self._symm = (buf, handle)
+        self.counters = torch.zeros(2, dtype=torch.int32, device="cuda")   # count, done CTAs
+        self.full, self.peers = [], []
+        for i, (o, (_, N, _, _)) in enumerate(zip(offs, self.plan)):
+            words = buf[o:o + 2 * N].view(N, 2)
+            n0, n1 = shard_rows(N, self.world, self.rank)
+            self.full.append(words)
+            self.outs.append(words[n0:n1])
+            self.gathered.append(None)
+            pr = L.Peer()
+            pr.rank, pr.world = self.rank, self.world
+            pr.wait = int(self.dependent and i > 0)
+            for r in range(self.world):
+                pr.delta[r] = ptrs[r] - ptrs[self.rank]
+            pr.seq = self.counters.data_ptr()
+            pr.done = self.counters.data_ptr() + 4
+            self.peers.append(pr)
+
     @property
     def launches(self) -> int:
         return 1 if self.chained else len(self.plan)
 
     def full_out(self, i: int) -> torch.Tensor:
         """Projection i's whole output row [1, N] (the gathered one with world > 1)."""
+        if self.fused:   # the values of the tagged words
+            return self.full[i][:, 0].unsqueeze(0)
         return self.gathered[i].reshape(1, -1) if self.world > 1 else self.outs[i]
 
     def step_eager(self):
         import torch.distributed as dist
         if self.chained:
             linear.qlinear_chain(self.table)
+            return
+        if self.fused:
+            for x, w, y, pr in zip(self.x_of, self.weights, self.outs, self.peers):
+                linear.qlinear_peer(x, w, y, pr, pdl=self.pdl)
             return
         for x, w, y, g in zip(self.x_of, self.weights, self.outs, self.gathered):
             linear.qlinear(x, w, out=y, pdl=self.pdl)
@@ -150,3 +213,4 @@ class DecodeChain:
 
     def release(self):
         self.graph = None
+        self.table = None

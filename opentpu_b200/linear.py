@@ -304,6 +304,35 @@ def gemm_w8a16_group(items) -> list:
     return outs
 
 
+def qlinear_peer(x: torch.Tensor, w: PackedWeight, y: torch.Tensor, peer, *,
+                 row_mode: bool = False, pdl: bool = False) -> torch.Tensor:
+    """QACT + MM of one activation row against this rank's rows of a row-sharded projection,
+    the output all-gather fused in (otq_qmm_peer). y is this rank's slice of its symmetric copy
+    of the output row as tagged words: a contiguous float32 tensor [N, 2] (value, tag bits).
+    x is plain fp32 [K] (peer.wait == 0) or the previous projection's tagged row [K, 2]
+    (peer.wait != 0). Every rank must make the same sequence of calls."""
+    if w.fmt == "int4-g32":
+        raise ValueError("int4-g32 is not an MM format; it has no fused gather")
+    _cuda(x, "x")
+    _cuda(y, "y")
+    if peer.wait:
+        if x.dtype != torch.float32 or x.numel() != 2 * w.K or not x.is_contiguous():
+            raise ValueError(f"a tagged x must be a contiguous float32 [{w.K}, 2] view")
+        xp, ldx = x.data_ptr(), w.K
+    else:
+        x2, _ = _as_rows(x, w.K)
+        if x2.shape[0] != 1:
+            raise ValueError("the fused gather takes one activation row")
+        xp, ldx = x2.data_ptr(), x2.stride(0)
+    if y.dtype != torch.float32 or y.numel() != 2 * w.N or not y.is_contiguous():
+        raise ValueError(f"y must be a contiguous float32 [{w.N}, 2] view")
+    import ctypes
+    L.call("otq_qmm_peer", L.FMT[w.mx_fmt], w.flags, w.rows.data_ptr(), w.rows.stride(0),
+           _ptr(w.srows), 0 if w.srows is None else w.srows.stride(0), w.k0, w.N, w.K,
+           xp, ldx, int(row_mode), y.data_ptr(), ctypes.addressof(peer), int(pdl), _stream())
+    return y
+
+
 def chain_table(steps) -> "ctypes.Array":
     """The otq_proj array of a chain: steps is a list of (x [K] or [1, K], w, out [N] or [1, N],
     acc, row_mode) with MX / int8-row weights. Kept by the caller to call qlinear_chain again."""
