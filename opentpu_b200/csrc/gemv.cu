@@ -412,12 +412,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 // stage sst, one commit group per issue.
 template <int FMT, bool PLAIN>
 __device__ __forceinline__ void gemv_issue(uint32_t st, uint32_t sst, uint32_t bar, const PArgs& p,
-                                           int64_t row0, int nrows, int kc, int lane) {
-  const int boxes = (nrows + kBox - 1) / kBox;
-  if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(boxes * kBox * kChunk));
+                                           int64_t row0, int nrows, int kc, int lane, int bh) {
+  // bh: rows of the map's box (8, or 32 for a single 32-row-block projection: one copy a stage,
+  // the same shared layout as four 8-row boxes stacked)
+  const int boxes = nrows > 0 ? (nrows + bh - 1) / bh : 0;
+  if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(boxes * bh * kChunk));
   __syncwarp();
   if (lane < boxes)
-    tma_load_2d(st + lane * kBox * kChunk, p.map, kc * kChunk, static_cast<int>(row0) + kBox * lane, bar);
+    tma_load_2d(st + lane * bh * kChunk, p.map, kc * kChunk, static_cast<int>(row0) + bh * lane, bar);
   if constexpr (!PLAIN) {
     if (lane < nrows) {
       const uint8_t* srow = p.srows + (row0 + lane) * p.srs;
@@ -634,7 +636,7 @@ struct RingIssue {
     if (k >= q.NSL || nrows < 0) nrows = 0;
     const int st = issued % NS;
     gemv_issue<FMT, PLAIN>(ring_s + st * stage_bytes, sring_s + st * scale_bytes, bar0 + 8 * st, d,
-                           r0, nrows, q.c0 + k, lane);
+                           r0, nrows, q.c0 + k, lane, MAXP == 1 && d.cfg == kCfgR32 ? 32 : kBox);
     ++issued;
     ++i;
     return true;
@@ -948,7 +950,8 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
 // The weight rows as a 2-D tensor of bytes: [N][row_bytes] with rows rs bytes apart, copied in
 // boxes of 8 rows x 128 bytes with the 128-byte swizzle. cuTensorMapEncodeTiled comes from the
 // driver through the runtime's entry-point query (nothing links libcuda).
-bool encode_rows_map(CUtensorMap* map, const uint8_t* rows, int row_bytes, int64_t N, int64_t rs) {
+bool encode_rows_map(CUtensorMap* map, const uint8_t* rows, int row_bytes, int64_t N, int64_t rs,
+                     int box_rows = kBox) {
   static PFN_cuTensorMapEncodeTiled encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
@@ -960,7 +963,7 @@ bool encode_rows_map(CUtensorMap* map, const uint8_t* rows, int row_bytes, int64
   }
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(N)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(rs)};
-  const cuuint32_t box[2] = {kChunk, kBox};
+  const cuuint32_t box[2] = {kChunk, static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(rows), dims, strides, box,
                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1015,6 +1018,15 @@ int launch_chain(const Chain<MAXP>& C, const GLayout& L, int grid, bool coop, cu
                              static_cast<int>(smem)) != cudaSuccess)
       return kErrCuda;
     configured_smem[dev] = smem;
+  }
+  // every instantiation asks for the same (largest) shared-memory carveout, so a dependent
+  // launch's CTAs can join an SM that still runs the previous kernel without reconfiguring it
+  static bool carveout[kMaxDevices] = {false};
+  if (!carveout[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+      return kErrCuda;
+    carveout[dev] = true;
   }
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess)
@@ -1113,7 +1125,6 @@ int single_fmt(const MMParams& p, cudaStream_t stream, bool pdl, int dev) {
     Chain<1> C;
     std::memset(&C, 0, sizeof(C));
     fill_proj(C.proj[0], p, m0, mt);
-    if (!encode_rows_map(&C.proj[0].map, p.rows, row_bytes, p.N, p.rs)) return kErrCuda;
     C.count = 1;
     C.status = p.status;
     if (p.peer != nullptr) {   // a row-sharded decode projection (M = 1: one pass)
@@ -1126,6 +1137,8 @@ int single_fmt(const MMParams& p, cudaStream_t stream, bool pdl, int dev) {
     }
     for (int attempt = 0; attempt < 2; ++attempt) {
       C.proj[0].cfg = cfg;
+      if (!encode_rows_map(&C.proj[0].map, p.rows, row_bytes, p.N, p.rs, cfg == kCfgR32 ? 32 : kBox))
+        return kErrCuda;
       const int R = cfg_rows(cfg), S = cfg_split(cfg);
       const int64_t grid = (p.N + static_cast<int64_t>(R) * (kWarps / S) - 1) / (static_cast<int64_t>(R) * (kWarps / S));
       const int g = static_cast<int>(grid < (1 << 20) ? grid : (1 << 20));

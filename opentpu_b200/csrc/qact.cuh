@@ -163,39 +163,59 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
   constexpr int NW = NT / 32;
   const int n4 = n >> 2;   // a multiple of 32: every lane of a warp runs the same iterations
   uint32_t tmax = 0u;
-  for (int i = tid; i < n4; i += NT) {
-    float4 v;
-    if (xt != nullptr) {
-      // a tagged row (value in the low word, the writer's tag in the high word): wait, bounded,
-      // until the four elements carry at least the expected tag
-      unsigned long long a0, a1, a2, a3;
-      for (uint32_t spin = 0;; ++spin) {
-        ld_tagged2(xt + 4 * i, a0, a1);
-        ld_tagged2(xt + 4 * i + 2, a2, a3);
-        if (min(min(tag_of(a0), tag_of(a1)), min(tag_of(a2), tag_of(a3))) >= expect) break;
-        if (spin >= (1u << 22)) {
-          if (status != nullptr) atomicOr(status, 1);   // a writer never arrived: not valid
-          break;
-        }
-        if (spin >= 16) __nanosleep(32);
+  // x comes from L2 (the previous kernel wrote it): all of a thread's loads of a batch are in
+  // flight together, so the prologue pays one memory latency a batch, not one a chunk
+  constexpr int kB = 4;
+  for (int i0 = tid; i0 < n4; i0 += NT * kB) {
+    float4 v[kB];
+    unsigned long long w[kB][4];
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int i = i0 + b * NT;   // warp-uniform bound: n4 is a multiple of 32
+      if (i >= n4) continue;
+      if (xt != nullptr) {
+        ld_tagged2(xt + 4 * i, w[b][0], w[b][1]);
+        ld_tagged2(xt + 4 * i + 2, w[b][2], w[b][3]);
+      } else if (x4) {
+        v[b] = ld_cg4(x + 4 * i);
+      } else {
+        v[b].x = __ldcg(x + 4 * i);
+        v[b].y = __ldcg(x + 4 * i + 1);
+        v[b].z = __ldcg(x + 4 * i + 2);
+        v[b].w = __ldcg(x + 4 * i + 3);
       }
-      v = make_float4(__uint_as_float(static_cast<uint32_t>(a0)), __uint_as_float(static_cast<uint32_t>(a1)),
-                      __uint_as_float(static_cast<uint32_t>(a2)), __uint_as_float(static_cast<uint32_t>(a3)));
-    } else if (x4) {
-      v = ld_cg4(x + 4 * i);
-    } else {
-      v.x = __ldcg(x + 4 * i);
-      v.y = __ldcg(x + 4 * i + 1);
-      v.z = __ldcg(x + 4 * i + 2);
-      v.w = __ldcg(x + 4 * i + 3);
     }
-    *reinterpret_cast<float4*>(xs + 4 * i) = v;
-    uint32_t m = max(max(mag_bits(v.x), mag_bits(v.y)), max(mag_bits(v.z), mag_bits(v.w)));
-    m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-    m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-    m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
-    if ((lane & 7) == 0) segm[i >> 3] = m;
-    tmax = max(tmax, m);
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int i = i0 + b * NT;
+      if (i >= n4) continue;
+      if (xt != nullptr) {
+        // a tagged row (value in the low word, the writer's tag in the high word): wait,
+        // bounded, until the four elements carry at least the expected tag
+        for (uint32_t spin = 0;
+             min(min(tag_of(w[b][0]), tag_of(w[b][1])), min(tag_of(w[b][2]), tag_of(w[b][3]))) < expect;
+             ++spin) {
+          if (spin >= (1u << 22)) {
+            if (status != nullptr) atomicOr(status, 1);   // a writer never arrived: not valid
+            break;
+          }
+          if (spin >= 16) __nanosleep(32);
+          ld_tagged2(xt + 4 * i, w[b][0], w[b][1]);
+          ld_tagged2(xt + 4 * i + 2, w[b][2], w[b][3]);
+        }
+        v[b] = make_float4(__uint_as_float(static_cast<uint32_t>(w[b][0])),
+                           __uint_as_float(static_cast<uint32_t>(w[b][1])),
+                           __uint_as_float(static_cast<uint32_t>(w[b][2])),
+                           __uint_as_float(static_cast<uint32_t>(w[b][3])));
+      }
+      *reinterpret_cast<float4*>(xs + 4 * i) = v[b];
+      uint32_t m = max(max(mag_bits(v[b].x), mag_bits(v[b].y)), max(mag_bits(v[b].z), mag_bits(v[b].w)));
+      m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+      m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+      m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
+      if ((lane & 7) == 0) segm[i >> 3] = m;
+      tmax = max(tmax, m);
+    }
   }
   tmax = __reduce_max_sync(0xFFFFFFFFu, tmax);
   if (lane == 0) red[warp] = tmax;
