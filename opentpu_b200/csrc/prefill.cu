@@ -11,10 +11,10 @@
 // A CTA tile is 256 tokens x 256 weight rows; the work units are tiles, or K slices of tiles,
 // of up to kW8A16MaxGroup independent projections (a layer's q/k/v/o/gate/up/down at prefill),
 // and a persistent CTA (one an SM) runs the units the host assigned it, longest first. A K
-// slice adds its share into y with vector float atomics (y zeroed first, or the old y with ACC),
-// so split tiles are summed in arrival order: still within the stated tolerance, but not
-// bit-reproducible from run to run; unsplit tiles are. K goes in chunks of 64 through two
-// shared-memory rings:
+// slice adds its share into y (tensor reduce-add, or vector float atomics; y zeroed first, or
+// the old y with ACC), so split tiles are summed in arrival order: still within the stated
+// tolerance, but not bit-reproducible from run to run; unsplit tiles are. K goes in chunks of
+// 64 through two shared-memory rings:
 //   warp 0      TMA: x's 256 x 64 bf16 box (128-byte swizzle: the K-major layout tcgen05.mma
 //               reads) and the weight tile's 256 x 64 int8 box into a load stage (lfull);
 //   warps 12-19 dequant prologue: int8 -> bf16 (exact) into a B stage in the same swizzled
@@ -24,8 +24,10 @@
 //               tcgen05.commit frees the stages (lempty, bempty) and, after the tile's last
 //               chunk, hands the two fp32 accumulators (2 x 256 columns) to the epilogue;
 //   warps 4-11  scale epilogue: tcgen05.ld of their 32 tensor-memory lanes (tokens), half the
-//               columns each, a transpose through shared memory, times Sw, coalesced fp32
-//               stores (ACC: added to the old y); then the accumulators are free again.
+//               columns each, times Sw, staged 32 x 8 at a time in shared memory and written by
+//               tensor bulk stores (bulk reduce-adds for K slices and ACC); when y does not
+//               suit the tensor engine (alignment), a transpose and coalesced fp32 stores. Then
+//               the accumulators are free again.
 // Every mbarrier wait is bounded (mm_common.cuh): a wait that runs out sets bit 0 of the
 // library's status word, and the CTA stops, letting the copies and MMAs it issued finish
 // (bounded) before it frees tensor memory.
@@ -69,7 +71,9 @@ struct Smem {
   uint8_t a[kNL][kABytes];   // 1024-aligned (128-byte swizzle atoms)
   uint8_t b[kNB][kBBytes];
   uint8_t i8[kNL][kIBytes];
-  float stage[kEpiWarps][32 * 16];   // epilogue transposes: a 32 x 16 block an epilogue warp
+  // epilogue staging, 2 KB an epilogue warp: a 32 x 16 transpose block, or two 32 x 8 blocks
+  // (32-byte swizzle) that tensor stores read
+  float stage[kEpiWarps][32 * 16];
   float sw[kTN];
   uint64_t lfull[kNL], lempty[kNL], bconv[kNB], bempty[kNB], acc_full, acc_empty, drain;
   uint32_t tmem;
@@ -85,7 +89,9 @@ struct alignas(64) GProj {
   int tiles_m, tile0;   // token tiles; first unit of this projection (round-robin mode)
   int nk, cps, splits;  // K chunks; chunks a K slice; K slices a tile (> 1: partial sums added)
   int flags;
-  int vec;   // y 16-byte aligned and ldy a multiple of 4: float4 stores
+  int vec;     // y 16-byte aligned and ldy a multiple of 4: float4 stores
+  int tma_y;   // ymap describes y: the epilogue writes (or adds) through the tensor engine
+  CUtensorMap ymap;   // y [M, N] fp32: box 8 columns x 32 rows, 32-byte swizzle
 };
 
 // Work units: a tile of one projection and one K slice of it. With a table, CTA b runs units
@@ -207,6 +213,39 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
+}
+
+// 8 consecutive fp32 columns of this warp's 32 tensor-memory lanes (the wait included).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+}
+
+// A 32-row x 8-column fp32 block from shared memory into y at (column x, row y): a store, or an
+// element-wise add (K slices, ACC). Out-of-range rows and columns are clipped by the engine.
+__device__ __forceinline__ void tma_store_y(const CUtensorMap* map, uint32_t src, int x, int y, bool add) {
+  if (add)
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::
+                     "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src)
+                 : "memory");
+  else
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::
+                     "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src)
+                 : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// At most N of this thread's bulk stores still reading shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -426,6 +465,44 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_kernel(const __grid_constan
       }
       tc_fence_after();
       const bool acc = (flags & OTQ_MM_ACC) != 0;
+      if (opaque(g.proj[t.p].tma_y)) {
+        // through the tensor engine: 32 x 8 blocks scaled in registers, staged (two buffers a
+        // warp, 32-byte swizzle), then one bulk store (or add: K slices, ACC) by lane 0
+        const CUtensorMap* ymap = &g.proj[t.p].ymap;
+        const bool add = t.split || acc;
+        const uint32_t buf0 = smem_addr(st);
+#pragma unroll 1
+        for (int h = 0; h < kMT; ++h) {
+          const int row0 = t.m0 + h * kBM + q * 32;
+#pragma unroll 1
+          for (int cb = 0; cb < 128; cb += 8) {
+            uint32_t r[8];
+            tmem_ld8(tmem + (static_cast<uint32_t>(q * 32) << 16) + h * kTN + hc * 128 + cb, r);
+            const float4 s0 = *reinterpret_cast<const float4*>(&s.sw[hc * 128 + cb]);
+            const float4 s1 = *reinterpret_cast<const float4*>(&s.sw[hc * 128 + cb + 4]);
+            const int blk = (h * 16 + cb / 8) & 1;
+            if (lane == 0) bulk_wait_read<1>();   // the store from this buffer two blocks ago
+            __syncwarp();
+            float* b = st + blk * 256 + lane * 8;
+            const int sx = (lane >> 2) & 1;   // 32-byte swizzle: chunk c of row r at c ^ (r / 4 % 2)
+            *reinterpret_cast<float4*>(b + 4 * sx) =
+                make_float4(__uint_as_float(r[0]) * s0.x, __uint_as_float(r[1]) * s0.y,
+                            __uint_as_float(r[2]) * s0.z, __uint_as_float(r[3]) * s0.w);
+            *reinterpret_cast<float4*>(b + 4 * (sx ^ 1)) =
+                make_float4(__uint_as_float(r[4]) * s1.x, __uint_as_float(r[5]) * s1.y,
+                            __uint_as_float(r[6]) * s1.z, __uint_as_float(r[7]) * s1.w);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // seen by the engine
+            __syncwarp();
+            if (lane == 0) tma_store_y(ymap, buf0 + blk * 1024, t.n0 + hc * 128 + cb, row0, add);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&s.acc_empty));
+        continue;
+      }
+      if (lane == 0) bulk_wait_read<0>();   // no tensor store still reads the staging block
+      __syncwarp();
       for (int h = 0; h < kMT; ++h) {
         const int64_t row0 = t.m0 + h * kBM + q * 32;   // this warp's 32 tokens
         const int64_t col0 = t.n0 + hc * 128;
@@ -495,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_kernel(const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&s.acc_empty));
     }
+    if (lane == 0) bulk_wait_all();   // this warp's tensor stores complete before the CTA exits
     if (!ok) atomicOr(&s.bad, 1);
   }
 
@@ -522,10 +600,11 @@ EncodeFn encoder() {
 }
 
 bool encode_2d(EncodeFn enc, CUtensorMap* map, CUtensorMapDataType type, const void* base,
-               int64_t inner, int64_t outer, int64_t stride_bytes, CUtensorMapSwizzle swizzle) {
+               int64_t inner, int64_t outer, int64_t stride_bytes, CUtensorMapSwizzle swizzle,
+               int box_inner = kBK, int box_outer = 256) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride_bytes)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), 256u};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
   const cuuint32_t estr[2] = {1, 1};
   return enc(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -716,6 +795,10 @@ int w8a16_launch(const W8A16Proj* projs, int count, cudaStream_t stream) {
     P.splits = pl->splits[i];
     P.flags = w.flags;
     P.vec = (reinterpret_cast<uintptr_t>(w.y) % 16 == 0 && w.ldy % 4 == 0) ? 1 : 0;
+    P.tma_y = P.vec && encode_2d(enc, &P.ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.y, w.N, w.M,
+                                 w.ldy * 4, CU_TENSOR_MAP_SWIZZLE_32B, 8, 32)
+                  ? 1
+                  : 0;
     // K slices add into y: start from zero unless ACC asks to add to the old values
     if (P.splits > 1 && !(w.flags & OTQ_MM_ACC) &&
         cudaMemset2DAsync(w.y, static_cast<size_t>(w.ldy) * 4, 0, static_cast<size_t>(w.N) * 4,
