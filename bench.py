@@ -4,9 +4,9 @@ One step = one decode token through every quantized projection of a Qwen3-0.6B-s
 (28 layers x q, k, v, o, gate, up, down, then the 151936 x 1024 LM head; int8 per-row weights
 from N(0, 0.02), the first input N(0, 1)). q/k/v and gate/up share their input and QACT range,
 so each group is one launch: 113 fused QACT+MM launches a step, each reading the previous
-launch's output as a decode step does (opentpu_b200.decode.DecodeChain, dependent), replayed as
-one CUDA graph. The weights (598 MB) exceed the 126 MB L2, so each step streams them from
-HBM.
+launch's output as a decode step does (opentpu_b200.decode.DecodeChain, dependent), then the
+greedy token (device argmax of the logits), replayed as one CUDA graph. The weights (598 MB)
+exceed the 126 MB L2, so each step streams them from HBM.
 
 --profile head|step|prefill runs a few launches and exits (the command the ncu summaries under
 profiles/ were captured with).
@@ -19,8 +19,8 @@ roofline is against the measured bf16 tensor peak.
 metric: decode weight GB/s (whole job) with tok/s = steps / s beside it. With --gpus N each
 projection's output rows are split over the N ranks (the reference's Weight(shard=0)) and every
 projection's output is assembled on every rank (the reference's GATHER) inside the GEMV itself:
-each rank stores its rows into every rank's copy over NVLink and the next projection waits on
-per-rank flags (DecodeChain gather="fused").
+each rank stores its rows' tagged 8-byte words into every rank's copy over NVLink and the next
+projection reads them when their tags arrive (DecodeChain gather="fused").
 
 --impl reference times the reference's CPU algorithm (the numpy port under oracle/, the same
 arithmetic as the reference's MM) on a bounded sample of the same step.
@@ -410,20 +410,21 @@ def main():
             if line.startswith("| dram_bytes_per_launch |"):
                 traffic = int(line.split("|")[2])
 
-    # end to end through the public API from host buffers: inputs H2D, logits D2H each step
+    # end to end through the public API from host buffers: the input H2D and the greedy token
+    # (the device argmax of the logits) D2H each step
     inputs_host = {shape.hidden: torch.randn((1, shape.hidden)).pin_memory()}
-    logits_host = torch.empty(tuple(chain.logits().shape), pin_memory=True)
+    token_host = torch.empty(1, dtype=torch.int64, pin_memory=True)
     h2d = sum(t.numel() * 4 for t in inputs_host.values())
-    d2h = logits_host.numel() * 4
+    d2h = token_host.numel() * 8
     for _ in range(3):
-        chain.run_host(inputs_host, logits_host)
+        chain.run_host(inputs_host, token_host)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     n_e2e = max(3, min(args.steps, 200))
     e0.record(stream)
     for _ in range(n_e2e):
-        chain.run_host(inputs_host, logits_host)
+        chain.run_host(inputs_host, token_host)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / n_e2e

@@ -229,6 +229,16 @@ OTQ_API int otq_gemm_w8a16(int flags, const uint8_t* rows, int64_t rs, const uin
  * each other. No counterpart in the reference (its projections are separate programs). */
 OTQ_API int otq_gemm_w8a16_group(const otq_gemm_proj* projs, int count, void* stream);
 
+/* ------------------------------------------------------------------ greedy token */
+
+/* The index of the first maximum of x[0], x[stride], ..., x[(n - 1) * stride] (stride 2 reads
+ * the values of a tagged row of otq_qmm_peer): the reference's greedy sink on the LM head's
+ * logits (llm/generate.py:252-280, numpy argmax, ties to the lowest index). out: two int64
+ * words of device memory (16-byte aligned), used as the reduction's accumulator and CTA count;
+ * the call zeroes them on `stream`, and after the launch out[0] holds the index and out[1]
+ * zero. 1 <= n < 2^32. */
+OTQ_API int otq_argmax(const float* x, int64_t n, int64_t stride, int64_t* out, void* stream);
+
 /* ------------------------------------------------------------------ 4-bit group-32 fp16 */
 
 /* quant.quantize(W, "int4", g=32, scale="fp16") (opentpu/quant.py:225-227 -> quant_block

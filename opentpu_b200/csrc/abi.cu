@@ -380,6 +380,16 @@ int otq_gemm_w8a16(int flags, const uint8_t* rows, int64_t rs, const uint8_t* sr
   return otq_gemm_w8a16_group(&p, 1, stream);
 }
 
+int otq_argmax(const float* x, int64_t n, int64_t stride, int64_t* out, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (x == nullptr || out == nullptr || n < 1 || n >= (int64_t{1} << 32) || stride < 1 ||
+      stride > (int64_t{1} << 20))
+    return kErrArg;
+  if (!aligned(x, 4) || !aligned(out, 16)) return kErrAlign;
+  return finish(argmax_launch(x, n, stride, out, out, static_cast<cudaStream_t>(stream)));
+}
+
 int otq_status_word(int* value, int reset) {
   int st = device_ok();
   if (st) return st;

@@ -873,6 +873,15 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
   iss.q = q;
 #pragma unroll 1
   for (int q = 0; q < NS - 1; ++q) iss.next();
+  // the row scales the epilogue reads (4 bytes a row, RSC): into L1 now, so that their memory
+  // latency is not paid at the end of the critical path (they never depend on the previous
+  // kernel)
+  if (MAXP == 1 && PLAIN && !(d.flags & kMmUnit) && lane < q.R) {
+    for (int b = 0; b < q.NBLK; ++b) {
+      const int64_t row = q.rb + static_cast<int64_t>(b) * q.R + lane;
+      if (row < q.re) asm volatile("prefetch.global.L1 [%0];" ::"l"(d.srows + row * d.srs));
+    }
+  }
   pdl_wait();   // the activations may come from the kernel launched before
 
   // output fan-out (single-projection launches of a row-sharded step): this rank's count of

@@ -113,6 +113,9 @@ class DecodeChain:
         self.graph = None
         self.stream = torch.cuda.Stream()
         self.table = None
+        # the greedy token of the step (the reference's device argmax over the head's logits,
+        # llm/generate.py:252-280): word 0 of this buffer after every step
+        self.token = torch.zeros(2, dtype=torch.int64, device="cuda")
         if self.chained:
             if world > 1:
                 raise ValueError("a chained step has no all-gather: world must be 1")
@@ -161,7 +164,7 @@ class DecodeChain:
 
     @property
     def launches(self) -> int:
-        return 1 if self.chained else len(self.plan)
+        return (1 if self.chained else len(self.plan)) + 1   # + the argmax
 
     def full_out(self, i: int) -> torch.Tensor:
         """Projection i's whole output row [1, N] (the gathered one with world > 1)."""
@@ -173,15 +176,15 @@ class DecodeChain:
         import torch.distributed as dist
         if self.chained:
             linear.qlinear_chain(self.table)
-            return
-        if self.fused:
+        elif self.fused:
             for x, w, y, pr in zip(self.x_of, self.weights, self.outs, self.peers):
                 linear.qlinear_peer(x, w, y, pr, pdl=self.pdl)
-            return
-        for x, w, y, g in zip(self.x_of, self.weights, self.outs, self.gathered):
-            linear.qlinear(x, w, out=y, pdl=self.pdl)
-            if self.world > 1:
-                dist.all_gather_into_tensor(g, y, group=self.group)
+        else:
+            for x, w, y, g in zip(self.x_of, self.weights, self.outs, self.gathered):
+                linear.qlinear(x, w, out=y, pdl=self.pdl)
+                if self.world > 1:
+                    dist.all_gather_into_tensor(g, y, group=self.group)
+        linear.argmax(self.logits(), out=self.token)
 
     def capture(self, warmup: int = 3):
         with torch.cuda.stream(self.stream):
@@ -198,15 +201,16 @@ class DecodeChain:
             for _ in range(n):
                 self.graph.replay()
 
-    def run_host(self, inputs_host: dict, logits_host: torch.Tensor):
+    def run_host(self, inputs_host: dict, token_host: torch.Tensor):
         """One step from host buffers: each input vector copied from pinned host memory, the
-        graph replayed, the logits copied back (all on the chain's stream, asynchronous)."""
+        graph replayed, the greedy token id copied back into token_host (int64 [1], pinned; all
+        on the chain's stream, asynchronous)."""
         with torch.cuda.stream(self.stream):
             for K, t in inputs_host.items():
                 if not self.dependent or K == self.plan[0][2]:
                     self.inputs[K].copy_(t, non_blocking=True)
             self.graph.replay()
-            logits_host.copy_(self.logits(), non_blocking=True)
+            token_host.copy_(self.token[:1], non_blocking=True)
 
     def logits(self) -> torch.Tensor:
         return self.full_out(len(self.plan) - 1)

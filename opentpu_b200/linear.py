@@ -333,6 +333,23 @@ def qlinear_peer(x: torch.Tensor, w: PackedWeight, y: torch.Tensor, peer, *,
     return y
 
 
+def argmax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The index of the first maximum of the logit row x (a 1-D or [1, N] float32 view with any
+    element stride): the reference's greedy sink (llm/generate.py:252-280; numpy argmax, ties to
+    the lowest id), on the device. Returns an int64 tensor of 2 words whose first is the index
+    (`out`, if given, is reused)."""
+    _cuda(x, "x")
+    if x.dtype != torch.float32:
+        raise ValueError("x must be float32")
+    v = x.reshape(-1) if x.dim() > 1 and x.shape[0] == 1 else x
+    if v.dim() != 1:
+        raise ValueError("x must be one row")
+    if out is None:
+        out = torch.empty(2, dtype=torch.int64, device=x.device)
+    L.call("otq_argmax", v.data_ptr(), v.numel(), v.stride(0), out.data_ptr(), _stream())
+    return out
+
+
 def chain_table(steps) -> "ctypes.Array":
     """The otq_proj array of a chain: steps is a list of (x [K] or [1, K], w, out [N] or [1, N],
     acc, row_mode) with MX / int8-row weights. Kept by the caller to call qlinear_chain again."""

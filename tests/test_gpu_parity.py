@@ -291,7 +291,7 @@ def test_decode_chain_chained_equals_launch_per_projection():
     from opentpu_b200.decode import DecodeChain
     a = DecodeChain(WL.TINY, chained=True)
     b = DecodeChain(WL.TINY, chained=False)
-    assert a.launches == 1 and b.launches == len(b.plan)
+    assert a.launches == 2 and b.launches == len(b.plan) + 1   # + the argmax launch
     a.step_eager()
     b.step_eager()
     torch.cuda.synchronize()
@@ -301,6 +301,10 @@ def test_decode_chain_chained_equals_launch_per_projection():
     a.replay(3)
     torch.cuda.synchronize()
     assert np.array_equal(bits(host(a.logits())), bits(host(b.logits())))
+    b.capture()
+    b.replay(1)
+    torch.cuda.synchronize()
+    assert int(a.token[0]) == int(b.token[0])
 
 
 # ---------------------------------------------------------------------------- token level
