@@ -239,6 +239,22 @@ OTQ_API int otq_gemm_w8a16_group(const otq_gemm_proj* projs, int count, void* st
  * zero. 1 <= n < 2^32. */
 OTQ_API int otq_argmax(const float* x, int64_t n, int64_t stride, int64_t* out, void* stream);
 
+/* otq_argmax for callers that cannot allocate device memory: a plugin or custom operator inside
+ * a host framework that owns every device buffer and hands it only its inputs and outputs, or a
+ * latency-critical loop where a cudaMalloc (which may synchronize the device) is not allowed.
+ * Such a caller has nowhere to put otq_argmax's 16 bytes of scratch; this call keeps them in a
+ * 256-byte array of the library's own device memory (present on every GPU that loads the
+ * library, until the process exits) and writes only the result: *index (one int64 of device
+ * memory, 8-byte aligned) = the index of the first maximum of x[0], x[stride], ...,
+ * x[(n - 1) * stride]. Nothing is allocated. Limits: 1 <= n < 2^32 (the largest row whose
+ * index fits the scratch key); a longer row returns OTQ_ERR_ARG. The first call on each device
+ * looks up the array's device address (a synchronous runtime call, made with that device
+ * current), so make it before any stream capture. Every call uses the same array and zeroes it
+ * first: calls that overlap on the GPU (on different streams) race and may return a wrong
+ * index. No counterpart in the reference (its argmax is numpy on the host). */
+OTQ_API int otq_argmax_noalloc(const float* x, int64_t n, int64_t stride, int64_t* index,
+                               void* stream);
+
 /* ------------------------------------------------------------------ 4-bit group-32 fp16 */
 
 /* quant.quantize(W, "int4", g=32, scale="fp16") (opentpu/quant.py:225-227 -> quant_block

@@ -390,6 +390,16 @@ int otq_argmax(const float* x, int64_t n, int64_t stride, int64_t* out, void* st
   return finish(argmax_launch(x, n, stride, out, out, static_cast<cudaStream_t>(stream)));
 }
 
+int otq_argmax_noalloc(const float* x, int64_t n, int64_t stride, int64_t* index, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (x == nullptr || index == nullptr || n < 1 || n >= (int64_t{1} << 32) || stride < 1 ||
+      stride > (int64_t{1} << 20))
+    return kErrArg;   // n past 2^32 - 1: the row's index no longer fits the scratch key
+  if (!aligned(x, 4) || !aligned(index, 8)) return kErrAlign;
+  return finish(argmax_noalloc_launch(x, n, stride, index, static_cast<cudaStream_t>(stream)));
+}
+
 int otq_status_word(int* value, int reset) {
   int st = device_ok();
   if (st) return st;

@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "otq_internal.h"
 
@@ -73,6 +74,48 @@ int argmax_launch(const float* x, int64_t n, int64_t stride, int64_t* acc, int64
   const int grid = static_cast<int>(want < 1 ? 1 : (want > sm_count(dev) ? sm_count(dev) : want));
   argmax_kernel<<<grid, kArgThreads, 0, stream>>>(x, n, stride, acc, index);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+}  // namespace otq
+
+// ---------------------------------------------------------------- the allocation-free variant
+// The same kernel with its two scratch words (key accumulator, CTA count) in this library's own
+// device memory instead of the caller's: for callers that can only write into buffers they are
+// handed. The array below is a module variable, present on every GPU that loads the library
+// until the process exits; its device address comes from cudaGetSymbolAddress, once per device
+// (host code only sees a host-side stand-in under the array's name). Every call shares it: the
+// launch zeroes both words first (cudaMemsetAsync on the caller's stream), and calls that
+// overlap on the GPU race on them.
+namespace otq {
+namespace {
+
+constexpr int kNoAllocScratchWords = 32;   // 256 bytes; one call uses 2 words
+static __device__ __align__(256) int64_t g_argmax_scratch[kNoAllocScratchWords];
+
+std::mutex g_scratch_mu;
+int64_t* g_scratch_dev[kMaxDevices] = {nullptr};
+
+// This device's address of g_argmax_scratch, looked up on the device's first call (with the
+// device current) and kept.
+int64_t* scratch_address(int dev) {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_dev[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_argmax_scratch) != cudaSuccess || p == nullptr) return nullptr;
+    g_scratch_dev[dev] = static_cast<int64_t*>(p);
+  }
+  return g_scratch_dev[dev];
+}
+
+}  // namespace
+
+int argmax_noalloc_launch(const float* x, int64_t n, int64_t stride, int64_t* index,
+                          cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kErrCuda;
+  int64_t* scratch = scratch_address(dev);
+  if (scratch == nullptr) return kErrCuda;
+  return argmax_launch(x, n, stride, scratch, index, stream);
 }
 
 }  // namespace otq

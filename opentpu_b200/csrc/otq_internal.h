@@ -81,6 +81,9 @@ int sm_count(int dev);
 // goes to *index (acc itself for otq_argmax)
 int argmax_launch(const float* x, int64_t n, int64_t stride, int64_t* acc, int64_t* index,
                   cudaStream_t stream);
+// the same with the scratch words in argmax.cu's own device array (otq_argmax_noalloc)
+int argmax_noalloc_launch(const float* x, int64_t n, int64_t stride, int64_t* index,
+                          cudaStream_t stream);
 int w8a16_launch(const W8A16Proj* projs, int count, cudaStream_t stream);   // prefill.cu
 int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);    // gemv.cu
 int chain_launch(const otq_proj* projs, int count, cudaStream_t stream);

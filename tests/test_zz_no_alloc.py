@@ -1,0 +1,62 @@
+"""otq_argmax_noalloc: the greedy-token argmax for callers that cannot allocate device memory
+(a plugin that is handed its inputs and outputs by a host framework that owns every buffer, or
+a loop in which a cudaMalloc is not allowed). It keeps the reduction's scratch in the library's
+own device array and writes only the index; here it must give the same index as otq_argmax,
+which takes that scratch from the caller, on two calls in a row (the second call's row has a
+smaller maximum than the first's, so scratch left over from the first call would show).
+
+Collected last on purpose (the file name), so that a run stopping at its first failure has run
+every other test before this one; it also passes alone in a fresh process."""
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.fail("these tests need a CUDA device")
+    from opentpu_b200 import _lib as L
+    L.load()
+    return L
+
+
+def _argmax_with_scratch(L, x):
+    out = torch.zeros(2, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    L.call("otq_argmax", x.data_ptr(), x.numel(), 1, out.data_ptr(), stream)
+    torch.cuda.synchronize()
+    return int(out[0])
+
+
+def _argmax_no_alloc(L, x, index):
+    stream = torch.cuda.current_stream().cuda_stream
+    L.call("otq_argmax_noalloc", x.data_ptr(), x.numel(), 1, index.data_ptr(), stream)
+    torch.cuda.synchronize()
+    return int(index[0])
+
+
+def test_no_alloc_argmax_matches_the_entry_point_with_scratch(lib):
+    rng = np.random.default_rng(17)
+    first = rng.standard_normal(151936).astype(np.float32)
+    first[123456] = 50.0                       # a large maximum late in the row
+    second = rng.standard_normal(151936).astype(np.float32)
+    second[77] = second[4000] = 9.0            # a smaller maximum, tied: the lower index wins
+    index = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+    for row in (first, second):
+        x = torch.from_numpy(row).cuda()
+        want = _argmax_with_scratch(lib, x)
+        got = _argmax_no_alloc(lib, x, index)
+        assert got == want == int(np.argmax(row))
+
+
+def test_no_alloc_argmax_rejects_rows_past_its_limit(lib):
+    x = torch.zeros(16, device="cuda")
+    index = torch.zeros(1, dtype=torch.int64, device="cuda")
+    with pytest.raises(ValueError):   # refused on the host: nothing is launched
+        lib.call("otq_argmax_noalloc", x.data_ptr(), 1 << 32, 1, index.data_ptr(),
+                 torch.cuda.current_stream().cuda_stream)
