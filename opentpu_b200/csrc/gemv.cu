@@ -413,8 +413,9 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 template <int FMT, bool PLAIN>
 __device__ __forceinline__ void gemv_issue(uint32_t st, uint32_t sst, uint32_t bar, const PArgs& p,
                                            int64_t row0, int nrows, int kc, int lane, int bh) {
-  // bh: rows of the map's box (8, or 32 for a single 32-row-block projection: one copy a stage,
-  // the same shared layout as four 8-row boxes stacked)
+  // bh: rows of the map's box. Launches use 8: a warp's partial last block then reads no rows
+  // past its range (a 32-row box needs a quarter of the issues but reads up to 31 rows of the
+  // next warp's range from DRAM a second time)
   const int boxes = nrows > 0 ? (nrows + bh - 1) / bh : 0;
   if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(boxes * bh * kChunk));
   __syncwarp();
@@ -636,7 +637,7 @@ struct RingIssue {
     if (k >= q.NSL || nrows < 0) nrows = 0;
     const int st = issued % NS;
     gemv_issue<FMT, PLAIN>(ring_s + st * stage_bytes, sring_s + st * scale_bytes, bar0 + 8 * st, d,
-                           r0, nrows, q.c0 + k, lane, MAXP == 1 && d.cfg == kCfgR32 ? 32 : kBox);
+                           r0, nrows, q.c0 + k, lane, kBox);
     ++issued;
     ++i;
     return true;
@@ -1146,8 +1147,7 @@ int single_fmt(const MMParams& p, cudaStream_t stream, bool pdl, int dev) {
     }
     for (int attempt = 0; attempt < 2; ++attempt) {
       C.proj[0].cfg = cfg;
-      if (!encode_rows_map(&C.proj[0].map, p.rows, row_bytes, p.N, p.rs, cfg == kCfgR32 ? 32 : kBox))
-        return kErrCuda;
+      if (!encode_rows_map(&C.proj[0].map, p.rows, row_bytes, p.N, p.rs)) return kErrCuda;
       const int R = cfg_rows(cfg), S = cfg_split(cfg);
       const int64_t grid = (p.N + static_cast<int64_t>(R) * (kWarps / S) - 1) / (static_cast<int64_t>(R) * (kWarps / S));
       const int g = static_cast<int>(grid < (1 << 20) ? grid : (1 << 20));
