@@ -189,6 +189,113 @@ __global__ void __launch_bounds__(kThreads) linear_g32_kernel(const G32Params p)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// One activation row (decode): one weight row a lane, 32 rows a CTA, the row's groups split over
+// the 8 warps, so every lane of a warp reads the same activations (shared-memory broadcasts).
+// x is staged as x'[k] = x[k] * 2^(-4 (k % 4)) (exact): nibble p of a half-word, masked in place
+// under the exponent of 2^23, is u * 16^p after one subtraction, and its product with x' is
+// u * x. With u = code ^ 8 = w + 8, a group adds s * (sum u x - 8 * sum x), the group sums of x
+// staged beside x'. Warps' partial sums meet in shared memory in a fixed order.
+
+__global__ void __launch_bounds__(kThreads) linear_g32_row_kernel(const G32Params p) {
+  extern __shared__ __align__(16) float sm[];
+  const int K = p.K, G = K >> 5;
+  float* const xs = sm;            // [K]  x'
+  float* const gsum = sm + K;      // [G]  sum of x over each group
+  float* const part = gsum + G;    // [8][32] the warps' partial sums
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int i = threadIdx.x; i < K; i += kThreads) {
+    const float v = __ldcg(p.x + i);
+    xs[i] = __fmul_rn(v, __int_as_float((127 - 4 * (i & 3)) << 23));   // x * 2^(-4 (i % 4))
+  }
+  for (int g = warp; g < G; g += kThreads / 32) {
+    float v = __ldcg(p.x + g * 32 + lane);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    if (lane == 0) gsum[g] = v;
+  }
+  __syncthreads();
+  const int g0 = warp * G / 8, g1 = (warp + 1) * G / 8;
+  const int64_t nblocks = (p.N + 31) / 32;
+  constexpr int U = 8;
+  for (int64_t rb = blockIdx.x; rb < nblocks; rb += gridDim.x) {   // persistent: x staged once
+  const int64_t row = rb * 32 + lane;
+  const bool valid = row < p.N;
+  const uint8_t* crow = p.codes + (valid ? row : 0) * (K / 2);
+  const uint16_t* srow = p.scales + (valid ? row : 0) * G;
+  float acc = 0.0f;
+  for (int g = g0; g < g1; g += U) {
+    uint4 w[U];
+    float sc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const bool ok = valid && g + u < g1;
+      w[u] = ok ? ld_stream(crow + static_cast<int64_t>(g + u) * 16) : make_uint4(0, 0, 0, 0);
+      sc[u] = ok ? half_bits_to_float(__ldg(srow + g + u)) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (g + u >= g1) break;
+      const float* xg = xs + (g + u) * 32;
+      const uint32_t ws[4] = {w[u].x ^ 0x88888888u, w[u].y ^ 0x88888888u, w[u].z ^ 0x88888888u,
+                              w[u].w ^ 0x88888888u};
+      float pa = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 x0 = *reinterpret_cast<const float4*>(xg + 8 * q);
+        const float4 x1 = *reinterpret_cast<const float4*>(xg + 8 * q + 4);
+        const uint32_t lo = ws[q], hi = ws[q] >> 16;
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t h = e < 4 ? lo : hi;
+          const uint32_t bitsv = (h & (0xFu << (4 * (e & 3)))) | 0x4B000000u;   // 2^23 + u 16^p
+          pa = __fmaf_rn(__fsub_rn(__uint_as_float(bitsv), 8388608.0f), xv[e], pa);
+        }
+      }
+      acc = __fmaf_rn(sc[u], __fmaf_rn(-8.0f, gsum[g + u], pa), acc);
+    }
+  }
+  part[warp * 32 + lane] = acc;
+  __syncthreads();
+  if (warp == 0 && valid) {
+    float v = part[lane];
+#pragma unroll
+    for (int w2 = 1; w2 < kThreads / 32; ++w2) v = __fadd_rn(v, part[w2 * 32 + lane]);
+    float* yp = p.y + row;
+    *yp = p.accumulate ? __fadd_rn(*yp, v) : v;
+  }
+  __syncthreads();   // part is rewritten by the next row block
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+int launch_g32_row(const G32Params& p, cudaStream_t stream) {
+  const size_t smem = (static_cast<size_t>(p.K) + p.K / 32 + kThreads) * 4;
+  static size_t configured[kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return kErrCuda;
+  if (smem > 48 * 1024 && configured[dev] < smem) {
+    if (cudaFuncSetAttribute(linear_g32_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return kErrCuda;
+    configured[dev] = smem;
+  }
+  static int occ_cache[kMaxDevices] = {0};
+  if (occ_cache[dev] == 0) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, linear_g32_row_kernel, kThreads,
+                                                      smem) != cudaSuccess)
+      return kErrCuda;
+    occ_cache[dev] = occ > 0 ? occ : 1;
+  }
+  const int64_t blocks = (p.N + 31) / 32;
+  const int64_t cap = static_cast<int64_t>(sm_count(dev)) * occ_cache[dev];
+  return launch_kernel(reinterpret_cast<const void*>(linear_g32_row_kernel),
+                       static_cast<int>(blocks < cap ? blocks : cap), kThreads, smem, stream, false,
+                       p);
+}
+
 template <int MT, int LPR>
 int launch_g32(const G32Params& p, cudaStream_t stream) {
   auto kern = linear_g32_kernel<MT, LPR>;
@@ -247,6 +354,8 @@ int linear_g32_launch(const uint8_t* codes, const uint16_t* scales, int64_t N, i
   G32Params p{codes, scales, N, K, x, ldx, M, accumulate, y, ldy};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  // one activation row: a weight row a lane, once there are enough 32-row blocks to fill the GPU
+  if (M == 1 && (N + 31) / 32 >= 64) return launch_g32_row(p, stream);
   const int nc = K / 32;
   int lpr = 4;
   while (lpr < 32 && nc / lpr > 8) lpr *= 2;
