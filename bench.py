@@ -11,6 +11,9 @@ exceed the 126 MB L2, so each step streams them from HBM.
 --profile head|step|prefill runs a few launches and exits (the command the ncu summaries under
 profiles/ were captured with).
 
+The line's "decode_4bit" object is BASELINE configuration 3: the same step with int4-g32 layers
+and an int8-row head (weight-only 4-bit GEMVs on fp32 activations).
+
 The line's "prefill" object is BASELINE configuration 4 (prefill TFLOP/s): 36 SmolLM3-3B-shaped
 layers of int8-row weights (2.8 GB) against 512 bf16 tokens, one grouped tcgen05 GEMM launch
 (opentpu_b200.linear.gemm_w8a16_group) a layer, the 36 launches one CUDA graph a step; its
@@ -332,6 +335,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["head", "step", "prefill"])
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-4bit", action="store_true")
     args = ap.parse_args()
     if args.profile:
         profile_run(args.profile)
@@ -438,6 +442,41 @@ def main():
         v, desc, threads = cpu_sample_seconds()
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
 
+    # BASELINE configuration 3 (the same decode with int4-g32 layers and an int8-row head)
+    dec4 = None
+    if not args.no_4bit:
+        # int4-g32 is weight-only (no MM, so no fused gather): NCCL all-gathers with world > 1
+        c4 = DecodeChain(shape, fmt="int4-g32", head_fmt="int8-row", world=world, rank=rank,
+                         group=group, gather="nccl")
+        c4.capture()
+        c4.replay(args.warmup)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        n4 = max(10, args.steps // 2)
+        with torch.cuda.stream(c4.stream):
+            e0.record(c4.stream)
+            c4.replay(n4)
+            e1.record(c4.stream)
+        torch.cuda.synchronize()
+        ms4 = e0.elapsed_time(e1) / n4
+        if world > 1:
+            t = torch.tensor([ms4], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms4 = float(t.item())
+        dec4 = {"metric": "decode weight GB/s", "value": c4.weight_bytes / (ms4 * 1e-3) / 1e9,
+                "unit": "GB/s", "ms_per_step": ms4, "tok_s": 1e3 / ms4, "steps": n4,
+                "config": {"workload": "Qwen3-0.6B-shaped decode step, layers int4 group-32 fp16 "
+                                       "scales (weight-only, fp32 activations), 151936x1024 "
+                                       "int8-row LM head, M=1 (BASELINE configuration 3)",
+                           "weights_bytes_per_step": c4.weight_bytes,
+                           "parallelism": f"row-shard x{world}" + (" + NCCL all-gather per "
+                                                                  "projection" if world > 1
+                                                                  else "")},
+                "gpu_launches": c4.launches * n4}
+        c4.release()
+        del c4
+
     prefill = None
     if not args.no_prefill:
         prefill = prefill_bench(world, rank, local, max(3, min(100, args.steps // 20)),
@@ -472,6 +511,7 @@ def main():
                     "ms_per_step": e2e_ms, "api": "DecodeChain.run_host"},
             "gpu_launches": chain.launches * args.steps,
             "clocks": clocks.summary(),
+            "decode_4bit": dec4,
             "prefill": prefill,
         }), flush=True)
     chain.release()
