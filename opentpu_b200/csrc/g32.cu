@@ -69,6 +69,13 @@ __global__ void __launch_bounds__(kThreads) pack_g32_kernel(const float* __restr
   if (lane == 0) scales[n * ng + g] = (amax == 0.0 || hb == 0) ? static_cast<uint16_t>(0x3C00) : hb;
 }
 
+// Both GEMV kernels launch with programmatic dependent launch: a CTA prefetches its first
+// weight rows into L2 before griddepcontrol.wait, and reads x and writes y only after it. The
+// next launch is released at exit (releasing it after x is staged, or at the start, measured
+// slower: its waiting CTAs then hold SM slots this launch's CTAs need). 4-bit Qwen3-0.6B step
+// 0.667 -> 0.600 ms.
+constexpr bool kG32Pdl = true;
+
 struct G32Params {
   const uint8_t* codes;
   const uint16_t* scales;
@@ -96,6 +103,21 @@ __device__ __forceinline__ float half_bits_to_float(uint16_t h) {
   return f;
 }
 
+// Weight rows [row0, row0 + rows) (clipped to N): codes and scales into L2, a hint issued before
+// griddepcontrol.wait (weights never depend on the kernel launched before). Whole 16-byte
+// pieces of 16-byte aligned ranges only.
+__device__ __forceinline__ void prefetch_rows_l2(const G32Params& p, int64_t row0, int rows) {
+  const int64_t n = p.N - row0 < rows ? p.N - row0 : rows;
+  const uint8_t* c = p.codes + row0 * (p.K / 2);
+  const uint8_t* s = reinterpret_cast<const uint8_t*>(p.scales + row0 * (p.K / 32));
+  const uint32_t cb = static_cast<uint32_t>(n * (p.K / 2)) & ~15u;
+  const uint32_t sb = static_cast<uint32_t>(n * (p.K / 32) * 2) & ~15u;
+  if ((reinterpret_cast<uintptr_t>(c) & 15u) == 0 && cb > 0)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(cb) : "memory");
+  if ((reinterpret_cast<uintptr_t>(s) & 15u) == 0 && sb > 0)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(s), "r"(sb) : "memory");
+}
+
 // LPR lanes per weight row, one 16-byte chunk (a whole group) per lane step; activations of
 // MT rows in shared memory as fp32. Signed nibbles become exact floats by the 2^23 + u trick.
 template <int MT, int LPR>
@@ -111,6 +133,7 @@ __global__ void __launch_bounds__(kThreads) linear_g32_kernel(const G32Params p)
   const int64_t ntasks = (p.N + R - 1) / R;
   const int64_t wstride = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
   const int64_t wfirst = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (lane == 0 && wfirst < ntasks) prefetch_rows_l2(p, wfirst * R, R);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int m0 = 0; m0 < p.M; m0 += MT) {
     const int mt = min(MT, p.M - m0);
@@ -203,6 +226,8 @@ __global__ void __launch_bounds__(kThreads) linear_g32_row_kernel(const G32Param
   float* const gsum = sm + K;      // [G]  sum of x over each group
   float* const part = gsum + G;    // [8][32] the warps' partial sums
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) * 32 < p.N)
+    prefetch_rows_l2(p, static_cast<int64_t>(blockIdx.x) * 32, 32);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int i = threadIdx.x; i < K; i += kThreads) {
     const float v = __ldcg(p.x + i);
@@ -292,7 +317,7 @@ int launch_g32_row(const G32Params& p, cudaStream_t stream) {
   const int64_t blocks = (p.N + 31) / 32;
   const int64_t cap = static_cast<int64_t>(sm_count(dev)) * occ_cache[dev];
   return launch_kernel(reinterpret_cast<const void*>(linear_g32_row_kernel),
-                       static_cast<int>(blocks < cap ? blocks : cap), kThreads, smem, stream, false,
+                       static_cast<int>(blocks < cap ? blocks : cap), kThreads, smem, stream, kG32Pdl,
                        p);
 }
 
@@ -322,7 +347,7 @@ int launch_g32(const G32Params& p, cudaStream_t stream) {
   const int64_t want = (ntasks + 7) / 8;
   const int64_t cap = static_cast<int64_t>(sm_count(dev)) * occ_cache[dev];
   return launch_kernel(reinterpret_cast<const void*>(kern), static_cast<int>(want < cap ? want : cap),
-                       kThreads, smem, stream, false, p);
+                       kThreads, smem, stream, kG32Pdl, p);
 }
 
 template <int MT>

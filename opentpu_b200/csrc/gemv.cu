@@ -297,11 +297,12 @@ __device__ __forceinline__ void put_group(const GSmem& s, int j, int G, int da) 
   }
 }
 
-// Activation rows [m0, m0 + mt) into shared memory (QACT of fp32 x, or copied bytes). Bytes past
-// K, and rows mt..MT-1, are zeros. With `frag`, the class path's A fragments as well.
+// The zeros the activation rows start from: bytes past K, rows mt..MT-1, the class flag and
+// (QACT of fp32 x on the class path) the A fragments. Touches shared memory only, so a launch
+// runs it before griddepcontrol.wait. Ends with a barrier.
 template <int FMT, int MT, bool PLAIN>
-__device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSmem& s, int mt, int kp, int ap,
-                                      bool frag, int expect = -1, int* status = nullptr) {
+__device__ __forceinline__ void gemv_clear_activations(const PArgs& p, const GSmem& s, int mt, int kp,
+                                                       int ap, bool frag) {
   const int K = p.K, KG = K / 32;
   if (threadIdx.x == 0) *s.flag = 0;
   for (int j = 0; j < MT; ++j) {
@@ -312,11 +313,20 @@ __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSme
       for (int G = threadIdx.x; G < KG; G += kThreads) s.term[G * MT + j] = 0;
   }
   if (threadIdx.x < MT && static_cast<int>(threadIdx.x) >= mt) s.Sa[threadIdx.x] = 0.0f;
-  __syncthreads();   // flag cleared before any group can set it
+  if (p.x != nullptr && frag)
+    for (int i = threadIdx.x; i < KG * 32; i += kThreads) s.afrag[i] = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();   // flag and fragments cleared before any group can set them
+}
+
+// Activation rows [m0, m0 + mt) into shared memory (QACT of fp32 x, or copied bytes). Bytes past
+// K, and rows mt..MT-1, are zeros. With `frag`, the class path's A fragments as well. cleared:
+// gemv_clear_activations already ran for this projection.
+template <int FMT, int MT, bool PLAIN>
+__device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSmem& s, int mt, int kp, int ap,
+                                      bool frag, bool cleared, int expect = -1, int* status = nullptr) {
+  const int K = p.K, KG = K / 32;
+  if (!cleared) gemv_clear_activations<FMT, MT, PLAIN>(p, s, mt, kp, ap, frag);
   if (p.x != nullptr) {
-    if (frag)   // the class path's A fragments start as zeros (ordered before the emits below
-                // by the first barrier of qact_row4)
-      for (int i = threadIdx.x; i < KG * 32; i += kThreads) s.afrag[i] = make_uint4(0u, 0u, 0u, 0u);
     for (int j = 0; j < mt; ++j) {
       const float* xr = p.x + static_cast<int64_t>(j) * p.ldx;
       const bool x4 = (reinterpret_cast<uintptr_t>(xr) & 15u) == 0;
@@ -834,7 +844,10 @@ __device__ __forceinline__ void run_proj(const PArgs& d, const Geo& q, const GSm
 // QACT + MM over the projections of C in order (M <= MT activation rows each). RMAX: the
 // largest row block the launch uses (the ring's stage size).
 template <int FMT, int MT, int NS, bool PLAIN, int MAXP, int RMAX, int FIXED>
-__global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 : 2)
+// One activation row, 8-row blocks: three CTAs' registers fit an SM (76-80 a thread, no spills),
+// so the next launch's CTAs start on SMs where two of this launch still run and issue their
+// first weight copies early (griddepcontrol). Measured 4-6 % off the Qwen3-0.6B step.
+__global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 : (MT == 1 ? 3 : 2))
     gemv_kernel(const __grid_constant__ Chain<MAXP> C, const GLayout L) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   using F = GF<FMT>;
@@ -883,6 +896,11 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
       if (row < q.re) asm volatile("prefetch.global.L1 [%0];" ::"l"(d.srows + row * d.srs));
     }
   }
+  // shared memory only: ahead of the wait
+  constexpr bool kCleared = MAXP == 1;
+  if (kCleared)
+    gemv_clear_activations<FMT, MT, PLAIN>(d, s, min(MT, d.M),
+                                           ((d.K + F::kElems - 1) / F::kElems) * F::kElems, L.ap, L.frag);
   pdl_wait();   // the activations may come from the kernel launched before
 
   // output fan-out (single-projection launches of a row-sharded step): this rank's count of
@@ -906,7 +924,8 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
     if (pi > 0) grid_barrier(C.status);   // projection pi may read what pi - 1 wrote
     const int KCH = (d.K + F::kElems - 1) / F::kElems;
     gemv_load_activations<FMT, MT, PLAIN>(d, s, min(MT, d.M), KCH * F::kElems, L.ap, L.frag,
-                                          pi == 0 ? expect : -1, C.status);
+                                          kCleared && pi == 0, pi == 0 ? expect : -1, C.status);
+    // the next launch starts here: earlier (before the wait) or later (at exit) measured slower
     if (pi == count - 1) pdl_launch();
     const int mt = min(MT, d.M);
     // Keep HBM busy past the grid barriers: this warp's rows of the next two projections into
