@@ -132,17 +132,34 @@ OTQ_API int otq_qmm_ex(int fmt, int flags, const uint8_t* rows, int64_t rs, cons
 /* The NVLink fan-out of a row-sharded decode projection (otq_qmm_peer). The ranks' output rows
  * live in symmetric buffers (one allocation a rank, mapped into every rank's address space);
  * delta[r] is the byte distance from this rank's buffer to rank r's as mapped here (delta[rank]
- * = 0). seq, done: two words of this GPU's memory, both zero before this rank's first
- * otq_qmm_peer launch; the launches keep done at zero between launches and seq equal to the
- * number of otq_qmm_peer launches this rank has run. */
+ * = 0). world 1 is one GPU: tagged outputs in its own memory, no fan-out. seq, done: two words
+ * of this GPU's memory, both zero before this rank's first otq_qmm_peer launch.
+ *
+ * Counted tags (tags = OTQ_TAGS_COUNTED): the launches keep done at zero between launches and
+ * seq equal to the number of otq_qmm_peer launches this rank has run; a launch's outputs carry
+ * tag seq + 1, read after the launch before it has finished.
+ *
+ * Stepped tags (tags = OTQ_TAGS_STEPPED): the launches form steps, a fixed sequence of
+ * launches run again and again (a decode step), each with its position step_pos (0 .. 1022) in
+ * the step, and seq counts completed steps: position p of step s tags its outputs s * 1024 + p
+ * + 1, and with wait != 0 reads x until its tags reach s * 1024 + p (the output of position p -
+ * 1 of the same step). Such a launch does not wait for the launch before it to finish (its
+ * input's tags order it; launched with pdl != 0 it overlaps that launch's tail); launches with
+ * wait == 0 wait for it as usual. The launch with step_last != 0 ends the step: when all its
+ * CTAs are done, seq advances. Every launch of a step must follow the one before it on one
+ * stream, and only the launch at position p - 1 writes the words a position-p launch waits on. */
+#define OTQ_TAGS_COUNTED 0
+#define OTQ_TAGS_STEPPED 1
 typedef struct otq_peer {
   int rank;
-  int world;             /* 2 .. 8 */
+  int world;             /* 1 .. 8 */
   int wait;              /* != 0: x is the previous projection's tagged output row */
-  int pad;
+  int tags;              /* OTQ_TAGS_COUNTED or OTQ_TAGS_STEPPED */
   int64_t delta[8];
   int* seq;
   int* done;
+  int step_pos;          /* stepped tags: this launch's position in its step */
+  int step_last;         /* stepped tags: != 0 for the step's last launch */
 } otq_peer;
 
 /* QACT + MM of one activation row against this rank's rows of a row-sharded projection

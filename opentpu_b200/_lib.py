@@ -25,8 +25,11 @@ class Proj(ctypes.Structure):
 
 class Peer(ctypes.Structure):
     """struct otq_peer of include/otq.h: the NVLink fan-out of otq_qmm_peer."""
-    _fields_ = [("rank", c_int), ("world", c_int), ("wait", c_int), ("pad", c_int),
-                ("delta", c_int64 * 8), ("seq", c_void_p), ("done", c_void_p)]
+    _fields_ = [("rank", c_int), ("world", c_int), ("wait", c_int), ("tags", c_int),
+                ("delta", c_int64 * 8), ("seq", c_void_p), ("done", c_void_p),
+                ("step_pos", c_int), ("step_last", c_int)]
+
+TAGS_COUNTED, TAGS_STEPPED = 0, 1
 
 
 class GemmProj(ctypes.Structure):

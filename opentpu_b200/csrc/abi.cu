@@ -298,8 +298,11 @@ int otq_qmm_peer(int fmt, int flags, const uint8_t* rows, int64_t rs, const uint
   if ((st = check_out(1, N, y, N, flags, nullptr))) return st;
   if (flags & (kMmAscale | kMmAcc)) return kErrArg;
   if (x == nullptr || ldx < K || ldx >= kStrideLimit) return kErrArg;
-  if (peer == nullptr || peer->world < 2 || peer->world > 8 || peer->rank < 0 ||
+  if (peer == nullptr || peer->world < 1 || peer->world > 8 || peer->rank < 0 ||
       peer->rank >= peer->world || peer->seq == nullptr || peer->done == nullptr)
+    return kErrArg;
+  if (peer->tags != OTQ_TAGS_COUNTED && peer->tags != OTQ_TAGS_STEPPED) return kErrArg;
+  if (peer->tags == OTQ_TAGS_STEPPED && (peer->step_pos < 0 || peer->step_pos >= 1023))
     return kErrArg;
   if (!aligned(y, 16) || !aligned(x, peer->wait ? 16 : 4)) return kErrAlign;
   if (!aligned(peer->seq, 4) || !aligned(peer->done, 4)) return kErrAlign;

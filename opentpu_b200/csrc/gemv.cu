@@ -168,11 +168,14 @@ __device__ __forceinline__ PArgs load_args(const Proj& d) {
 // output without a fence or a flag. The launch's last CTA advances the count (device scope).
 constexpr int kMaxPeers = 8;
 struct PeerArgs {
-  int rank, world, wait, pad;
+  int rank, world, wait, tags;
   int64_t delta[kMaxPeers];
-  int* seq;     // projections this rank has completed (this GPU's memory)
+  int* seq;     // counted tags: launches this rank has completed; stepped: steps completed
   int* done;    // CTAs of the current launch that have finished (zero between launches)
+  int step_pos, step_last;
 };
+
+constexpr uint32_t kStepTags = 1024;   // stepped tags: s * 1024 + position + 1
 
 template <int MAXP>
 struct Chain {
@@ -323,7 +326,8 @@ __device__ __forceinline__ void gemv_clear_activations(const PArgs& p, const GSm
 // gemv_clear_activations already ran for this projection.
 template <int FMT, int MT, bool PLAIN>
 __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSmem& s, int mt, int kp, int ap,
-                                      bool frag, bool cleared, int expect = -1, int* status = nullptr) {
+                                      bool frag, bool cleared, bool tagged = false, uint32_t expect = 0,
+                                      int* status = nullptr) {
   const int K = p.K, KG = K / 32;
   if (!cleared) gemv_clear_activations<FMT, MT, PLAIN>(p, s, mt, kp, ap, frag);
   if (p.x != nullptr) {
@@ -361,7 +365,7 @@ __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSme
               }
             }
           },
-          expect >= 0 ? reinterpret_cast<const unsigned long long*>(xr) : nullptr, expect, status);
+          tagged ? reinterpret_cast<const unsigned long long*>(xr) : nullptr, expect, status);
       if (threadIdx.x == 0) s.Sa[j] = r.S;
     }
   } else {
@@ -901,22 +905,35 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
   if (kCleared)
     gemv_clear_activations<FMT, MT, PLAIN>(d, s, min(MT, d.M),
                                            ((d.K + F::kElems - 1) / F::kElems) * F::kElems, L.ap, L.frag);
-  pdl_wait();   // the activations may come from the kernel launched before
+  // Stepped tags with a tagged input: the input's tags alone order this launch after the one
+  // before (whose CTAs all run: this launch started after each of them released it), so the
+  // kernel does not wait for that launch to finish. Otherwise the activations may come from the
+  // kernel launched before.
+  const bool stepped = MAXP == 1 && C.peer.world > 0 && C.peer.tags != 0;
+  if (!(stepped && C.peer.wait)) pdl_wait();
 
-  // output fan-out (single-projection launches of a row-sharded step): this rank's count of
-  // completed projections tags this launch's outputs and is the tag its tagged input must reach
+  // output fan-out (single-projection launches of a decode step): tagged output words, and the
+  // tag a tagged input must carry. Counted tags: this rank's count of completed launches (read
+  // after the wait above); stepped tags: the count of completed steps and this launch's position
+  // in the step (the count only changes at the end of a step's last launch, which starts after
+  // every other launch of the step has read it)
   __shared__ int64_t peer_delta[kMaxPeers];
   __shared__ int peer_count;
   Fan fan{0, 0, 0u, peer_delta};
-  int expect = -1;   // >= 0: x is a tagged row
+  bool tagged_in = false;
+  uint32_t expect = 0;
   if (MAXP == 1 && C.peer.world > 0) {
     if (threadIdx.x < kMaxPeers) peer_delta[threadIdx.x] = C.peer.delta[threadIdx.x];
     if (threadIdx.x == 0) peer_count = *reinterpret_cast<volatile int*>(C.peer.seq);
     __syncthreads();
     fan.world = C.peer.world;
     fan.rank = C.peer.rank;
-    fan.tag = static_cast<uint32_t>(peer_count + 1);
-    if (C.peer.wait) expect = peer_count;
+    const uint32_t base = stepped ? static_cast<uint32_t>(peer_count) * kStepTags +
+                                        static_cast<uint32_t>(C.peer.step_pos)
+                                  : static_cast<uint32_t>(peer_count);
+    fan.tag = base + 1u;
+    tagged_in = C.peer.wait != 0;
+    expect = base;
   }
 
   int f = 0;
@@ -924,7 +941,7 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
     if (pi > 0) grid_barrier(C.status);   // projection pi may read what pi - 1 wrote
     const int KCH = (d.K + F::kElems - 1) / F::kElems;
     gemv_load_activations<FMT, MT, PLAIN>(d, s, min(MT, d.M), KCH * F::kElems, L.ap, L.frag,
-                                          kCleared && pi == 0, pi == 0 ? expect : -1, C.status);
+                                          kCleared && pi == 0, pi == 0 && tagged_in, expect, C.status);
     // the next launch starts here: earlier (before the wait) or later (at exit) measured slower
     if (pi == count - 1) pdl_launch();
     const int mt = min(MT, d.M);
@@ -968,7 +985,8 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
     }
     if (MAXP > 1) __syncthreads();   // the next projection's activations overwrite shared memory
   }
-  if (MAXP == 1 && C.peer.world > 0) {   // the last CTA advances this rank's count
+  // the last CTA advances this rank's count (stepped tags: at the end of the step only)
+  if (MAXP == 1 && C.peer.world > 0 && (!stepped || C.peer.step_last)) {
     __syncthreads();
     if (threadIdx.x == 0 && atomicAdd(C.peer.done, 1) == static_cast<int>(gridDim.x) - 1) {
       *C.peer.done = 0;
@@ -1163,6 +1181,9 @@ int single_fmt(const MMParams& p, cudaStream_t stream, bool pdl, int dev) {
       for (int r = 0; r < kMaxPeers; ++r) C.peer.delta[r] = r < p.peer->world ? p.peer->delta[r] : 0;
       C.peer.seq = p.peer->seq;
       C.peer.done = p.peer->done;
+      C.peer.tags = p.peer->tags;
+      C.peer.step_pos = p.peer->step_pos;
+      C.peer.step_last = p.peer->step_last;
     }
     for (int attempt = 0; attempt < 2; ++attempt) {
       C.proj[0].cfg = cfg;

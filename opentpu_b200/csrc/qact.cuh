@@ -149,8 +149,9 @@ __device__ __forceinline__ void ld_tagged2(const unsigned long long* p, unsigned
                                            unsigned long long& b) {
   asm volatile("ld.volatile.global.v2.u64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
-__device__ __forceinline__ int tag_of(unsigned long long w) {
-  return static_cast<int>(static_cast<uint32_t>(w >> 32));
+// The word's tag is behind `expect` (serial-number order: tags may wrap around 2^32).
+__device__ __forceinline__ bool behind(unsigned long long w, uint32_t expect) {
+  return static_cast<int>(static_cast<uint32_t>(w >> 32) - expect) < 0;
 }
 
 template <int NT, class Emit4>
@@ -158,7 +159,7 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
                                                    int n, bool row_mode, uint32_t* segm,
                                                    uint32_t* red, Emit4 emit,
                                                    const unsigned long long* xt = nullptr,
-                                                   int expect = 0, int* status = nullptr) {
+                                                   uint32_t expect = 0, int* status = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NW = NT / 32;
   const int n4 = n >> 2;   // a multiple of 32: every lane of a warp runs the same iterations
@@ -193,7 +194,8 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
         // a tagged row (value in the low word, the writer's tag in the high word): wait,
         // bounded, until the four elements carry at least the expected tag
         for (uint32_t spin = 0;
-             min(min(tag_of(w[b][0]), tag_of(w[b][1])), min(tag_of(w[b][2]), tag_of(w[b][3]))) < expect;
+             behind(w[b][0], expect) || behind(w[b][1], expect) || behind(w[b][2], expect) ||
+             behind(w[b][3], expect);
              ++spin) {
           if (spin >= (1u << 22)) {
             if (status != nullptr) atomicOr(status, 1);   // a writer never arrived: not valid

@@ -20,6 +20,13 @@ kernel reads its input words until their tags show every rank's output has arriv
 (linear.qlinear_peer): no fence, flag or extra launch. gather="nccl" runs an NCCL all-gather
 after each projection instead.
 
+gather="tagged" runs a dependent chain of QACT + MM projections on one GPU with the same
+tagged words in its own memory (no fan-out): a launch reads its input words until their tags
+show the previous launch's output is complete instead of waiting for that launch to end. It is
+bit-identical to the plain chain but slower on a B200 (0.672 against 0.623 ms for the
+Qwen3-0.6B int8 step: the 8-byte tagged words cost more than the launch-end wait they remove),
+so one GPU keeps plain outputs by default.
+
 dependent=True (the default) chains the projections through their outputs the way a decode
 step does: each projection reads the first K outputs of the previous one (QKV's q part feeds O,
 O feeds GateUp, GateUp's gate part feeds Down, Down feeds the next layer's QKV and, after the
@@ -58,9 +65,12 @@ class DecodeChain:
                  std: float = 0.02, dependent: bool = True, chained: bool | None = None,
                  gather: str = "fused"):
         self.shape, self.world, self.rank, self.group, self.pdl = shape, world, rank, group, pdl
-        if gather not in ("fused", "nccl"):
-            raise ValueError("gather must be 'fused' or 'nccl'")
-        self.fused = world > 1 and gather == "fused"
+        if gather not in ("fused", "nccl", "tagged"):
+            raise ValueError("gather must be 'fused', 'nccl' or 'tagged'")
+        mm_only = fmt != "int4-g32" and head_fmt != "int4-g32"   # the tagged path is QACT + MM
+        if gather == "tagged" and (world > 1 or not (dependent and mm_only) or chained):
+            raise ValueError("gather='tagged' is a dependent QACT + MM chain on one GPU")
+        self.fused = (world > 1 and gather == "fused") or gather == "tagged"
         self.dependent = dependent
         # chained: the whole step as one persistent launch (linear.qlinear_chain). Measured on
         # a B200 it is slower today than one launch a projection (1.12 vs 0.61 ms for the
@@ -124,28 +134,34 @@ class DecodeChain:
 
     def _symmetric_outputs(self):
         """Every projection's full output row as tagged words ([N, 2] float32: value, tag bits)
-        in one symmetric buffer (16-byte aligned slots); this rank's projection count and the
-        launches' CTA count in ordinary device memory. All zero before the first launch."""
-        import torch.distributed as dist
-        import torch.distributed._symmetric_memory as symm
+        in one buffer (16-byte aligned slots): symmetric with world > 1, plain device memory on
+        one GPU; this rank's step count and the last launch's CTA count in ordinary device
+        memory. All zero before the first launch. The launches use stepped tags: position i of
+        the step waits on the tags of position i - 1's output, not on that launch's end."""
         from . import _lib as L
         offs, tot = [], 0
         for _, N, _, _ in self.plan:
             offs.append(tot)
             tot += 2 * (-(-N // 2) * 2)   # N words of 8 bytes, rounded to 16 bytes
-        try:
-            symm.set_backend("CUDA")
-        except Exception:
-            pass   # already chosen by an earlier allocation
-        buf = symm.empty(tot, dtype=torch.float32, device="cuda")
-        buf.zero_()
-        group = self.group if self.group is not None else dist.group.WORLD
-        handle = symm.rendezvous(buf, group)
-        torch.cuda.synchronize()
-        dist.barrier(group=group)
-        ptrs = handle.buffer_ptrs
+        if self.world > 1:
+            import torch.distributed as dist
+            import torch.distributed._symmetric_memory as symm
+            try:
+                symm.set_backend("CUDA")
+            except Exception:
+                pass   # already chosen by an earlier allocation
+            buf = symm.empty(tot, dtype=torch.float32, device="cuda")
+            buf.zero_()
+            group = self.group if self.group is not None else dist.group.WORLD
+            handle = symm.rendezvous(buf, group)
+            torch.cuda.synchronize()
+            dist.barrier(group=group)
+            ptrs = handle.buffer_ptrs
+        else:
+            buf = torch.zeros(tot, dtype=torch.float32, device="cuda")
+            handle, ptrs = None, [buf.data_ptr()]
         self._symm = (buf, handle)
-        self.counters = torch.zeros(2, dtype=torch.int32, device="cuda")   # count, done CTAs
+        self.counters = torch.zeros(2, dtype=torch.int32, device="cuda")   # steps, done CTAs
         self.full, self.peers = [], []
         for i, (o, (_, N, _, _)) in enumerate(zip(offs, self.plan)):
             words = buf[o:o + 2 * N].view(N, 2)
@@ -160,6 +176,9 @@ class DecodeChain:
                 pr.delta[r] = ptrs[r] - ptrs[self.rank]
             pr.seq = self.counters.data_ptr()
             pr.done = self.counters.data_ptr() + 4
+            pr.tags = L.TAGS_STEPPED
+            pr.step_pos = i
+            pr.step_last = int(i == len(self.plan) - 1)
             self.peers.append(pr)
 
     @property
