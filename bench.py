@@ -383,17 +383,19 @@ def main():
         ms = float(t.item())
     value = total_bytes / (ms * 1e-3) / 1e9
 
-    # the dominant kernel alone: the LM head GEMV (this rank's rows), 20 launches in a graph
+    # the dominant kernel alone: the LM head GEMV (this rank's rows), 20 launches in a graph,
+    # launched as in the step (programmatic dependent launch: a launch's CTAs start on SMs the
+    # one before has left)
     head, hx = chain.weights[-1], chain.inputs[shape.hidden]
     hy = torch.empty((1, head.N), device="cuda")
     hg = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         for _ in range(3):
-            linear.qlinear(hx, head, out=hy)
+            linear.qlinear(hx, head, out=hy, pdl=True)
     torch.cuda.synchronize()
     with torch.cuda.graph(hg, stream=stream):
         for _ in range(20):
-            linear.qlinear(hx, head, out=hy)
+            linear.qlinear(hx, head, out=hy, pdl=True)
     with torch.cuda.stream(stream):
         hg.replay()
         torch.cuda.synchronize()
