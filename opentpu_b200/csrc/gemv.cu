@@ -335,7 +335,7 @@ __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSme
       const float* xr = p.x + static_cast<int64_t>(j) * p.ldx;
       const bool x4 = (reinterpret_cast<uintptr_t>(xr) & 15u) == 0;
       uint8_t* arow = s.act + static_cast<size_t>(j) * ap;
-      QactRowResult r = qact_row4<kThreads>(
+      qact_row4<kThreads>(
           xr, x4, s.xs, K, p.row_mode != 0, s.seg, s.qred,
           [&](int i, int q0, int q1, int q2, int q3, int d) {
             const int G = i >> 3;
@@ -365,9 +365,10 @@ __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSme
               }
             }
           },
-          tagged ? reinterpret_cast<const unsigned long long*>(xr) : nullptr, expect, status);
-      if (threadIdx.x == 0) s.Sa[j] = r.S;
+          tagged ? reinterpret_cast<const unsigned long long*>(xr) : nullptr, expect, status,
+          s.Sa + j);
     }
+    return;   // qact_row4 ends with a barrier, after every write above (Sa included)
   } else {
     for (int j = 0; j < mt; ++j) {
       const int8_t* qr = p.q + static_cast<int64_t>(j) * p.ldq;

@@ -159,7 +159,8 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
                                                    int n, bool row_mode, uint32_t* segm,
                                                    uint32_t* red, Emit4 emit,
                                                    const unsigned long long* xt = nullptr,
-                                                   uint32_t expect = 0, int* status = nullptr) {
+                                                   uint32_t expect = 0, int* status = nullptr,
+                                                   float* S_out = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NW = NT / 32;
   const int n4 = n >> 2;   // a multiple of 32: every lane of a warp runs the same iterations
@@ -222,26 +223,19 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
   tmax = __reduce_max_sync(0xFFFFFFFFu, tmax);
   if (lane == 0) red[warp] = tmax;
   __syncthreads();
-  if (warp == 0) {
-    uint32_t m = lane < NW ? red[lane] : 0u;
-    m = __reduce_max_sync(0xFFFFFFFFu, m);
-    if (lane == 0) {
-      float S = 0.0f, inv = 0.0f;
-      if (m != 0u) {
-        const float amax = __uint_as_float(m);
-        S = fmul(amax, __uint_as_float(kInv127Bits));
-        inv = fmul(127.0f, recip(amax));
-      }
-      red[NW] = __float_as_uint(S);
-      red[NW + 1] = __float_as_uint(inv);
-      red[NW + 2] = m;
-    }
-  }
-  __syncthreads();
+  // every warp reduces the warp maxima and derives the scales itself: one barrier, not two
+  uint32_t m = lane < NW ? red[lane] : 0u;
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
   QactRowResult r;
-  r.S = __uint_as_float(red[NW]);
-  r.inv = __uint_as_float(red[NW + 1]);
-  r.amax_bits = red[NW + 2];
+  r.S = 0.0f;
+  r.inv = 0.0f;
+  r.amax_bits = m;
+  if (m != 0u) {
+    const float amax = __uint_as_float(m);
+    r.S = fmul(amax, __uint_as_float(kInv127Bits));
+    r.inv = fmul(127.0f, recip(amax));
+  }
+  if (S_out != nullptr && tid == 0) *S_out = r.S;   // ordered before its readers by the barrier below
   for (int i = tid; i < n4; i += NT) {
     const float4 v = *reinterpret_cast<const float4*>(xs + 4 * i);
     const int d = row_mode ? 0 : group_offset(segm[i >> 3], r.amax_bits);
