@@ -137,9 +137,18 @@ __global__ void __launch_bounds__(kThreads) linear_g32_kernel(const G32Params p)
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int m0 = 0; m0 < p.M; m0 += MT) {
     const int mt = min(MT, p.M - m0);
-    for (int j = 0; j < mt; ++j)
-      for (int i = threadIdx.x; i < K; i += kThreads)
-        xs[j * K + i] = __ldcg(p.x + static_cast<int64_t>(m0 + j) * p.ldx + i);
+    if ((reinterpret_cast<uintptr_t>(p.x) & 15u) == 0 && (p.ldx & 3) == 0) {
+      // 16-byte loads, every one of the block's loads issued before the shared-memory stores
+      for (int j = 0; j < mt; ++j) {
+        const float4* xr = reinterpret_cast<const float4*>(p.x + static_cast<int64_t>(m0 + j) * p.ldx);
+        for (int i = threadIdx.x; i < (K >> 2); i += kThreads)
+          reinterpret_cast<float4*>(xs + j * K)[i] = __ldcg(xr + i);
+      }
+    } else {
+      for (int j = 0; j < mt; ++j)
+        for (int i = threadIdx.x; i < K; i += kThreads)
+          xs[j * K + i] = __ldcg(p.x + static_cast<int64_t>(m0 + j) * p.ldx + i);
+    }
     __syncthreads();
     for (int64_t t = wfirst; t < ntasks; t += wstride) {
       const int64_t n = t * R + r;
@@ -229,15 +238,37 @@ __global__ void __launch_bounds__(kThreads) linear_g32_row_kernel(const G32Param
   if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) * 32 < p.N)
     prefetch_rows_l2(p, static_cast<int64_t>(blockIdx.x) * 32, 32);
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  for (int i = threadIdx.x; i < K; i += kThreads) {
-    const float v = __ldcg(p.x + i);
-    xs[i] = __fmul_rn(v, __int_as_float((127 - 4 * (i & 3)) << 23));   // x * 2^(-4 (i % 4))
-  }
-  for (int g = warp; g < G; g += kThreads / 32) {
-    float v = __ldcg(p.x + g * 32 + lane);
+  if ((reinterpret_cast<uintptr_t>(p.x) & 15u) == 0) {
+    // one pass over x, four elements a thread: x' and, over the 8 lanes holding a group, the
+    // group's sum (x is read from L2 once; K is a multiple of 32, so groups never straddle a
+    // warp and the loop bound is warp-uniform)
+    const int K4 = K >> 2;
+    for (int base = 0; base < K4; base += kThreads) {
+      const int i = base + threadIdx.x;
+      const bool in = i < K4;
+      const float4 v = in ? __ldcg(reinterpret_cast<const float4*>(p.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float sum = __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w));
+      sum = __fadd_rn(sum, __shfl_xor_sync(0xFFFFFFFFu, sum, 1));
+      sum = __fadd_rn(sum, __shfl_xor_sync(0xFFFFFFFFu, sum, 2));
+      sum = __fadd_rn(sum, __shfl_xor_sync(0xFFFFFFFFu, sum, 4));
+      if (in) {
+        *reinterpret_cast<float4*>(xs + 4 * i) =
+            make_float4(v.x, __fmul_rn(v.y, 0.0625f), __fmul_rn(v.z, 0.00390625f),
+                        __fmul_rn(v.w, 0.000244140625f));   // x * 2^(-4 (k % 4)), exact
+        if ((lane & 7) == 0) gsum[i >> 3] = sum;
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < K; i += kThreads) {
+      const float v = __ldcg(p.x + i);
+      xs[i] = __fmul_rn(v, __int_as_float((127 - 4 * (i & 3)) << 23));   // x * 2^(-4 (i % 4))
+    }
+    for (int g = warp; g < G; g += kThreads / 32) {
+      float v = __ldcg(p.x + g * 32 + lane);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-    if (lane == 0) gsum[g] = v;
+      for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+      if (lane == 0) gsum[g] = v;
+    }
   }
   __syncthreads();
   const int g0 = warp * G / 8, g1 = (warp + 1) * G / 8;
