@@ -60,8 +60,9 @@ def peaks():
 
 
 def profile_run(what: str):
-    """A few launches for an ncu capture: the LM head GEMV alone, two decode steps, or three
-    grouped prefill launches of one SmolLM3-3B layer."""
+    """A few launches for an ncu capture: the LM head GEMV alone, two decode steps, three
+    grouped prefill launches of one SmolLM3-3B layer, or five int4-g32 GEMVs of one activation
+    row over a 65536 x 4096 matrix (144 MB of codes and scales, more than L2)."""
     import torch
     from opentpu_b200 import linear
     from opentpu_b200.decode import DecodeChain
@@ -73,6 +74,14 @@ def profile_run(what: str):
         del W
         x = torch.randn((1, shape.hidden), device="cuda")
         y = torch.empty((1, shape.vocab), device="cuda")
+        for _ in range(5):
+            linear.qlinear(x, w, out=y)
+    elif what == "g32":
+        W = torch.randn((65536, 4096), device="cuda") * 0.02
+        w = linear.PackedWeight.from_float(W, "int4-g32")
+        del W
+        x = torch.randn((1, 4096), device="cuda")
+        y = torch.empty((1, 65536), device="cuda")
         for _ in range(5):
             linear.qlinear(x, w, out=y)
     elif what == "prefill":
@@ -333,7 +342,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["head", "step", "prefill"])
+    ap.add_argument("--profile", choices=["head", "step", "prefill", "g32"])
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-4bit", action="store_true")
     args = ap.parse_args()
