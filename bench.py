@@ -1,32 +1,40 @@
-"""Benchmark of the quantized linear layer's decode hot path.
+"""Benchmark of the quantized linear layer's hot path.
 
-One step = one decode token through every quantized projection of a Qwen3-0.6B-shaped decoder
-(28 layers x q, k, v, o, gate, up, down, then the 151936 x 1024 LM head; int8 per-row weights
-from N(0, 0.02), the first input N(0, 1)). q/k/v and gate/up share their input and QACT range,
-so each group is one launch: 113 fused QACT+MM launches a step, each reading the previous
-launch's output as a decode step does (opentpu_b200.decode.DecodeChain, dependent), then the
-greedy token (device argmax of the logits), replayed as one CUDA graph. The weights (598 MB)
-exceed the 126 MB L2, so each step streams them from HBM.
-
---profile head|step|prefill runs a few launches and exits (the command the ncu summaries under
-profiles/ were captured with).
-
-The line's "decode_4bit" object is BASELINE configuration 3: the same step with int4-g32 layers
-and an int8-row head (weight-only 4-bit GEMVs on fp32 activations).
-
-The line's "prefill" object is BASELINE configuration 4 (prefill TFLOP/s): 36 SmolLM3-3B-shaped
-layers of int8-row weights (2.8 GB) against 512 bf16 tokens, one grouped tcgen05 GEMM launch
-(opentpu_b200.linear.gemm_w8a16_group) a layer, the 36 launches one CUDA graph a step; its
-roofline is against the measured bf16 tensor peak.
+Main line (configuration 2): one step = one decode token through every quantized projection of
+a Qwen3-0.6B-shaped decoder (28 layers x q, k, v, o, gate, up, down, then the 151936 x 1024 LM
+head; int8 per-row weights from N(0, 0.02), the first input N(0, 1)). q/k/v and gate/up share
+their input and QACT range, so each group is one launch: 113 fused QACT+MM launches a step, each
+reading the previous launch's output as a decode step does (opentpu_b200.decode.DecodeChain,
+dependent), then the greedy token (device argmax of the logits), replayed as one CUDA graph.
+The weights (598 MB) exceed the 126 MB L2, so each step streams them from HBM.
 
 metric: decode weight GB/s (whole job) with tok/s = steps / s beside it. With --gpus N each
 projection's output rows are split over the N ranks (the reference's Weight(shard=0)) and every
 projection's output is assembled on every rank (the reference's GATHER) inside the GEMV itself:
 each rank stores its rows' tagged 8-byte words into every rank's copy over NVLink and the next
-projection reads them when their tags arrive (DecodeChain gather="fused").
+projection reads them when their tags arrive (DecodeChain gather="fused"). After timing, rank 0
+replays the same seeded step on one GPU and compares the logits bit for bit ("parity").
 
---impl reference times the reference's CPU algorithm (the numpy port under oracle/, the same
-arithmetic as the reference's MM) on a bounded sample of the same step.
+Objects of the same line:
+- "roofline": the dominant kernel, the 112 layer-projection launches of a step (95 % of its
+  time), timed as their own graph with CUDA events; "roofline_head" the LM-head launch alone.
+- "e2e": a closed greedy loop through the public API (DecodeChain.run_host): each step copies
+  its input vector from pinned host memory (the row of a host table picked by the previous
+  token), replays the step, copies the token back, waits for it and reads it on the host.
+- "cpu_baseline": the reference's exact MM algorithm (oracle port, all host cores) on a bounded
+  sample; "cpu_baseline_blas": the reference's weight-only float path `deq @ x` (numpy fp32
+  BLAS, all host cores) on a bounded sample.
+- "config1": BASELINE configuration 1 (1024 x 1024 int8 per-row GEMV) as a latency, over a
+  rotating pool of 256 distinct weight copies (257 MB > 2 x L2) and L2-resident.
+- "decode_4bit": configuration 3 (int4-g32 layers, int8-row head) with its own roofline, CPU
+  baseline and closed-loop e2e.
+- "prefill": configuration 4 (36 SmolLM3-3B-shaped int8-row layers, 512 bf16 tokens, tcgen05
+  GEMM); with N > 1 each projection's rows are sharded and its output all-gathered (NCCL) in the
+  timed graph, and rank 0 checks layer 0 against the unsharded GEMM within the tolerance.
+
+--profile head|step|prefill|g32 runs a few launches and exits (the commands the ncu summaries
+under profiles/ were captured with). --impl reference times the reference's CPU algorithm (the
+numpy port under oracle/, the same arithmetic as the reference's MM) on a bounded sample.
 """
 from __future__ import annotations
 
@@ -49,16 +57,582 @@ from opentpu_b200 import workloads as WL  # noqa: E402
 
 METRIC = "decode weight GB/s"
 UNIT = "GB/s"
+PREFILL_TOKENS = 512
 
 
 def peaks():
+    """(HBM GB/s, bf16 burst TFLOP/s, kind): MEASURED_PEAKS.json, else the pool's fallback."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
 
 
+def host_threads():
+    """Every host core for the CPU baselines, whatever OMP_NUM_THREADS torchrun set: (the
+    threadpoolctl context or None, the thread count)."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(limits=n), n
+    except Exception:
+        return None, 1
+
+
+def threads_used():
+    try:
+        from threadpoolctl import threadpool_info
+        return max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:
+        return 1
+
+
+class Clocks:
+    """nvidia-smi sampling while the timed regions run (SM clock, throttle reasons). The first
+    sample is awaited before the timed region starts."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5 and self.proc.poll() is None:
+                time.sleep(0.02)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.15)   # one more sample after the last timed kernel
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        mhz = [v for v in (num(r[1]) for r in self.rows if len(r) > 1) if v is not None]
+        mx = [v for v in (num(r[2]) for r in self.rows if len(r) > 2) if v is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------------------ timing helpers
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def graph_ms(graph, stream, reps: int, world: int) -> float:
+    """Milliseconds a replay of `graph` (CUDA events on its stream, max over ranks)."""
+    import torch
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return max_over_ranks(e0.elapsed_time(e1) / reps, world)
+
+
+def capture(fn, stream, warm: int = 2):
+    """A CUDA graph of fn() on `stream` (after `warm` eager runs)."""
+    import torch
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def read_traffic(name: str, world: int):
+    """dram bytes per launch from a committed ncu summary (one GPU only), or None."""
+    tp = ROOT / "profiles" / name
+    if tp.exists() and world == 1:
+        for line in tp.read_text().splitlines():
+            if line.startswith("| dram_bytes_per_launch |"):
+                return int(line.split("|")[2])
+    return None
+
+
+# ------------------------------------------------------------------------------ CPU baselines
+def cpu_exact_sample(budget_s: float = 10.0, shape=WL.QWEN3_0_6B):
+    """The oracle's exact decode GEMV (the reference's MM algorithm) on every host core over a
+    bounded sample of the step's projections: (GB/s of weight bytes, description, threads)."""
+    from oracle import fp32 as F
+    from oracle import mx as X
+    lim, n = host_threads()
+    try:
+        rng = np.random.default_rng(0)
+        shapes = [(N, K) for _, N, K in shape.projections()] + [(16384, shape.hidden)]
+        mats = []
+        for N, K in shapes:
+            W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+            q, s = X.quantize_rows_rsc(W)
+            mats.append((q, s, rng.standard_normal(K).astype(np.float32), K))
+        nbytes = sum(q.shape[0] * (q.shape[1] + 4) for q, _, _, _ in mats)
+        done, t0 = 0, time.perf_counter()
+        while True:
+            for q, s, x, K in mats:
+                qa, Sa, da = F.quantize_rows(x[None, :], 32)
+                X.mm(qa, Sa, da, q, s, "int8", K, rsc=True)
+            done += 1
+            el = time.perf_counter() - t0
+            if el > budget_s or done >= 50:
+                break
+        th = threads_used()
+    finally:
+        if lim is not None:
+            lim.restore_original_limits()
+    desc = (f"{done} passes over 1 layer (7 projections) + a 16384-row head slice "
+            f"({nbytes / 1e6:.1f} MB of int8 rows), exact MM port (QACT + integer MM), numpy, "
+            f"{n} host threads allowed")
+    return done * nbytes / el / 1e9, desc, th
+
+
+def cpu_blas_sample(fmt: str = "int8-row", budget_s: float = 4.0, shape=WL.QWEN3_0_6B):
+    """The reference's weight-only float path, `deq @ x` in numpy fp32 BLAS (reference.py:14-17
+    on quant.quantize's deq), on every host core: one layer's seven projections + a 16384-row
+    head slice, GB/s of the format's packed weight bytes. (value, description, threads)."""
+    from oracle import survey as SV
+    lim, n = host_threads()
+    try:
+        rng = np.random.default_rng(0)
+        shapes = [(N, K, fmt) for _, N, K in shape.projections()] + [(16384, shape.hidden,
+                                                                      "int8-row")]
+        mats, nbytes = [], 0
+        for N, K, f in shapes:
+            W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+            if f == "int4-g32":
+                _, _, deq = SV.quantize_g32(W)
+                nbytes += N * K // 2 + N * K // 32 * 2
+            else:
+                sw = np.abs(W).max(1, keepdims=True) / 127
+                deq = (np.rint(W / sw) * sw).astype(np.float32)
+                nbytes += N * (K + 4)
+            mats.append((np.ascontiguousarray(deq), rng.standard_normal(K).astype(np.float32)))
+        done, t0 = 0, time.perf_counter()
+        while True:
+            for d, x in mats:
+                d @ x
+            done += 1
+            el = time.perf_counter() - t0
+            if el > budget_s or done >= 2000:
+                break
+        th = threads_used()
+    finally:
+        if lim is not None:
+            lim.restore_original_limits()
+    desc = (f"{done} passes of `deq @ x` (numpy fp32 BLAS) over 1 layer ({fmt}) + a 16384-row "
+            f"int8-row head slice, {nbytes / 1e6:.1f} MB of packed weights a pass")
+    return done * nbytes / el / 1e9, desc, th
+
+
+def prefill_cpu_sample(budget_s: float = 6.0):
+    """The oracle's float64 `deq @ x` (oracle/prefill.py) on every host core over one 2048 x
+    2048 projection at 512 tokens: (TFLOP/s, description, threads)."""
+    from oracle import prefill as PF
+    lim, n = host_threads()
+    try:
+        rng = np.random.default_rng(0)
+        K = N = 2048
+        x = PF.bf16_round(rng.standard_normal((PREFILL_TOKENS, K)).astype(np.float32))
+        rows = rng.integers(-127, 128, (N, K), dtype=np.int8).view(np.uint8)
+        srows = (rng.random(N).astype(np.float32) * 1e-3).view(np.uint8).reshape(N, 4)
+        done, t0 = 0, time.perf_counter()
+        while True:
+            PF.gemm_w8a16(x, rows, srows, K)
+            done += 1
+            el = time.perf_counter() - t0
+            if el > budget_s or done >= 20:
+                break
+        th = threads_used()
+    finally:
+        if lim is not None:
+            lim.restore_original_limits()
+    flops = 2.0 * PREFILL_TOKENS * N * K
+    desc = (f"{done} x one 2048x2048 projection at 512 tokens, float64 numpy (oracle, also "
+            "forms the error bound |x| @ |deq|^T)")
+    return done * flops / el / 1e12, desc, th
+
+
+# ------------------------------------------------------------------------------ decode objects
+def layers_roofline(chain, world, reps, hbm, peak_kind, kernel, traffic_name=None):
+    """The step's layer projections (all launches but the head's and the argmax) as their own
+    graph, launched as in the step: bytes (weights + scales + x + y) / CUDA-event time."""
+    import torch
+    from opentpu_b200 import linear
+    items = list(zip(chain.x_of[:-1], chain.weights[:-1], chain.outs[:-1]))
+
+    def run():
+        for x, w, y in items:
+            linear.qlinear(x, w, out=y, pdl=chain.pdl)
+    g = capture(run, chain.stream)
+    graph_ms(g, chain.stream, 3, world)
+    ms = graph_ms(g, chain.stream, reps, world)
+    nbytes = sum(w.stream_bytes + 4 * w.K + 4 * w.N for _, w, _ in items)
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    del g
+    torch.cuda.synchronize()
+    return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm, "traffic": read_traffic(traffic_name, world)
+            if traffic_name else None,
+            "kernel": kernel, "launches_per_step": len(items), "bytes_per_step": nbytes,
+            "us_per_step": ms * 1e3, "us_per_launch": ms * 1e3 / len(items),
+            "peak_kind": f"{peak_kind} (copy)"}
+
+
+def head_roofline(chain, stream, world, hbm, peak_kind):
+    """The LM-head launch alone (this rank's rows), 20 launches in a graph, launched as in the
+    step (programmatic dependent launch)."""
+    import torch
+    from opentpu_b200 import linear
+    head, hx = chain.weights[-1], chain.inputs[chain.shape.hidden]
+    hy = torch.empty((1, head.N), device="cuda")
+
+    def run():
+        for _ in range(20):
+            linear.qlinear(hx, head, out=hy, pdl=True)
+    g = capture(run, stream, warm=1)
+    graph_ms(g, stream, 1, world)
+    ms = graph_ms(g, stream, 5, world) / 20
+    nbytes = head.stream_bytes + head.K * 4 + head.N * 4
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    del g
+    return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm,
+            "traffic": read_traffic("gemv_kernel_lm_head_int8row_151936x1024_m1.md", world),
+            "kernel": f"gemv_kernel (LM head launch, {head.N}x{head.K} {head.fmt}, M=1)",
+            "bytes_per_launch": nbytes, "us_per_launch": ms * 1e3,
+            "peak_kind": f"{peak_kind} (copy)"}
+
+
+def closed_loop(chain, n: int, world: int):
+    """Greedy decode through the public API from host buffers: each step's input is the row of
+    a pinned host table picked by the previous step's token (copied to the device), the step's
+    graph replays, the token comes back to pinned host memory, the host waits for it and reads
+    it. Returns (wall ms a token, max over ranks; h2d bytes, d2h bytes, tokens seen)."""
+    import torch
+    K = chain.plan[0][2]
+    table = torch.randn((64, K), generator=torch.Generator().manual_seed(5)).pin_memory()
+    tok_host = torch.zeros(1, dtype=torch.int64).pin_memory()
+    tok, seen = 0, []
+    for _ in range(3):
+        chain.run_host({K: table[tok % 64]}, tok_host)
+        chain.stream.synchronize()
+        tok = int(tok_host[0])
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(n):
+        chain.run_host({K: table[tok % 64]}, tok_host)
+        chain.stream.synchronize()
+        tok = int(tok_host[0])
+        seen.append(tok)
+    wall = (time.perf_counter() - t0) / n * 1e3
+    return max_over_ranks(wall, world), K * 4, 8, seen
+
+
+def config1(world: int, reps: int):
+    """W N(0, 0.02) [1024, 1024] -> int8 per row + fp32 scale, x
+    N(0, 1) [1024], M = 1, as a latency. Rotating pool: 256 distinct copies of the packed
+    weight (257 MB, more than twice the 126 MB L2), one launch each, in one graph; L2-resident:
+    one copy launched 256 times. Bytes a launch = 1 060 864 (W + Sw + x + y)."""
+    import torch
+    from opentpu_b200 import linear
+    W, x = WL.gemv_config1(0)
+    w0 = linear.PackedWeight.from_float(torch.from_numpy(W).cuda(), "int8-row")
+    xs = torch.from_numpy(x).cuda().reshape(1, -1)
+    pool = [linear.PackedWeight("int8-row", w0.N, w0.K, w0.rows.clone(), w0.srows.clone())
+            for _ in range(256)]
+    y = torch.empty((1, 1024), device="cuda")
+    stream = torch.cuda.Stream()
+    nbytes = 1024 * 1024 + 4096 + 4096 + 4096
+    out = {}
+    for name, ws in (("pool", pool), ("l2_resident", [w0] * 256)):
+        def run(ws=ws):
+            for w in ws:
+                linear.qlinear(xs, w, out=y, pdl=True)
+        g = capture(run, stream, warm=1)
+        graph_ms(g, stream, 2, world)
+        ms = graph_ms(g, stream, reps, world) / len(ws)
+        out[name] = {"us_per_gemv": ms * 1e3, "GB/s": nbytes / (ms * 1e-3) / 1e9}
+        del g
+    del pool
+    torch.cuda.synchronize()
+    return {"metric": "1024x1024 int8-row GEMV latency", "unit": "us",
+            "value": out["pool"]["us_per_gemv"], "higher_is_better": False,
+            "bytes_per_gemv": nbytes, **out,
+            "config": {"workload": "BASELINE configuration 1: W N(0,0.02) 1024x1024 int8 per "
+                                   "row + fp32 scale, x N(0,1) fp32 [1024], seed 0, M=1",
+                       "pool": "256 distinct packed copies (257 MB > 2 x 126 MB L2), one "
+                               "launch each in one CUDA graph (PDL)",
+                       "l2_resident": "one copy launched 256 times"}}
+
+
+def decode_4bit(args, world, rank, group, hbm, peak_kind):
+    """the Qwen3-0.6B step with int4-g32 layers (fp16 group scales,
+    weight-only, fp32 activations) and the int8-row head."""
+    import torch
+    from opentpu_b200.decode import DecodeChain
+    shape = WL.QWEN3_0_6B
+    # int4-g32 is weight-only (no MM, so no fused gather): NCCL all-gathers with world > 1
+    c4 = DecodeChain(shape, fmt="int4-g32", head_fmt="int8-row", world=world, rank=rank,
+                     group=group, gather="nccl")
+    c4.capture()
+    c4.replay(args.warmup)
+    torch.cuda.synchronize()
+    n4 = max(10, args.steps)
+    ms4 = graph_ms(c4.graph, c4.stream, n4, world)
+    roof = None
+    if world == 1:
+        roof = layers_roofline(c4, world, max(10, args.steps), hbm, peak_kind,
+                               "linear_g32_row_kernel / linear_g32_kernel (the 112 layer "
+                               "projections of a step, int4-g32, M=1)")
+    e2e_ms, h2d, d2h, _ = closed_loop(c4, max(10, min(args.steps, 200)), world)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, desc, th = cpu_blas_sample("int4-g32")
+        cpu = {"value": v, "unit": UNIT, "cores": th, "kind": "port", "sample": desc}
+    out = {"metric": METRIC, "value": c4.weight_bytes / (ms4 * 1e-3) / 1e9, "unit": UNIT,
+           "ms_per_step": ms4, "tok_s": 1e3 / ms4, "steps": n4,
+           "config": {"workload": "Qwen3-0.6B-shaped decode step, layers int4 group-32 fp16 "
+                                  "scales (weight-only, fp32 activations), 151936x1024 "
+                                  "int8-row LM head, M=1 (BASELINE configuration 3)",
+                      "weights_bytes_per_step": c4.weight_bytes,
+                      "parallelism": f"row-shard x{world}" + (" + NCCL all-gather per "
+                                                             "projection" if world > 1 else "")},
+           "roofline": roof, "cpu_baseline": cpu,
+           "e2e": {"value": c4.weight_bytes / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
+                   "ms_per_token": e2e_ms, "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h, "api": "DecodeChain.run_host, closed loop"},
+           "gpu_launches": c4.launches * n4}
+    c4.release()
+    del c4
+    torch.cuda.synchronize()
+    return out
+
+
+def parity_vs_one_gpu(chain, world, rank):
+    """Rank 0: the same seeded step replayed unsharded on one GPU; the sharded step's logits and
+    token compared bit for bit (the other ranks wait at a barrier)."""
+    import torch
+    from opentpu_b200.decode import DecodeChain
+    res = None
+    torch.cuda.synchronize()
+    if rank == 0:
+        one = DecodeChain(chain.shape, fmt=chain.plan[0][3], head_fmt=chain.plan[-1][3], seed=0)
+        one.step_eager()
+        torch.cuda.synchronize()
+        a = chain.logits().float().contiguous().cpu().numpy().view(np.uint32)
+        b = one.logits().float().contiguous().cpu().numpy().view(np.uint32)
+        same = bool(np.array_equal(a, b))
+        res = {"vs_1gpu": "bit-identical" if same else "differs",
+               "token": int(chain.token[0]), "token_1gpu": int(one.token[0]),
+               "logits_differing": int((a != b).sum())}
+        one.release()
+        del one
+        torch.cuda.synchronize()
+    barrier(world)
+    return res
+
+
+# ------------------------------------------------------------------------------ prefill
+def prefill_layer(shape, world, rank, gen, xs=None):
+    """One layer's seven projections for the prefill GEMM (BASELINE configuration 4): int8-row
+    weights (uniform int8 rows, Sw ~ 1e-3: the GEMM's cost does not depend on the values),
+    drawn whole from a generator every rank seeds alike and cut to this rank's row shard, bf16
+    activations N(0, 1) [512, K] (shared across layers when xs is given) and fp32 outputs.
+    Returns (gemm_w8a16_group items, the full weights' (rows, Sw) for a parity check)."""
+    import torch
+    from opentpu_b200 import linear
+    items, full = [], []
+    for i, (_, N, K) in enumerate(shape.projections()):
+        n = N // world
+        rows = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda",
+                             generator=gen).view(torch.uint8)
+        sw = torch.rand(N, device="cuda", generator=gen) * 1e-3 + 1e-4
+        mine_r = rows[rank * n:(rank + 1) * n].clone()
+        mine_s = sw[rank * n:(rank + 1) * n].clone()
+        w = linear.PackedWeight("int8-row", n, K, mine_r, mine_s.view(torch.uint8).reshape(n, 4))
+        x = xs[i] if xs is not None else torch.randn((PREFILL_TOKENS, K), device="cuda",
+                                                      generator=gen).to(torch.bfloat16)
+        y = torch.empty((PREFILL_TOKENS, n), device="cuda")
+        items.append((x, w, y, False))
+        full.append((rows, sw))
+    return items, full
+
+
+def prefill_bench(args, world, rank, local, group, steps, warmup):
+    """BASELINE configuration 4 on this rank: 36 SmolLM3-3B layers, each one grouped launch of
+    its seven projections (row shard 1/world of each; with world > 1 an NCCL all-gather of each
+    projection's output follows, in the same graph), one CUDA graph a step."""
+    import torch
+    import torch.distributed as dist
+    from opentpu_b200 import linear
+    shape = WL.SMOLLM3_3B
+    gen = torch.Generator(device="cuda").manual_seed(1234)
+    first, full0 = prefill_layer(shape, world, rank, gen)
+    xs = [it[0] for it in first]
+    layers = [first] + [prefill_layer(shape, world, rank, gen, xs)[0]
+                        for _ in range(shape.layers - 1)]
+    flops_layer = sum(2.0 * PREFILL_TOKENS * it[1].N * it[1].K for it in first)
+    gathered = [[torch.empty((world, PREFILL_TOKENS, it[1].N), device="cuda") for it in items]
+                for items in layers] if world > 1 else None
+
+    def layer(li):
+        linear.gemm_w8a16_group(layers[li])
+        if world > 1:
+            for it, g in zip(layers[li], gathered[li]):
+                dist.all_gather_into_tensor(g, it[2], group=group)
+
+    def step():
+        for li in range(shape.layers):
+            layer(li)
+    stream = torch.cuda.Stream()
+    g = capture(step, stream, warm=1)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            g.replay()
+    torch.cuda.synchronize()
+    ms = graph_ms(g, stream, steps, world)
+    # the GEMM launches alone (no all-gather): the kernel's roofline
+    gk = capture(lambda: [linear.gemm_w8a16_group(items) for items in layers], stream, warm=1)
+    graph_ms(gk, stream, 1, world)
+    kms = graph_ms(gk, stream, steps, world)
+    del gk
+    total_flops = flops_layer * world * shape.layers
+    tflops = total_flops / (ms * 1e-3) / 1e12
+    launch_us = kms * 1e3 / shape.layers
+    achieved = flops_layer / (launch_us * 1e-6) / 1e12
+    _, bf16_peak, peak_kind = peaks()
+    traffic = read_traffic("w8a16_kernel_smollm3_layer_m512.md", world)
+
+    # end to end from host buffers: the seven activation matrices H2D (pinned bf16), the step,
+    # the last layer's outputs D2H (pinned fp32), waited for on the host
+    hx = [x.cpu().pin_memory() for x in xs]
+    last = gathered[-1] if world > 1 else [it[2] for it in layers[-1]]
+    hy = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in last]
+    h2d = sum(t.numel() * t.element_size() for t in hx)
+    d2h = sum(t.numel() * t.element_size() for t in hy)
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            for d, h in zip(xs, hx):
+                d.copy_(h, non_blocking=True)
+            g.replay()
+            for h, d in zip(hy, last):
+                h.copy_(d, non_blocking=True)
+        stream.synchronize()
+    e2e_step()
+    barrier(world)
+    ne = max(3, min(steps, 20))
+    t0 = time.perf_counter()
+    for _ in range(ne):
+        e2e_step()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) / ne * 1e3, world)
+
+    parity = None
+    if world > 1:
+        # layer 0 unsharded on rank 0 against the gathered sharded outputs (fp32 sums in
+        # different orders: within 2^-18 of |x| @ |deq|^T elementwise)
+        torch.cuda.synchronize()
+        if rank == 0:
+            worst = 0.0
+            for (x, w, y, _), gth, (rows, sw) in zip(layers[0], gathered[0], full0):
+                wf = linear.PackedWeight("int8-row", rows.shape[0], w.K, rows,
+                                         sw.view(torch.uint8).reshape(-1, 4))
+                ref = linear.gemm_w8a16(x, wf)
+                got = gth.permute(1, 0, 2).reshape(PREFILL_TOKENS, -1)
+                deq = rows.view(torch.int8).float().abs() * sw[:, None]
+                bound = x.float().abs() @ deq.t()
+                worst = max(worst, float(((got - ref).abs() / (bound + 1e-30)).max()))
+            parity = {"vs_1gpu": "within tolerance" if worst <= 2.0 ** -18 else "differs",
+                      "max_err_over_bound": worst, "tolerance": 2.0 ** -18, "layer": 0}
+        barrier(world)
+    del g
+    torch.cuda.synchronize()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, desc, threads = prefill_cpu_sample()
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}
+    return {
+        "metric": "prefill TFLOP/s", "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms,
+        "steps": steps, "warmup": warmup, "scaling": "strong", "dtype": "bf16 x int8 -> fp32",
+        "config": {"workload": "SmolLM3-3B-shaped prefill GEMMs: 36 layers x (q 2048x2048, k/v "
+                               "512x2048, o 2048x2048, gate/up 11008x2048, down 2048x11008) "
+                               "int8 per-row weights, 512 tokens bf16 N(0,1)",
+                   "flops_per_step": total_flops, "launch": "one grouped launch a layer "
+                   "(7 projections), 36 in one CUDA graph",
+                   "parallelism": f"row-shard x{world}" + (" + NCCL all-gather of every "
+                                                          "projection's fp32 output (in the "
+                                                          "timed graph)" if world > 1 else ""),
+                   "l2": "weights 2.8 GB > 126 MB L2 (no flush needed)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_peak,
+                     "unit": "TFLOP/s", "frac": achieved / bf16_peak, "traffic": traffic,
+                     "kernel": "w8a16_kernel (one SmolLM3-3B layer, 7 projections, M=512)",
+                     "flops_per_launch": flops_layer, "us_per_launch": launch_us,
+                     "peak_kind": f"{peak_kind} bf16 (burst)"},
+        "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "gemm_w8a16_group graph from pinned host bf16 X to host fp32 y of the "
+                       "last layer"},
+        "parity": parity,
+        "cpu_baseline": cpu,
+        "gpu_launches": shape.layers * steps,
+    }
+
+
+# ------------------------------------------------------------------------------ profile runs
 def profile_run(what: str):
     """A few launches for an ncu capture: the LM head GEMV alone, two decode steps, three
     grouped prefill launches of one SmolLM3-3B layer, or five int4-g32 GEMVs of one activation
@@ -85,7 +659,8 @@ def profile_run(what: str):
         for _ in range(5):
             linear.qlinear(x, w, out=y)
     elif what == "prefill":
-        items = prefill_layer(WL.SMOLLM3_3B, 1, 0, torch.Generator(device="cuda").manual_seed(0))
+        items, _ = prefill_layer(WL.SMOLLM3_3B, 1, 0,
+                                 torch.Generator(device="cuda").manual_seed(0))
         for _ in range(3):
             linear.gemm_w8a16_group(items)
     else:
@@ -96,231 +671,16 @@ def profile_run(what: str):
     torch.cuda.synchronize()
 
 
-PREFILL_TOKENS = 512
-
-
-def prefill_layer(shape, world, rank, gen, xs=None):
-    """One layer's seven projections for the prefill GEMM (BASELINE configuration 4): int8-row
-    weights (uniform int8 rows, Sw ~ 1e-3: the GEMM's cost does not depend on the values) for
-    this rank's row shard, bf16 activations N(0, 1) [512, K] (shared across layers when xs is
-    given) and fp32 outputs. Returns gemm_w8a16_group items."""
-    import torch
-    from opentpu_b200 import linear
-    items = []
-    for i, (_, N, K) in enumerate(shape.projections()):
-        n = N // world
-        rows = torch.randint(-127, 128, (n, K), dtype=torch.int8, device="cuda",
-                             generator=gen).view(torch.uint8)
-        sw = (torch.rand(n, device="cuda", generator=gen) * 1e-3 + 1e-4)
-        w = linear.PackedWeight("int8-row", n, K, rows, sw.view(torch.uint8).reshape(n, 4))
-        x = xs[i] if xs is not None else torch.randn((PREFILL_TOKENS, K), device="cuda",
-                                                      generator=gen).to(torch.bfloat16)
-        y = torch.empty((PREFILL_TOKENS, n), device="cuda")
-        items.append((x, w, y, False))
-    return items
-
-
-def prefill_cpu_sample(budget_s: float = 6.0):
-    """The oracle's float64 `deq @ x` (oracle/prefill.py) on host cores over one 2048 x 2048
-    projection at 512 tokens: (TFLOP/s, description, threads)."""
-    from oracle import prefill as PF
-    rng = np.random.default_rng(0)
-    K = N = 2048
-    x = PF.bf16_round(rng.standard_normal((PREFILL_TOKENS, K)).astype(np.float32))
-    rows = rng.integers(-127, 128, (N, K), dtype=np.int8).view(np.uint8)
-    srows = (rng.random(N).astype(np.float32) * 1e-3).view(np.uint8).reshape(N, 4)
-    done, t0 = 0, time.perf_counter()
-    while True:
-        PF.gemm_w8a16(x, rows, srows, K)
-        done += 1
-        el = time.perf_counter() - t0
-        if el > budget_s or done >= 20:
-            break
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
-    except Exception:
-        threads = 1
-    flops = 2.0 * PREFILL_TOKENS * N * K
-    desc = (f"{done} x one 2048x2048 projection at 512 tokens, float64 numpy (oracle, also "
-            "forms the error bound |x| @ |deq|^T)")
-    return done * flops / el / 1e12, desc, threads
-
-
-def prefill_bench(world, rank, local, steps, warmup, cpu_baseline: bool):
-    """BASELINE configuration 4 on this rank: 36 SmolLM3-3B layers, each one grouped launch of
-    its seven projections (row shard 1/world of each), captured in one CUDA graph a step.
-    Returns the prefill part of the bench line (rank 0) after a max over ranks."""
-    import torch
-    import torch.distributed as dist
-    from opentpu_b200 import linear
-    shape = WL.SMOLLM3_3B
-    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    first = prefill_layer(shape, world, rank, gen)
-    xs = [it[0] for it in first]
-    layers = [first] + [prefill_layer(shape, world, rank, gen, xs) for _ in range(shape.layers - 1)]
-    flops_layer = sum(2.0 * PREFILL_TOKENS * it[1].N * it[1].K for it in first)
-    stream = torch.cuda.Stream()
-    with torch.cuda.stream(stream):
-        for items in layers[:2]:
-            linear.gemm_w8a16_group(items)
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        for items in layers:
-            linear.gemm_w8a16_group(items)
-    with torch.cuda.stream(stream):
-        for _ in range(warmup):
-            g.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clocks:
-        torch.cuda.synchronize()
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(steps):
-                g.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    del g
-    total_flops = flops_layer * world * shape.layers
-    tflops = total_flops / (ms * 1e-3) / 1e12
-    launch_us = ms * 1e3 / shape.layers
-    achieved = flops_layer / (launch_us * 1e-6) / 1e12
-    pk = ROOT / "MEASURED_PEAKS.json"
-    if pk.exists():
-        peak, peak_kind = float(json.loads(pk.read_text())["bf16_tflops"]), "measured (burst)"
-    else:
-        peak, peak_kind = 1590.0, "fallback"
-    traffic = None
-    tp = ROOT / "profiles" / "w8a16_kernel_smollm3_layer_m512.md"
-    if tp.exists() and world == 1:
-        for line in tp.read_text().splitlines():
-            if line.startswith("| dram_bytes_per_launch |"):
-                traffic = int(line.split("|")[2])
-    cpu = None
-    if rank == 0 and world == 1 and cpu_baseline:
-        v, desc, threads = prefill_cpu_sample()
-        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}
-    return {
-        "metric": "prefill TFLOP/s", "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms,
-        "steps": steps, "warmup": warmup, "scaling": "strong", "dtype": "bf16 x int8 -> fp32",
-        "config": {"workload": "SmolLM3-3B-shaped prefill GEMMs: 36 layers x (q 2048x2048, k/v "
-                               "512x2048, o 2048x2048, gate/up 11008x2048, down 2048x11008) "
-                               "int8 per-row weights, 512 tokens bf16 N(0,1)",
-                   "flops_per_step": total_flops, "launch": "one grouped launch a layer "
-                   "(7 projections), 36 in one CUDA graph",
-                   "parallelism": f"row-shard x{world}",
-                   "l2": "weights 2.8 GB > 126 MB L2 (no flush needed)"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "w8a16_kernel (one SmolLM3-3B layer, 7 projections, M=512)",
-                     "flops_per_launch": flops_layer, "us_per_launch": launch_us,
-                     "peak_kind": peak_kind},
-        "cpu_baseline": cpu,
-        "gpu_launches": shape.layers * steps,
-        "clocks": clocks.summary(),
-    }
-
-
-class Clocks:
-    """nvidia-smi sampling while the timed region runs (SM clock, throttle reasons)."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, index: int):
-        self.index = index
-        self.rows = []
-        self.proc = None
-
-    def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except OSError:
-            self.proc = None
-        return self
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
-
-    def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.t.join(timeout=2)
-
-    def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        mhz = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
-                          if len(r) > 5 + i and r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(mhz) if mhz else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
-
-
-def cpu_sample_seconds(budget_s: float = 12.0):
-    """The oracle's exact decode GEMV chain on host cores over a bounded sample of the step's
-    projections: returns (GB/s of weight bytes, sample description, threads)."""
-    from oracle import fp32 as F
-    from oracle import mx as X
-    shape = WL.QWEN3_0_6B
-    rng = np.random.default_rng(0)
-    # one layer's seven projections plus a 16384-row slice of the head
-    shapes = [(N, K) for _, N, K in shape.projections()] + [(16384, shape.hidden)]
-    mats = []
-    for N, K in shapes:
-        W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
-        q, s = X.quantize_rows_rsc(W)
-        x = rng.standard_normal(K).astype(np.float32)
-        mats.append((q, s, x, K))
-    nbytes = sum(q.shape[0] * (q.shape[1] + 4) for q, _, _, _ in mats)
-    done, t0 = 0, time.perf_counter()
-    while True:
-        for q, s, x, K in mats:
-            qa, Sa, da = F.quantize_rows(x[None, :], 32)
-            X.mm(qa, Sa, da, q, s, "int8", K, rsc=True)
-        done += 1
-        el = time.perf_counter() - t0
-        if el > budget_s or done >= 50:
-            break
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
-    except Exception:
-        threads = 1
-    desc = (f"{done} passes over 1 layer (7 projections) + a 16384-row head slice "
-            f"({nbytes / 1e6:.1f} MB of int8 rows), exact MM port, numpy")
-    return done * nbytes / el / 1e9, desc, threads
-
-
+# ------------------------------------------------------------------------------ arms
 def run_reference(args, rank, world):
+    """The reference's CPU algorithm for the decode GEMV (the exact QACT + MM of the oracle
+    port) on every host core, on rank 0 only; the other ranks exit without work."""
     if rank != 0:
         return
     vals = []
     desc, threads = "", 1
     for i in range(args.warmup + args.steps):
-        v, desc, threads = cpu_sample_seconds(budget_s=8.0)
+        v, desc, threads = cpu_exact_sample(budget_s=6.0 if i >= args.warmup else 1.0)
         if i >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
@@ -338,14 +698,17 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["head", "step", "prefill", "g32"])
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-4bit", action="store_true")
+    ap.add_argument("--no-config1", action="store_true")
     args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
     if args.profile:
         profile_run(args.profile)
         return
@@ -358,7 +721,6 @@ def main():
 
     import torch
     import torch.distributed as dist
-    from opentpu_b200 import linear
     from opentpu_b200.decode import DecodeChain
 
     torch.cuda.set_device(local)
@@ -367,131 +729,46 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+    hbm, _, peak_kind = peaks()
     shape = WL.QWEN3_0_6B
     fmt = "int8-row"
     chain = DecodeChain(shape, fmt=fmt, head_fmt=fmt, world=world, rank=rank, group=group)
     chain.capture()
-    stream = chain.stream
     total_bytes = chain.weight_bytes
-
     chain.replay(args.warmup)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
     with Clocks(local) as clocks:
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        chain.replay(args.steps)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = total_bytes / (ms * 1e-3) / 1e9
+        ms = graph_ms(chain.graph, chain.stream, args.steps, world)
+        value = total_bytes / (ms * 1e-3) / 1e9
+        e2e_ms, h2d, d2h, _ = closed_loop(chain, max(10, min(args.steps, 200)), world)
+        parity = parity_vs_one_gpu(chain, world, rank) if world > 1 else None
+        if world == 1:
+            roof = layers_roofline(chain, world, max(10, args.steps), hbm, peak_kind,
+                                   "gemv_kernel (the 112 layer projections of a step: "
+                                   "QKV 4096x1024, O 1024x2048, GateUp 6144x1024, Down "
+                                   "1024x3072, int8-row, M=1; one launch each)")
+        else:   # the whole sharded step per rank (the stepped tags span the whole step)
+            per_rank = total_bytes / world
+            ach = per_rank / (ms * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                    "frac": ach / hbm, "traffic": None,
+                    "kernel": "gemv_kernel (all 113 launches of this rank's shard of a step)",
+                    "bytes_per_step": per_rank, "us_per_step": ms * 1e3,
+                    "peak_kind": f"{peak_kind} (copy)"}
+        head = head_roofline(chain, chain.stream, world, hbm, peak_kind)
+        c1 = None if args.no_config1 else config1(world, max(3, min(args.steps, 50)))
+        dec4 = None if args.no_4bit else decode_4bit(args, world, rank, group, hbm, peak_kind)
+        prefill = None if args.no_prefill else prefill_bench(
+            args, world, rank, local, group, max(3, min(100, args.steps // 4)),
+            max(3, min(5, args.warmup)))
 
-    # the dominant kernel alone: the LM head GEMV (this rank's rows), 20 launches in a graph,
-    # launched as in the step (programmatic dependent launch: a launch's CTAs start on SMs the
-    # one before has left)
-    head, hx = chain.weights[-1], chain.inputs[shape.hidden]
-    hy = torch.empty((1, head.N), device="cuda")
-    hg = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            linear.qlinear(hx, head, out=hy, pdl=True)
-    torch.cuda.synchronize()
-    with torch.cuda.graph(hg, stream=stream):
-        for _ in range(20):
-            linear.qlinear(hx, head, out=hy, pdl=True)
-    with torch.cuda.stream(stream):
-        hg.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(5):
-            hg.replay()
-        e1.record(stream)
-    torch.cuda.synchronize()
-    head_ms = e0.elapsed_time(e1) / 100
-    head_bytes = head.stream_bytes + head.K * 4 + head.N * 4
-    peak, peak_kind = peaks()
-    achieved = head_bytes / (head_ms * 1e-3) / 1e9
-    traffic = None
-    tp = ROOT / "profiles" / "gemv_kernel_lm_head_int8row_151936x1024_m1.md"
-    if tp.exists() and world == 1:
-        for line in tp.read_text().splitlines():
-            if line.startswith("| dram_bytes_per_launch |"):
-                traffic = int(line.split("|")[2])
-
-    # end to end through the public API from host buffers: the input H2D and the greedy token
-    # (the device argmax of the logits) D2H each step
-    inputs_host = {shape.hidden: torch.randn((1, shape.hidden)).pin_memory()}
-    token_host = torch.empty(1, dtype=torch.int64, pin_memory=True)
-    h2d = sum(t.numel() * 4 for t in inputs_host.values())
-    d2h = token_host.numel() * 8
-    for _ in range(3):
-        chain.run_host(inputs_host, token_host)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    n_e2e = max(3, min(args.steps, 200))
-    e0.record(stream)
-    for _ in range(n_e2e):
-        chain.run_host(inputs_host, token_host)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / n_e2e
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-
-    cpu = None
+    cpu = blas = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, desc, threads = cpu_sample_seconds()
+        v, desc, threads = cpu_exact_sample()
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
-
-    # BASELINE configuration 3 (the same decode with int4-g32 layers and an int8-row head)
-    dec4 = None
-    if not args.no_4bit:
-        # int4-g32 is weight-only (no MM, so no fused gather): NCCL all-gathers with world > 1
-        c4 = DecodeChain(shape, fmt="int4-g32", head_fmt="int8-row", world=world, rank=rank,
-                         group=group, gather="nccl")
-        c4.capture()
-        c4.replay(args.warmup)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        n4 = max(10, args.steps // 2)
-        with torch.cuda.stream(c4.stream):
-            e0.record(c4.stream)
-            c4.replay(n4)
-            e1.record(c4.stream)
-        torch.cuda.synchronize()
-        ms4 = e0.elapsed_time(e1) / n4
-        if world > 1:
-            t = torch.tensor([ms4], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms4 = float(t.item())
-        dec4 = {"metric": "decode weight GB/s", "value": c4.weight_bytes / (ms4 * 1e-3) / 1e9,
-                "unit": "GB/s", "ms_per_step": ms4, "tok_s": 1e3 / ms4, "steps": n4,
-                "config": {"workload": "Qwen3-0.6B-shaped decode step, layers int4 group-32 fp16 "
-                                       "scales (weight-only, fp32 activations), 151936x1024 "
-                                       "int8-row LM head, M=1 (BASELINE configuration 3)",
-                           "weights_bytes_per_step": c4.weight_bytes,
-                           "parallelism": f"row-shard x{world}" + (" + NCCL all-gather per "
-                                                                  "projection" if world > 1
-                                                                  else "")},
-                "gpu_launches": c4.launches * n4}
-        c4.release()
-        del c4
-
-    prefill = None
-    if not args.no_prefill:
-        prefill = prefill_bench(world, rank, local, max(3, min(100, args.steps // 20)),
-                                max(3, min(5, args.warmup)), not args.no_cpu_baseline)
+        v, desc, threads = cpu_blas_sample("int8-row")
+        blas = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
 
     if rank == 0:
         print(json.dumps({
@@ -500,7 +777,8 @@ def main():
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8", "data": "synthetic",
             "config": {"workload": "Qwen3-0.6B-shaped int8 per-row decode step: 28 layers x "
-                                   "(QKV, O, GateUp, Down) + 151936x1024 LM head, M=1",
+                                   "(QKV, O, GateUp, Down) + 151936x1024 LM head + greedy "
+                                   "token, M=1",
                        "weights_bytes_per_step": total_bytes, "format": fmt,
                        "parallelism": f"row-shard x{world}" + (" + all-gather per projection "
                                                               "fused into the GEMV (tagged 8-byte "
@@ -510,23 +788,24 @@ def main():
                        "l2": "weights 598 MB > 126 MB L2 (no flush needed)",
                        "graph": "one CUDA graph per step, PDL launches"},
             "tok_s": 1e3 / ms,
-            "hbm_frac": value / world / peak,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "gemv_kernel (LM head launch, 151936x1024 int8-row, M=1)",
-                         "bytes_per_launch": head_bytes, "us_per_launch": head_ms * 1e3,
-                         "peak_kind": peak_kind},
+            "hbm_frac": value / world / hbm,
+            "roofline": roof,
+            "roofline_head": head,
             "cpu_baseline": cpu,
+            "cpu_baseline_blas": blas,
             "e2e": {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
+                    "ms_per_token": e2e_ms, "tok_s": 1e3 / e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms, "api": "DecodeChain.run_host"},
+                    "api": "DecodeChain.run_host, closed loop (each input picked by the "
+                           "previous token, read on the host)"},
+            "parity": parity,
             "gpu_launches": chain.launches * args.steps,
             "clocks": clocks.summary(),
+            "config1": c1,
             "decode_4bit": dec4,
             "prefill": prefill,
         }), flush=True)
     chain.release()
-    del hg
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -2,9 +2,8 @@
  * libotq -- openTPU's quantized linear layer on NVIDIA B200 (sm_100a): the C ABI.
  *
  * The reference (FeSens/openTPU) is a Python package; this ABI is what its numpy call sites for
- * the quantized linear layer would bind through ctypes (the binding is in INTEGRATION.md). Each
- * entry point names the reference function (path:line inside the reference project) whose
- * results it reproduces.
+ * the quantized linear layer would bind through ctypes. Each entry point names the reference
+ * function (path:line inside the reference project) whose results it reproduces.
  *
  * Conventions
  *  - Every pointer is a CUDA device pointer (or managed memory) owned by the caller; no entry
@@ -210,6 +209,15 @@ OTQ_API int otq_qmm_chain(const otq_proj* projs, int count, void* stream);
  * outputs are not valid. reset != 0 clears it (and, if it was set, re-arms the grid barrier). No counterpart in the reference (a simulator has no
  * such failure). */
 OTQ_API int otq_status_word(int* value, int reset);
+
+/* How long a kernel waits for tagged input words (otq_qmm_peer with wait != 0) on the current
+ * device: `polls` reads of a word that has not arrived, with a short back-off between them,
+ * before the wait gives up, sets bit 0 of the status word and lets the launch finish (its
+ * outputs are then not valid). 0 restores the default of 2^22 polls (about a quarter of a
+ * second). A failure detector sets a short limit so that a rank that never writes its words
+ * turns into a status the host reads instead of a long stall. Applies to launches made after
+ * the call. No counterpart in the reference. */
+OTQ_API int otq_set_wait_limit(uint32_t polls);
 
 /* ------------------------------------------------------------------ prefill GEMM */
 

@@ -58,6 +58,7 @@ SIGNATURES = {
     "otq_gemm_w8a16": (_I, [_I, _P, _L, _P, _L, _L, _L, _P, _L, _L, _P, _L, _P]),
     "otq_gemm_w8a16_group": (_I, [_P, _I, _P]),
     "otq_status_word": (_I, [_P, _I]),
+    "otq_set_wait_limit": (_I, [ctypes.c_uint32]),
     "otq_argmax": (_I, [_P, _L, _L, _P, _P]),
     "otq_argmax_noalloc": (_I, [_P, _L, _L, _P, _P]),
     "otq_pack_g32": (_I, [_P, _L, _L, _L, _P, _P, _P]),

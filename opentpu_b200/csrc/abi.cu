@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 #include <cstring>
 
 #include "otq_internal.h"
@@ -124,10 +125,14 @@ int check_out(int64_t M, int64_t N, const float* y, int64_t ldy, int flags, cons
 
 }  // namespace
 
+// The address is looked up once per device (under a lock: two host threads may make their first
+// calls together) and kept; a cudaDeviceReset invalidates it.
 int* status_word() {
   static int* addr[kMaxDevices] = {nullptr};
+  static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
   if (addr[dev] == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
@@ -418,6 +423,12 @@ int otq_status_word(int* value, int reset) {
   }
   *value = v;
   return kOk;
+}
+
+int otq_set_wait_limit(uint32_t polls) {
+  int st = device_ok();
+  if (st) return st;
+  return finish(set_tag_wait_limit(polls));
 }
 
 int otq_pack_g32(const float* W, int64_t N, int64_t K, int64_t ldw, uint8_t* codes,

@@ -89,14 +89,17 @@ int argmax_launch(const float* x, int64_t n, int64_t stride, int64_t* acc, int64
 namespace otq {
 namespace {
 
-constexpr int kNoAllocScratchWords = 32;   // 256 bytes; one call uses 2 words
+// A call uses words 0 and 1 only (every call the same two); the array is 256 bytes so that it
+// starts and ends on its own 256-byte boundary, not to give calls separate slots.
+constexpr int kNoAllocScratchWords = 32;
 static __device__ __align__(256) int64_t g_argmax_scratch[kNoAllocScratchWords];
 
 std::mutex g_scratch_mu;
 int64_t* g_scratch_dev[kMaxDevices] = {nullptr};
 
 // This device's address of g_argmax_scratch, looked up on the device's first call (with the
-// device current) and kept.
+// device current) and kept for the life of the process. A cudaDeviceReset unloads the module and
+// invalidates the kept address: this entry point must not be called on a device after a reset.
 int64_t* scratch_address(int dev) {
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (g_scratch_dev[dev] == nullptr) {

@@ -327,7 +327,7 @@ __device__ __forceinline__ void gemv_clear_activations(const PArgs& p, const GSm
 template <int FMT, int MT, bool PLAIN>
 __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSmem& s, int mt, int kp, int ap,
                                       bool frag, bool cleared, bool tagged = false, uint32_t expect = 0,
-                                      int* status = nullptr) {
+                                      int* status = nullptr, uint32_t limit = 1u << 22) {
   const int K = p.K, KG = K / 32;
   if (!cleared) gemv_clear_activations<FMT, MT, PLAIN>(p, s, mt, kp, ap, frag);
   if (p.x != nullptr) {
@@ -366,7 +366,7 @@ __device__ __forceinline__ void gemv_load_activations(const PArgs& p, const GSme
             }
           },
           tagged ? reinterpret_cast<const unsigned long long*>(xr) : nullptr, expect, status,
-          s.Sa + j);
+          s.Sa + j, limit);
     }
     return;   // qact_row4 ends with a barrier, after every write above (Sa included)
   } else {
@@ -583,6 +583,10 @@ __device__ __forceinline__ Geo geometry(const PArgs& d, int warp) {
   q.total = q.NBLK * q.NIT;
   return q;
 }
+
+// Polls a wait on tagged input words makes before it gives up and records kStatusTimeout
+// (otq_set_wait_limit); 2^22 by default, about a quarter of a second with the back-off.
+__device__ uint32_t g_tag_wait_limit = 1u << 22;
 
 __device__ unsigned int g_bar_count;   // CTAs arrived at the current grid barrier
 __device__ unsigned int g_bar_gen;     // grid barriers completed (wraps)
@@ -942,7 +946,8 @@ __global__ void __launch_bounds__(kThreads, (FIXED < 0 || FIXED == kCfgR32) ? 1 
     if (pi > 0) grid_barrier(C.status);   // projection pi may read what pi - 1 wrote
     const int KCH = (d.K + F::kElems - 1) / F::kElems;
     gemv_load_activations<FMT, MT, PLAIN>(d, s, min(MT, d.M), KCH * F::kElems, L.ap, L.frag,
-                                          kCleared && pi == 0, pi == 0 && tagged_in, expect, C.status);
+                                          kCleared && pi == 0, pi == 0 && tagged_in, expect, C.status,
+                                          tagged_in ? g_tag_wait_limit : 0u);
     // the next launch starts here: earlier (before the wait) or later (at exit) measured slower
     if (pi == count - 1) pdl_launch();
     const int mt = min(MT, d.M);
@@ -1303,6 +1308,12 @@ int chain_launch(const otq_proj* pr, int count, cudaStream_t stream) {
     i = j;
   }
   return kOk;
+}
+
+// The polls of a tagged-input wait on the current device (0: the default).
+int set_tag_wait_limit(uint32_t polls) {
+  const uint32_t v = polls == 0 ? (1u << 22) : polls;
+  return cudaMemcpyToSymbol(g_tag_wait_limit, &v, sizeof(v)) == cudaSuccess ? kOk : kErrCuda;
 }
 
 // The grid barrier's words back to zero (after a launch whose barrier wait ran out).

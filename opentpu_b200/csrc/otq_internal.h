@@ -88,6 +88,7 @@ int w8a16_launch(const W8A16Proj* projs, int count, cudaStream_t stream);   // p
 int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);    // gemv.cu
 int chain_launch(const otq_proj* projs, int count, cudaStream_t stream);
 int chain_reset();   // the grid barrier's count back to zero
+int set_tag_wait_limit(uint32_t polls);   // gemv.cu: otq_set_wait_limit
 int* status_word();   // this device's status word (device address), or null
 
 // Launch with an optional programmatic-dependent-launch attribute (the kernel then may start

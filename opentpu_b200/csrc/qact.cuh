@@ -160,7 +160,8 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
                                                    uint32_t* red, Emit4 emit,
                                                    const unsigned long long* xt = nullptr,
                                                    uint32_t expect = 0, int* status = nullptr,
-                                                   float* S_out = nullptr) {
+                                                   float* S_out = nullptr,
+                                                   uint32_t limit = 1u << 22) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NW = NT / 32;
   const int n4 = n >> 2;   // a multiple of 32: every lane of a warp runs the same iterations
@@ -193,12 +194,12 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
       if (i >= n4) continue;
       if (xt != nullptr) {
         // a tagged row (value in the low word, the writer's tag in the high word): wait,
-        // bounded, until the four elements carry at least the expected tag
+        // bounded (`limit` polls), until the four elements carry at least the expected tag
         for (uint32_t spin = 0;
              behind(w[b][0], expect) || behind(w[b][1], expect) || behind(w[b][2], expect) ||
              behind(w[b][3], expect);
              ++spin) {
-          if (spin >= (1u << 22)) {
+          if (spin >= limit) {
             if (status != nullptr) atomicOr(status, 1);   // a writer never arrived: not valid
             break;
           }

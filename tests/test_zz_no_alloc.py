@@ -54,6 +54,32 @@ def test_no_alloc_argmax_matches_the_entry_point_with_scratch(lib):
         assert got == want == int(np.argmax(row))
 
 
+def test_no_alloc_argmax_strided_rows_nan_and_signed_zeros(lib):
+    """A tagged row read with stride 2 (the values of (value, tag) words), a row whose maximum
+    is -0 tied with +0 (the lower index wins: numpy compares them equal) and a row with a NaN
+    (numpy's argmax stops at the first NaN), each against otq_argmax and numpy."""
+    rng = np.random.default_rng(5)
+    tagged = np.zeros((4096, 2), np.float32)
+    tagged[:, 0] = rng.standard_normal(4096)
+    tagged[:, 1] = 1e30                        # tags larger than every value: must be skipped
+    tagged[3001, 0] = 12.0
+    zeros = -np.abs(rng.standard_normal(1000)).astype(np.float32) - 1.0
+    zeros[10], zeros[20] = -0.0, 0.0
+    nan = rng.standard_normal(1000).astype(np.float32)
+    nan[500], nan[700] = np.nan, 99.0
+    index = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for row, stride, want in ((tagged, 2, int(np.argmax(tagged[:, 0]))), (zeros, 1, 10),
+                              (nan, 1, int(np.argmax(nan)))):
+        x = torch.from_numpy(np.ascontiguousarray(row)).cuda().reshape(-1)
+        n = x.numel() // stride
+        out = torch.zeros(2, dtype=torch.int64, device="cuda")
+        lib.call("otq_argmax", x.data_ptr(), n, stride, out.data_ptr(), stream)
+        lib.call("otq_argmax_noalloc", x.data_ptr(), n, stride, index.data_ptr(), stream)
+        torch.cuda.synchronize()
+        assert int(index[0]) == int(out[0]) == want
+
+
 def test_no_alloc_argmax_rejects_rows_past_its_limit(lib):
     x = torch.zeros(16, device="cuda")
     index = torch.zeros(1, dtype=torch.int64, device="cuda")
