@@ -52,9 +52,37 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
             raise RuntimeError(f"nvcc failed on {src}")
     if not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(LIB),
-               *map(str, objs), "-cudart", "static"]
+               *map(str, objs), "-cudart", "static", "-Xlinker", "-soname=libotq.so"]
         subprocess.run(cmd, check=True)
+    build_torch_ops(verbose)
     return LIB
+
+
+TORCH_OPS = PKG / "libotq_torch.so"
+
+
+def build_torch_ops(verbose: bool = False) -> Path:
+    """torch.ops.otq.* (csrc/torch_ops.cpp): a C++ file against PyTorch's headers, linked to
+    libotq.so (found next to it at run time) and to PyTorch's own libraries."""
+    import torch
+    src = CSRC / "torch_ops.cpp"
+    deps = [src, ROOT / "include" / "otq.h", LIB]
+    if TORCH_OPS.exists() and TORCH_OPS.stat().st_mtime > max(p.stat().st_mtime for p in deps):
+        return TORCH_OPS
+    tdir = Path(torch.__file__).resolve().parent
+    cuda = Path(nvcc()).resolve().parent.parent if nvcc() != "nvcc" else Path("/usr/local/cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-I", str(tdir / "include"), "-I", str(tdir / "include" / "torch" / "csrc" / "api" /
+                                                   "include"),
+           "-I", str(cuda / "include"), str(src), "-o", str(TORCH_OPS),
+           "-L", str(tdir / "lib"), "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+           "-ltorch_cuda", "-L", str(PKG), "-lotq", "-Wl,-rpath,$ORIGIN",
+           f"-Wl,-rpath,{tdir / 'lib'}"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return TORCH_OPS
 
 
 if __name__ == "__main__":

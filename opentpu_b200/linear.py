@@ -117,13 +117,37 @@ class PackedWeight:
         return self.N * row_bytes(self.K, self.fmt) + s
 
     @staticmethod
-    def from_float(W: torch.Tensor, fmt: str) -> "PackedWeight":
-        """Quantize fp32 W [N, K] on the GPU into `fmt` (the reference quantizer's bytes)."""
+    def from_float(W: torch.Tensor, fmt: str, shard: int | None = None, world: int = 1,
+                   rank: int = 0) -> "PackedWeight":
+        """Quantize fp32 W [N, K] on the GPU into `fmt` (the reference quantizer's bytes).
+
+        shard (runtime.Weight(array, shard, fmt), runtime.py:38-51,138-142): None keeps the
+        whole matrix; 0 keeps rank `rank`'s contiguous block of N / world rows (the row shard a
+        row-sharded projection runs: every output's exact sum stays on one rank); 1 keeps its
+        block of K / world columns, quantized on its own as the reference quantizes a slice's
+        part (per-row scales of the part). ValueError for a bad shard, a world that does not
+        divide the sharded dimension, or a column block that is not whole quantization
+        blocks, as for a bad format or shape."""
         if fmt not in FORMATS:
             raise ValueError(f"Weight fmt must be one of {FORMATS}")
+        if shard not in (None, 0, 1):
+            raise ValueError("Weight shard must be None, 0 (rows) or 1 (columns)")
         W = _cuda(W, "W")
         if W.ndim != 2:
             raise ValueError("Weight must be 2-D [N, K]")
+        if world < 1 or not 0 <= rank < world:
+            raise ValueError(f"rank {rank} of world {world}")
+        if shard is not None and world > 1:
+            n = W.shape[shard]
+            if n % world:
+                raise ValueError(f"{n} {'rows' if shard == 0 else 'columns'} do not split over "
+                                 f"{world} ranks")
+            part = n // world
+            if shard == 1 and part % (32 if fmt == "int4-g32" else D):
+                raise ValueError(f"a column shard of {part} is not whole blocks of "
+                                 f"{32 if fmt == 'int4-g32' else D}")
+            W = W[rank * part:(rank + 1) * part] if shard == 0 else \
+                W[:, rank * part:(rank + 1) * part]
         W = W.to(torch.float32).contiguous()
         N, K = W.shape
         dev = W.device
