@@ -145,7 +145,8 @@ def test_packed_weight_shards(fmt):
         alone = linear.PackedWeight.from_float(W[:, 256 * rank:256 * (rank + 1)].contiguous(), fmt)
         assert col.N == 64 and col.K == 256
         assert torch.equal(col.rows, alone.rows) and torch.equal(col.srows, alone.srows)
-    for bad in ({"shard": 2}, {"shard": 0, "world": 3}, {"shard": 1, "world": 16},
+    bad_cols = {"shard": 1, "world": 64 if fmt == "int4-g32" else 16}   # part not whole blocks
+    for bad in ({"shard": 2}, {"shard": 0, "world": 3}, {"shard": 1, "world": 3}, bad_cols,
                 {"shard": 0, "world": 2, "rank": 2}):
         with pytest.raises(ValueError):
             linear.PackedWeight.from_float(W, fmt, **bad)
