@@ -466,11 +466,10 @@ def parity_vs_one_gpu(chain, world, rank):
     """Rank 0: the same seeded step replayed unsharded on one GPU; the sharded step's logits and
     token compared bit for bit (the other ranks wait at a barrier)."""
     import torch
-    from opentpu_b200.decode import DecodeChain
     res = None
     torch.cuda.synchronize()
     if rank == 0:
-        one = DecodeChain(chain.shape, fmt=chain.plan[0][3], head_fmt=chain.plan[-1][3], seed=0)
+        one = type(chain)(chain.shape, seed=0)
         one.step_eager()
         torch.cuda.synchronize()
         a = chain.logits().float().contiguous().cpu().numpy().view(np.uint32)
@@ -721,7 +720,7 @@ def main():
 
     import torch
     import torch.distributed as dist
-    from opentpu_b200.decode import DecodeChain
+    from opentpu_b200.decode import DecodeStep
 
     torch.cuda.set_device(local)
     group = None
@@ -732,7 +731,7 @@ def main():
     hbm, _, peak_kind = peaks()
     shape = WL.QWEN3_0_6B
     fmt = "int8-row"
-    chain = DecodeChain(shape, fmt=fmt, head_fmt=fmt, world=world, rank=rank, group=group)
+    chain = DecodeStep(shape, fmt=fmt, head_fmt=fmt, world=world, rank=rank, group=group)
     chain.capture()
     total_bytes = chain.weight_bytes
     chain.replay(args.warmup)
@@ -743,20 +742,19 @@ def main():
         value = total_bytes / (ms * 1e-3) / 1e9
         e2e_ms, h2d, d2h, _ = closed_loop(chain, max(10, min(args.steps, 200)), world)
         parity = parity_vs_one_gpu(chain, world, rank) if world > 1 else None
-        if world == 1:
-            roof = layers_roofline(chain, world, max(10, args.steps), hbm, peak_kind,
-                                   "gemv_kernel (the 112 layer projections of a step: "
-                                   "QKV 4096x1024, O 1024x2048, GateUp 6144x1024, Down "
-                                   "1024x3072, int8-row, M=1; one launch each)")
-        else:   # the whole sharded step per rank (the stepped tags span the whole step)
-            per_rank = total_bytes / world
-            ach = per_rank / (ms * 1e-3) / 1e9
-            roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
-                    "frac": ach / hbm, "traffic": None,
-                    "kernel": "gemv_kernel (all 113 launches of this rank's shard of a step)",
-                    "bytes_per_step": per_rank, "us_per_step": ms * 1e3,
-                    "peak_kind": f"{peak_kind} (copy)"}
-        head = head_roofline(chain, chain.stream, world, hbm, peak_kind)
+        # the dominant (only) kernel: the step's one launch; its bytes are this rank's weights
+        # and scales plus every projection's input row and output words
+        per_rank = total_bytes / world + sum(4 * K + 8 * N for _, N, K, _ in chain.plan)
+        ach = per_rank / (ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                "frac": ach / hbm,
+                "traffic": read_traffic("step_kernel_qwen3_0_6b_int8row.md", world),
+                "kernel": "step_kernel (the whole decode step, 113 projections + greedy token, "
+                          "one persistent launch" + (f", this rank's 1/{world} row shard"
+                                                     if world > 1 else "") + ")",
+                "bytes_per_launch": per_rank, "us_per_launch": ms * 1e3,
+                "peak_kind": f"{peak_kind} (copy)"}
+        head = None
         c1 = None if args.no_config1 else config1(world, max(3, min(args.steps, 50)))
         dec4 = None if args.no_4bit else decode_4bit(args, world, rank, group, hbm, peak_kind)
         prefill = None if args.no_prefill else prefill_bench(
@@ -781,12 +779,13 @@ def main():
                                    "token, M=1",
                        "weights_bytes_per_step": total_bytes, "format": fmt,
                        "parallelism": f"row-shard x{world}" + (" + all-gather per projection "
-                                                              "fused into the GEMV (tagged 8-byte "
-                                                              "words stored to every rank over "
-                                                              "NVLink)"
+                                                              "fused into the step kernel (tagged "
+                                                              "8-byte words stored to every rank "
+                                                              "over NVLink)"
                                                               if world > 1 else ""),
                        "l2": "weights 598 MB > 126 MB L2 (no flush needed)",
-                       "graph": "one CUDA graph per step, PDL launches"},
+                       "launch": "one persistent launch a step (otq_decode_step), replayed "
+                                 "from a CUDA graph"},
             "tok_s": 1e3 / ms,
             "hbm_frac": value / world / hbm,
             "roofline": roof,

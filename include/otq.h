@@ -210,7 +210,7 @@ OTQ_API int otq_qmm_chain(const otq_proj* projs, int count, void* stream);
  * such failure). */
 OTQ_API int otq_status_word(int* value, int reset);
 
-/* How long a kernel waits for tagged input words (otq_qmm_peer with wait != 0) on the current
+/* How long a kernel waits for tagged input words (otq_qmm_peer with wait != 0, otq_decode_step) on the current
  * device: `polls` reads of a word that has not arrived, with a short back-off between them,
  * before the wait gives up, sets bit 0 of the status word and lets the launch finish (its
  * outputs are then not valid). 0 restores the default of 2^22 polls (about a quarter of a
@@ -218,6 +218,74 @@ OTQ_API int otq_status_word(int* value, int reset);
  * turns into a status the host reads instead of a long stall. Applies to launches made after
  * the call. No counterpart in the reference. */
 OTQ_API int otq_set_wait_limit(uint32_t polls);
+
+/* ------------------------------------------------------------------ the decode step, one launch */
+
+/* Weight formats of otq_decode_step. */
+#define OTQ_STEP_RSC 0   /* int8 rows with a per-row fp32 scale (MM RSC) or UNIT: QACT + MM */
+#define OTQ_STEP_G32 1   /* 4-bit group-32 fp16-scale rows (otq_pack_g32): weight-only */
+
+/* One projection of otq_decode_step. */
+typedef struct otq_step_proj {
+  const uint8_t* rows;   /* RSC: int8 rows [N][rs]; G32: codes [N][rs] (K/2 bytes used).
+                            16-byte aligned, rs a multiple of 16 */
+  int64_t rs;
+  const uint8_t* srows;  /* RSC: scale rows [N][srs], Sw their first fp32 word, or NULL (UNIT);
+                            G32: fp16 scales [N][srs] (K/16 bytes used, 16-byte aligned, srs a
+                            multiple of 16) */
+  int64_t srs;
+  int64_t N;             /* this rank's rows (with world > 1: its contiguous row shard) */
+  int64_t K;             /* RSC: a multiple of 128; G32: of 256; at most 32640 */
+  int in;                /* -1: the input is x0; else the index of an earlier projection whose
+                            output row (its first K elements) is the input */
+  int fmt;               /* OTQ_STEP_RSC or OTQ_STEP_G32 */
+} otq_step_proj;
+
+#define OTQ_STEP_MAX 120
+
+typedef struct otq_step {
+  const otq_step_proj* projs;
+  int count;             /* 1 .. OTQ_STEP_MAX */
+  int rank, world;       /* world 1 .. 8: the projections' rows are split over the ranks */
+  int64_t delta[8];      /* byte distance from this rank's `out` to rank r's, as mapped here */
+  const float* x0;       /* the plain input row (16-byte aligned) */
+  float* out;            /* every projection's output row as tagged 8-byte words (fp32 value,
+                            32-bit tag), at the word offsets otq_step_layout gives: this rank's
+                            copy of a symmetric buffer (16-byte aligned), all zero before the
+                            first step */
+  int* counters;         /* 4 ints of this GPU's memory (16-byte aligned), zero before the first
+                            step: steps completed, CTAs done, the greedy token's accumulator */
+  int64_t* token;        /* the index of the first maximum of the last projection's full output
+                            row (the greedy token), or NULL */
+} otq_step;
+
+/* Word offsets of every projection's output row (offsets[count], may be NULL) and the words
+ * the buffer needs (total_words): each row N * world words, 16-byte aligned. */
+OTQ_API int otq_step_layout(const otq_step_proj* projs, int count, int world, int64_t* offsets,
+                            int64_t* total_words);
+
+/* Bytes of the device table otq_step_prepare writes (the projections' tensor maps and
+ * operands, read by the kernel; 128-byte aligned device memory of the caller). */
+OTQ_API int otq_step_table_bytes(int64_t* bytes);
+
+/* Checks a step and writes its table into `table` (synchronous: call it before any stream
+ * capture, and again when a pointer of the step changes). */
+OTQ_API int otq_step_prepare(const otq_step* step, void* table);
+
+/* One decode step -- every projection of one activation row in order, each reading an earlier
+ * one's output -- as ONE persistent launch (the reference's qwen3_step, opentpu/llm/qwen3.py:
+ * 1793, runs them as a sequence of QACT + MM programs, opentpu/isasim.py:749-959, with GATHER,
+ * :1413-1438, between row-sharded slices). Projections are ordered by their data: each output
+ * element is stored as a tagged word (with world > 1 also into every other rank's copy over
+ * NVLink: the all-gather fused in), and a projection reads its input words until their tags
+ * show the current step. RSC projections are bit-identical to otq_qmm; G32 ones are otq_linear_g32's
+ * arithmetic in another fp32 summation order. `table`: written by otq_step_prepare for this
+ * step. Steps must follow one another on one stream (a launch reads the step count the launch
+ * before advanced); with world > 1 every rank runs the same steps. A wait that runs out
+ * (otq_set_wait_limit) sets the status word. All CTAs must be resident at once (a cooperative
+ * launch of one CTA an SM). No counterpart in the reference (its projections are separate
+ * programs). */
+OTQ_API int otq_decode_step(const otq_step* step, const void* table, void* stream);
 
 /* ------------------------------------------------------------------ prefill GEMM */
 

@@ -32,6 +32,22 @@ class Peer(ctypes.Structure):
 TAGS_COUNTED, TAGS_STEPPED = 0, 1
 
 
+class StepProj(ctypes.Structure):
+    """struct otq_step_proj of include/otq.h: one projection of otq_decode_step."""
+    _fields_ = [("rows", c_void_p), ("rs", c_int64), ("srows", c_void_p), ("srs", c_int64),
+                ("N", c_int64), ("K", c_int64), ("input", c_int), ("fmt", c_int)]
+
+
+STEP_RSC, STEP_G32 = 0, 1
+
+
+class Step(ctypes.Structure):
+    """struct otq_step of include/otq.h: one decode step as one launch."""
+    _fields_ = [("projs", c_void_p), ("count", c_int), ("rank", c_int), ("world", c_int),
+                ("delta", c_int64 * 8), ("x0", c_void_p), ("out", c_void_p),
+                ("counters", c_void_p), ("token", c_void_p)]
+
+
 class GemmProj(ctypes.Structure):
     """struct otq_gemm_proj of include/otq.h: one projection of otq_gemm_w8a16_group."""
     _fields_ = [("flags", c_int), ("rows", c_void_p), ("rs", c_int64), ("srows", c_void_p),
@@ -59,6 +75,10 @@ SIGNATURES = {
     "otq_gemm_w8a16_group": (_I, [_P, _I, _P]),
     "otq_status_word": (_I, [_P, _I]),
     "otq_set_wait_limit": (_I, [ctypes.c_uint32]),
+    "otq_step_layout": (_I, [_P, _I, _I, _P, _P]),
+    "otq_step_table_bytes": (_I, [_P]),
+    "otq_step_prepare": (_I, [_P, _P]),
+    "otq_decode_step": (_I, [_P, _P, _P]),
     "otq_argmax": (_I, [_P, _L, _L, _P, _P]),
     "otq_argmax_noalloc": (_I, [_P, _L, _L, _P, _P]),
     "otq_pack_g32": (_I, [_P, _L, _L, _L, _P, _P, _P]),

@@ -428,7 +428,77 @@ int otq_status_word(int* value, int reset) {
 int otq_set_wait_limit(uint32_t polls) {
   int st = device_ok();
   if (st) return st;
-  return finish(set_tag_wait_limit(polls));
+  if ((st = set_tag_wait_limit(polls))) return finish(st);
+  return finish(set_step_wait_limit(polls));
+}
+
+int otq_step_layout(const otq_step_proj* projs, int count, int world, int64_t* offsets,
+                    int64_t* total_words) {
+  if (projs == nullptr || total_words == nullptr || count < 1 || count > OTQ_STEP_MAX ||
+      world < 1 || world > 8)
+    return kErrArg;
+  for (int i = 0; i < count; ++i)
+    if (projs[i].N <= 0) return kErrArg;
+  return step_layout(projs, count, world, offsets, total_words);
+}
+
+namespace {
+int check_step(const otq_step* s) {
+  if (s == nullptr || s->projs == nullptr || s->count < 1 || s->count > OTQ_STEP_MAX) return kErrArg;
+  if (s->world < 1 || s->world > 8 || s->rank < 0 || s->rank >= s->world) return kErrArg;
+  if (s->out == nullptr || s->counters == nullptr) return kErrArg;
+  if (!aligned(s->out, 16) || !aligned(s->counters, 16)) return kErrAlign;
+  for (int r = 0; r < s->world; ++r)
+    if (s->delta[r] % 16 || (r == s->rank && s->delta[r] != 0)) return kErrAlign;
+  if (s->token != nullptr && !aligned(s->token, 8)) return kErrAlign;
+  bool plain_in = false;
+  for (int i = 0; i < s->count; ++i) {
+    const otq_step_proj& p = s->projs[i];
+    const bool g32 = p.fmt == OTQ_STEP_G32;
+    if (p.fmt != OTQ_STEP_RSC && !g32) return kErrFormat;
+    if (p.N <= 0 || p.K <= 0 || p.K % (g32 ? 256 : OTQ_D) || p.K > 255 * OTQ_D) return kErrArg;
+    if (p.N * s->world >= (int64_t{1} << 30)) return kErrArg;
+    if (p.rows == nullptr || p.rs < (g32 ? p.K / 2 : p.K) || p.rs >= kStrideLimit) return kErrArg;
+    if (!aligned(p.rows, 16) || p.rs % 16) return kErrAlign;
+    if (g32) {
+      if (p.srows == nullptr || p.srs < p.K / 16 || p.srs >= kStrideLimit) return kErrArg;
+      if (!aligned(p.srows, 16) || p.srs % 16) return kErrAlign;
+    } else if (p.srows != nullptr && (!aligned(p.srows, 4) || p.srs % 4 || p.srs < 4 ||
+                                      p.srs >= kStrideLimit)) {
+      return kErrAlign;
+    }
+    if (p.in < -1 || p.in >= i) return kErrArg;   // an earlier projection, or the plain input
+    if (p.in == -1) plain_in = true;
+    else if (s->projs[p.in].N * s->world < p.K) return kErrArg;
+  }
+  if (plain_in && s->x0 == nullptr) return kErrArg;
+  if (plain_in && !aligned(s->x0, 16)) return kErrAlign;
+  return kOk;
+}
+}  // namespace
+
+int otq_step_table_bytes(int64_t* bytes) {
+  if (bytes == nullptr) return kErrArg;
+  *bytes = step_table_bytes();
+  return kOk;
+}
+
+int otq_step_prepare(const otq_step* s, void* table) {
+  int st = device_ok();
+  if (st) return st;
+  if ((st = check_step(s))) return st;
+  if (table == nullptr) return kErrArg;
+  if (!aligned(table, 128)) return kErrAlign;
+  return finish(step_prepare(s, table));
+}
+
+int otq_decode_step(const otq_step* s, const void* table, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if ((st = check_step(s))) return st;
+  if (table == nullptr) return kErrArg;
+  if (!aligned(table, 128)) return kErrAlign;
+  return finish(step_launch(s, table, static_cast<cudaStream_t>(stream)));
 }
 
 int otq_pack_g32(const float* W, int64_t N, int64_t K, int64_t ldw, uint8_t* codes,

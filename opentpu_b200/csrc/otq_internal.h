@@ -89,6 +89,12 @@ int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);    // gemv.cu
 int chain_launch(const otq_proj* projs, int count, cudaStream_t stream);
 int chain_reset();   // the grid barrier's count back to zero
 int set_tag_wait_limit(uint32_t polls);   // gemv.cu: otq_set_wait_limit
+int set_step_wait_limit(uint32_t polls);  // step.cu: otq_set_wait_limit
+// step.cu: the persistent decode step
+int step_layout(const otq_step_proj* projs, int count, int world, int64_t* offsets, int64_t* total);
+int64_t step_table_bytes();
+int step_prepare(const otq_step* step, void* table);
+int step_launch(const otq_step* step, const void* table, cudaStream_t stream);
 int* status_word();   // this device's status word (device address), or null
 
 // Launch with an optional programmatic-dependent-launch attribute (the kernel then may start

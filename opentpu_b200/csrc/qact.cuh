@@ -154,7 +154,9 @@ __device__ __forceinline__ bool behind(unsigned long long w, uint32_t expect) {
   return static_cast<int>(static_cast<uint32_t>(w >> 32) - expect) < 0;
 }
 
-template <int NT, class Emit4>
+// BAR: 0 -- the whole CTA meets on __syncthreads (NT = the CTA's threads); else the NT threads
+// 0 .. NT - 1 meet on named barrier BAR (the CTA's other threads do something else).
+template <int NT, int BAR = 0, class Emit4>
 __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, bool x4, float* xs,
                                                    int n, bool row_mode, uint32_t* segm,
                                                    uint32_t* red, Emit4 emit,
@@ -223,7 +225,7 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
   }
   tmax = __reduce_max_sync(0xFFFFFFFFu, tmax);
   if (lane == 0) red[warp] = tmax;
-  __syncthreads();
+  if constexpr (BAR == 0) { __syncthreads(); } else { asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory"); }
   // every warp reduces the warp maxima and derives the scales itself: one barrier, not two
   uint32_t m = lane < NW ? red[lane] : 0u;
   m = __reduce_max_sync(0xFFFFFFFFu, m);
@@ -243,7 +245,7 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
     const float scale = fmul(r.inv, pow2i(d));
     emit(i, q8(fmul(v.x, scale)), q8(fmul(v.y, scale)), q8(fmul(v.z, scale)), q8(fmul(v.w, scale)), d);
   }
-  __syncthreads();
+  if constexpr (BAR == 0) { __syncthreads(); } else { asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory"); }
   return r;
 }
 

@@ -59,6 +59,157 @@ def shard_rows(N: int, world: int, rank: int) -> tuple[int, int]:
     return rank * n, (rank + 1) * n
 
 
+def step_plan(shape: DecoderShape, fmt: str, head_fmt: str):
+    """(name, N, K, fmt) of every projection of a decode step, in order: per layer QKV, O,
+    GateUp, Down, then the head."""
+    H, d = shape.hidden, shape.head_dim
+    qkv = shape.n_q * d + 2 * shape.n_kv * d
+    layer = [("qkv", qkv, H), ("o", H, shape.n_q * d), ("gateup", 2 * shape.ffn, H),
+             ("down", H, shape.ffn)]
+    plan = [(f"layers.{i}.{n}", N, K, fmt) for i in range(shape.layers) for n, N, K in layer]
+    plan.append(("head", shape.vocab, H, head_fmt))
+    return plan
+
+
+def seeded_weights(plan, seed: int, world: int, rank: int, std: float = 0.02):
+    """The step's packed weights (this rank's row shard of each) and first-input rows, drawn
+    from one generator in plan order: every world size and rank sees the same matrices.
+    Returns (weights, inputs {K: [1, K]}, weight bytes of the whole step over all ranks)."""
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    weights, inputs, nbytes = [], {}, 0
+    for name, N, K, f in plan:
+        try:
+            n0, n1 = shard_rows(N, world, rank)
+        except ValueError as e:
+            raise ValueError(f"{name}: {e}") from None
+        W = torch.randn((N, K), generator=gen, device="cuda")[n0:n1] * std
+        w = linear.PackedWeight.from_float(W, f)
+        del W
+        weights.append(w)
+        nbytes += w.stream_bytes * world
+        if K not in inputs:
+            inputs[K] = torch.randn((1, K), generator=gen, device="cuda")
+    return weights, inputs, nbytes
+
+
+class DecodeStep:
+    """The decode step as ONE persistent launch (otq_decode_step): the same projections, seeded
+    weights and chaining as DecodeChain(dependent=True) -- each projection reads the first K
+    outputs of the one before, the first reads a fixed input -- ordered by tagged output words
+    instead of kernel boundaries, the greedy token folded into the head's epilogue. Layers in
+    int8-row (bit-identical to DecodeChain) or int4-g32 (weight-only, fp32 sums in another
+    order than otq_linear_g32's); the head in int8-row. With world > 1 the rows are sharded and
+    every output word is stored into every rank's copy of a symmetric buffer over NVLink (the
+    all-gather fused in): bit-identical to one GPU."""
+
+    def __init__(self, shape: DecoderShape, fmt: str = "int8-row", head_fmt: str = "int8-row",
+                 seed: int = 0, world: int = 1, rank: int = 0, group=None):
+        import ctypes
+        from . import _lib as L
+        if fmt not in ("int8-row", "int4-g32") or head_fmt != "int8-row":
+            raise ValueError("the persistent decode step takes int8-row or int4-g32 layers and "
+                             "an int8-row head")
+        self.shape, self.world, self.rank, self.group = shape, world, rank, group
+        self.plan = step_plan(shape, fmt, head_fmt)
+        self.weights, self.inputs, self.weight_bytes = seeded_weights(self.plan, seed, world, rank)
+        n = len(self.plan)
+        self.projs = (L.StepProj * n)()
+        for i, w in enumerate(self.weights):
+            p = self.projs[i]
+            p.rows, p.rs = w.rows.data_ptr(), w.rows.stride(0)
+            p.srows = w.srows.data_ptr()
+            p.srs = w.srows.stride(0) * w.srows.element_size()
+            p.N, p.K, p.input = w.N, w.K, i - 1
+            p.fmt = L.STEP_G32 if w.fmt == "int4-g32" else L.STEP_RSC
+        offs = (ctypes.c_int64 * n)()
+        total = ctypes.c_int64(0)
+        L.call("otq_step_layout", ctypes.addressof(self.projs), n, world, ctypes.addressof(offs),
+               ctypes.byref(total))
+        self.offsets = list(offs)
+        words = total.value
+        if world > 1:
+            import torch.distributed as dist
+            import torch.distributed._symmetric_memory as symm
+            try:
+                symm.set_backend("CUDA")
+            except Exception:
+                pass
+            buf = symm.empty(2 * words, dtype=torch.float32, device="cuda")
+            buf.zero_()
+            grp = group if group is not None else dist.group.WORLD
+            handle = symm.rendezvous(buf, grp)
+            torch.cuda.synchronize()
+            dist.barrier(group=grp)
+            ptrs = handle.buffer_ptrs
+        else:
+            buf = torch.zeros(2 * words, dtype=torch.float32, device="cuda")
+            handle, ptrs = None, [buf.data_ptr()]
+        self._buf = (buf, handle)
+        self.counters = torch.zeros(4, dtype=torch.int32, device="cuda")
+        self.token = torch.zeros(2, dtype=torch.int64, device="cuda")
+        self.x0 = self.inputs[self.plan[0][2]]
+        st = L.Step()
+        st.projs, st.count, st.rank, st.world = ctypes.addressof(self.projs), n, rank, world
+        for r in range(world):
+            st.delta[r] = ptrs[r] - ptrs[rank]
+        st.x0, st.out = self.x0.data_ptr(), buf.data_ptr()
+        st.counters, st.token = self.counters.data_ptr(), self.token.data_ptr()
+        self.step_args = st
+        nb = ctypes.c_int64(0)
+        L.call("otq_step_table_bytes", ctypes.byref(nb))
+        self.table = torch.empty(nb.value, dtype=torch.uint8, device="cuda")
+        L.call("otq_step_prepare", ctypes.addressof(st), self.table.data_ptr())
+        self.graph = None
+        self.stream = torch.cuda.Stream()
+
+    @property
+    def launches(self) -> int:
+        return 1
+
+    def full_out(self, i: int) -> torch.Tensor:
+        """Projection i's whole output row [1, N] (the values of its tagged words)."""
+        N = self.plan[i][1]
+        o = self.offsets[i]
+        return self._buf[0][2 * o:2 * (o + N)].view(N, 2)[:, 0].unsqueeze(0)
+
+    def logits(self) -> torch.Tensor:
+        return self.full_out(len(self.plan) - 1)
+
+    def step_eager(self):
+        import ctypes
+        from . import _lib as L
+        L.call("otq_decode_step", ctypes.addressof(self.step_args), self.table.data_ptr(),
+               torch.cuda.current_stream().cuda_stream)
+
+    def capture(self, warmup: int = 3):
+        with torch.cuda.stream(self.stream):
+            for _ in range(warmup):
+                self.step_eager()
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.step_eager()
+        torch.cuda.synchronize()
+
+    def replay(self, n: int = 1):
+        with torch.cuda.stream(self.stream):
+            for _ in range(n):
+                self.graph.replay()
+
+    def run_host(self, inputs_host: dict, token_host: torch.Tensor):
+        """One step from host buffers: the first input copied from pinned host memory, the
+        step, the greedy token copied back into token_host (pinned; all asynchronous on the
+        step's stream)."""
+        K = self.plan[0][2]
+        with torch.cuda.stream(self.stream):
+            self.x0.copy_(inputs_host[K], non_blocking=True)
+            self.graph.replay()
+            token_host.copy_(self.token[:1], non_blocking=True)
+
+    def release(self):
+        self.graph = None
+
+
 class DecodeChain:
     def __init__(self, shape: DecoderShape, fmt: str = "int8-row", head_fmt: str = "int8-row",
                  seed: int = 0, world: int = 1, rank: int = 0, group=None, pdl: bool = True,
@@ -77,33 +228,15 @@ class DecodeChain:
         # Qwen3-0.6B step: per projection the grid barrier and the QACT prologue cost as much as
         # a launch, and a warp's ring holds under one projection of look-ahead), so it is opt-in.
         self.chained = bool(chained)
-        H, d = shape.hidden, shape.head_dim
-        qkv = shape.n_q * d + 2 * shape.n_kv * d
-        layer = [("qkv", qkv, H), ("o", H, shape.n_q * d), ("gateup", 2 * shape.ffn, H),
-                 ("down", H, shape.ffn)]
-        self.plan = [(f"layers.{i}.{n}", N, K, fmt) for i in range(shape.layers)
-                     for n, N, K in layer]
-        self.plan.append(("head", shape.vocab, H, head_fmt))
-        gen = torch.Generator(device="cuda").manual_seed(seed)
-        self.weights, self.outs, self.gathered = [], [], []
-        self.inputs: dict[int, torch.Tensor] = {}
-        self.weight_bytes = 0
-        for name, N, K, f in self.plan:
-            try:
-                n0, n1 = shard_rows(N, world, rank)
-            except ValueError as e:
-                raise ValueError(f"{name}: {e}") from None
-            n = n1 - n0
-            W = torch.randn((N, K), generator=gen, device="cuda")[n0:n1] * std
-            w = linear.PackedWeight.from_float(W, f)
-            del W
-            self.weights.append(w)
-            self.weight_bytes += w.stream_bytes * world
-            if K not in self.inputs:
-                self.inputs[K] = torch.randn((1, K), generator=gen, device="cuda")
-            if not self.fused:
-                self.outs.append(torch.zeros((1, n), device="cuda"))
-                self.gathered.append(torch.zeros((world, n), device="cuda") if world > 1 else None)
+        self.plan = step_plan(shape, fmt, head_fmt)
+        self.weights, self.inputs, self.weight_bytes = seeded_weights(self.plan, seed, world,
+                                                                      rank, std)
+        self.outs, self.gathered = [], []
+        if not self.fused:
+            for w in self.weights:
+                self.outs.append(torch.zeros((1, w.N), device="cuda"))
+                self.gathered.append(torch.zeros((world, w.N), device="cuda") if world > 1
+                                     else None)
         if self.fused:
             self._symmetric_outputs()
         # the input each projection reads: a fixed vector, or the previous projection's output

@@ -1,19 +1,26 @@
 """A Qwen3-shaped decoder whose projections are this library's quantized linear layer.
 
 The float math around the projections follows the reference's fp32 model
-(opentpu/llm/qwen3.py:701-743 reference_logits), one token at a time with a KV cache:
+(opentpu/llm/qwen3.py:701-743 reference_logits):
 
     x = embed[token]
     per layer: h = rmsnorm(x); q, k, v = h @ Wqkv^T (one QACT + MM: q, k and v share the input
                and its QACT range); per-head rmsnorm of q and k; RoPE (rotate-half, tables from
                float64); causal softmax attention over the cache (GQA); x += o @ Wo^T;
-               h = rmsnorm(x); g, u = h @ Wgateup^T (one QACT + MM); x += (silu(g) * u) @ Wdown^T
+               h = rmsnorm(x); g, u = h @ Wgateup^T (one QACT + MM);
+               x += (silu(g) * u) @ Wdown^T, the down projection's input quantized in QACT
+               ranges of `down_chunk` columns, one MM each, later ones added in order (ACC), as
+               the reference's MLP kernel does (kernels/mlp.py:8-30; compiler.py:2622-2726)
     logits = rmsnorm(x) @ Whead^T (Whead = embed, tied as in Qwen3-0.6B)
 
+`prefill(prompt)` runs the prompt's rows together (each projection one launch over all rows:
+QACT is per row, so each row's bits are those of a row alone), `step(token)` one token with the
+KV cache, and `generate` picks each next token on the device (otq_argmax: the first maximal
+logit, the reference's greedy sink, opentpu/llm/generate.py:252-280).
+
 Every projection runs through linear.qlinear (QACT + MM bit-exact with the reference's MM for
-the MX formats; weight-only fp32 accumulation for int4-g32); the norms, RoPE, attention and
-SwiGLU are fp32 torch on the GPU. Greedy decoding takes the first maximal logit (the
-reference's greedy sink, opentpu/llm/generate.py:252-280).
+the MX formats and int8-row; weight-only fp32 accumulation for int4-g32); the norms, RoPE,
+attention and SwiGLU are fp32 torch on the GPU.
 """
 from __future__ import annotations
 
@@ -23,14 +30,50 @@ import torch
 from . import linear
 from . import workloads as WL
 
+D = 128
+
+
+def reference_down_chunk(F: int, fmt: str) -> int | None:
+    """The QACT range of the down projection's input in the reference's MLP (kernels/mlp.py:8-30
+    _chunk / down_chunk: about F/8 columns, a multiple of D -- 2D for 4-bit rows -- and at least
+    2D where F allows); None for the weight-only int4-g32 (no QACT)."""
+    if fmt == "int4-g32":
+        return None
+    q = D if fmt in ("int8", "int8-row") else 2 * D
+    if F % q:
+        raise ValueError(f"F {F} is not a multiple of {q}")
+    lo = min(F, -(-2 * D // q) * q)
+    c = max(lo, (F // 8) // q * q)
+    while F % c and c > lo:
+        c -= q
+    while F % c:
+        c += q
+    return c
+
+
+def column_parts(w: linear.PackedWeight, C: int) -> list:
+    """The weight's column blocks of C as PackedWeights (views of its rows; MX scale rows read
+    from block k0 = c0 / 128): MM over one QACT range each (quant.column_parts' layout)."""
+    parts = []
+    for c0 in range(0, w.K, C):
+        if w.fmt in ("int8", "int8-row"):
+            rows = w.rows[:, c0:c0 + C]
+        else:
+            rows = w.rows[:, c0 // 2:(c0 + C) // 2]
+        parts.append(linear.PackedWeight(w.fmt, w.N, C, rows, w.srows, w.k0 + c0 // D, w.rsc))
+    return parts
+
 
 class Qwen3Decoder:
     def __init__(self, shape: WL.DecoderShape, weights: dict, fmt: str = "int8-row",
-                 head_fmt: str = "int8-row", max_pos: int = 1024, device: str = "cuda"):
+                 head_fmt: str = "int8-row", max_pos: int = 1024, device: str = "cuda",
+                 down_chunk="reference"):
         self.shape, self.fmt, self.head_fmt, self.max_pos = shape, fmt, head_fmt, max_pos
         dev = torch.device(device)
         H, d = shape.hidden, shape.head_dim
         self.d = d
+        dc = reference_down_chunk(shape.ffn, fmt) if down_chunk == "reference" else down_chunk
+        self.down_chunk = dc if dc and dc < shape.ffn else None
 
         def t(a):
             return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
@@ -55,6 +98,8 @@ class Qwen3Decoder:
                                             weights[p + "mlp.up_proj.weight"]]), fmt),
                 "down": q(weights[p + "mlp.down_proj.weight"], fmt),
             }
+            L["down_parts"] = column_parts(L["down"], self.down_chunk) if self.down_chunk \
+                else [L["down"]]
             if shape.qk_norm:
                 L["qn"] = t(weights[p + "self_attn.q_norm.weight"])
                 L["kn"] = t(weights[p + "self_attn.k_norm.weight"])
@@ -65,63 +110,103 @@ class Qwen3Decoder:
         self.K = torch.zeros((shape.layers, max_pos, shape.n_kv, d), device=dev)
         self.V = torch.zeros_like(self.K)
         self.pos = 0
+        self.token = torch.zeros(2, dtype=torch.int64, device=dev)
 
     def _norm(self, v, g):
         return (v / torch.sqrt(torch.mean(v * v, dim=-1, keepdim=True) + self.shape.eps)) * g
 
     def _rot(self, v, pos):
+        """RoPE of v [..., n_heads, d] at positions pos (an int, or a tensor of T positions for
+        v [T, n_heads, d])."""
         h = self.d // 2
         c, s = self.cos[pos], self.sin[pos]
+        if isinstance(pos, torch.Tensor):
+            c, s = c[:, None, :], s[:, None, :]
         v1, v2 = v[..., :h], v[..., h:]
         return torch.cat([v1 * c - v2 * s, v2 * c + v1 * s], dim=-1)
+
+    def _down(self, a, L):
+        """The down projection of a [M, F] over its QACT ranges (ACC in range order)."""
+        parts = L["down_parts"]
+        if len(parts) == 1:
+            return linear.qlinear(a, parts[0])
+        C = self.down_chunk
+        y = linear.qlinear(a[..., :C], parts[0])
+        for i, w in enumerate(parts[1:], 1):
+            linear.qlinear(a[..., i * C:(i + 1) * C], w, out=y, acc=True)
+        return y
+
+    def _layers(self, x, pos0: int):
+        """x [T, H] at positions pos0 .. pos0 + T - 1 through every layer (the KV cache holds
+        positions < pos0 and receives these)."""
+        sh, d = self.shape, self.d
+        T = x.shape[0]
+        G = sh.n_q // sh.n_kv
+        nq, nk = sh.n_q * d, sh.n_kv * d
+        pos = torch.arange(pos0, pos0 + T, device=x.device)
+        end = pos0 + T
+        causal = None
+        if T > 1:
+            causal = torch.full((T, end), float("-inf"), device=x.device).triu(pos0 + 1)
+        for i, L in enumerate(self.layers):
+            h = self._norm(x, L["in"])
+            qkv = linear.qlinear(h, L["qkv"])
+            q = qkv[:, :nq].reshape(T, sh.n_q, d)
+            k = qkv[:, nq:nq + nk].reshape(T, sh.n_kv, d)
+            v = qkv[:, nq + nk:].reshape(T, sh.n_kv, d)
+            if sh.qk_norm:
+                q, k = self._norm(q, L["qn"]), self._norm(k, L["kn"])
+            q, k = self._rot(q, pos), self._rot(k, pos)
+            self.K[i, pos0:end] = k
+            self.V[i, pos0:end] = v
+            Kc = self.K[i, :end].repeat_interleave(G, dim=1)      # [end, n_q, d]
+            Vc = self.V[i, :end].repeat_interleave(G, dim=1)
+            s = torch.einsum("thd,uhd->htu", q, Kc) / float(np.sqrt(d))
+            if causal is not None:
+                s = s + causal
+            p = torch.exp(s - s.max(dim=-1, keepdim=True).values)
+            o = torch.einsum("htu,uhd->thd", p / p.sum(dim=-1, keepdim=True), Vc)
+            x = x + linear.qlinear(o.reshape(T, -1), L["o"])
+            h = self._norm(x, L["post"])
+            gu = linear.qlinear(h, L["gateup"])
+            g, u = gu[:, :sh.ffn], gu[:, sh.ffn:]
+            x = x + self._down((g / (1 + torch.exp(-g))) * u, L)
+        return x
 
     def reset(self):
         self.pos = 0
 
+    def prefill(self, prompt: list) -> torch.Tensor:
+        """The prompt's tokens at positions 0 .. T - 1, all rows of a projection in one launch:
+        the logits [vocab] (fp32) after its last token."""
+        T = len(prompt)
+        if T > self.max_pos:
+            raise ValueError(f"a prompt of {T} past the cache ({self.max_pos})")
+        self.pos = 0
+        ids = torch.tensor(prompt, dtype=torch.long, device=self.embed.device)
+        x = self._layers(self.embed[ids].clone(), 0)
+        self.pos = T
+        return linear.qlinear(self._norm(x[-1:], self.norm), self.head).reshape(-1)
+
     def step(self, token: int) -> torch.Tensor:
         """One decode step at the next position: the logits [vocab] (fp32)."""
-        sh, d, pos = self.shape, self.d, self.pos
-        if pos >= self.max_pos:
-            raise ValueError(f"position {pos} past the cache ({self.max_pos})")
-        G = sh.n_q // sh.n_kv
-        x = self.embed[token].clone()
-        for i, L in enumerate(self.layers):
-            h = self._norm(x, L["in"])
-            qkv = linear.qlinear(h, L["qkv"])
-            nq, nk = sh.n_q * d, sh.n_kv * d
-            q = qkv[:nq].view(sh.n_q, d)
-            k = qkv[nq:nq + nk].view(sh.n_kv, d)
-            v = qkv[nq + nk:].view(sh.n_kv, d)
-            if sh.qk_norm:
-                q, k = self._norm(q, L["qn"]), self._norm(k, L["kn"])
-            q, k = self._rot(q, pos), self._rot(k, pos)
-            self.K[i, pos] = k
-            self.V[i, pos] = v
-            Kc = self.K[i, :pos + 1].repeat_interleave(G, dim=1)      # [T, n_q, d]
-            Vc = self.V[i, :pos + 1].repeat_interleave(G, dim=1)
-            s = torch.einsum("hd,thd->ht", q, Kc) / float(np.sqrt(d))
-            p = torch.exp(s - s.max(dim=1, keepdim=True).values)
-            o = torch.einsum("ht,thd->hd", p / p.sum(dim=1, keepdim=True), Vc)
-            x = x + linear.qlinear(o.reshape(-1), L["o"])
-            h = self._norm(x, L["post"])
-            gu = linear.qlinear(h, L["gateup"])
-            g, u = gu[:sh.ffn], gu[sh.ffn:]
-            x = x + linear.qlinear((g / (1 + torch.exp(-g))) * u, L["down"])
+        if self.pos >= self.max_pos:
+            raise ValueError(f"position {self.pos} past the cache ({self.max_pos})")
+        x = self._layers(self.embed[token].clone().reshape(1, -1), self.pos)
         self.pos += 1
-        return linear.qlinear(self._norm(x, self.norm), self.head)
+        return linear.qlinear(self._norm(x, self.norm), self.head).reshape(-1)
 
-    def generate(self, prompt: list, n_new: int):
-        """Greedy decoding: the prompt token by token, then n_new tokens each the first maximal
-        logit of the step before. Returns (new tokens, the logits of every step after the
-        prompt's last token as a host array [n_new, vocab])."""
-        self.reset()
-        logits = None
-        for tk in prompt:
-            logits = self.step(tk)
+    def generate(self, prompt: list, n_new: int, keep_logits: bool = True):
+        """Greedy decoding: the prompt (prefill), then n_new tokens, each the first maximal
+        logit of the step before (on the device). Returns (new tokens, the logits of every step
+        that chose one, as a host array [n_new, vocab], or None)."""
+        logits = self.prefill(prompt)
         out, rows = [], []
         for _ in range(n_new):
-            tk = int(torch.argmax(logits).item())
+            linear.argmax(logits, out=self.token)
+            tk = int(self.token[0].item())
             out.append(tk)
-            rows.append(logits.float().cpu().numpy())
+            if keep_logits:
+                rows.append(logits.float().cpu().numpy())
             logits = self.step(tk)
-        return out, np.stack(rows)
+        return out, (np.stack(rows) if keep_logits else None)

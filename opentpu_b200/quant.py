@@ -308,7 +308,11 @@ def quantize(W: np.ndarray, fmt: str, g: int | None = None, scale: str | None = 
         codes = torch.stack([lo, hi], -1).reshape(N, K)
         codes = torch.where(codes >= 8, codes - 16, codes).to(torch.float64)
         s = w.srows.to(torch.float64)
-        deq = (codes.reshape(N, K // 32, 32) * s[..., None]).reshape(N, K).float()
+        deq = (codes.reshape(N, K // 32, 32) * s[..., None]).reshape(N, K)
+        # an element that rounds to 0 keeps the sign of rint(x / s), i.e. of x (the reference's
+        # clip(rint(x / s)) * s in float64)
+        deq = torch.where(codes == 0, torch.copysign(torch.zeros_like(deq),
+                                                     _dev(W).to(torch.float64)), deq).float()
         return Quantized(fmt, _host(deq), np.zeros(0), _host(s), g, 4 + SCALE_BITS[scale] / g)
     raise ValueError(f"unknown format {fmt!r}" if fmt not in ("mxfp4", "nvfp4", "e2m1", "int4k",
                                                               "e2m1k")
@@ -427,7 +431,9 @@ def fake_act(x, D: int = 128, n: int | None = None, row: bool = False,
         fm, em = torch.frexp(amax.expand_as(ag))
         d = torch.where(ag > 0, torch.clamp(em.long() - ea.long() - (fa > fm).long(), 0, 31),
                         torch.zeros((), dtype=torch.int64, device=ag.device))
-    s = torch.where(amax == 0, torch.ones_like(amax), amax / 127)
+    # a tensor divisor: PyTorch turns division by a Python scalar into a multiplication by its
+    # reciprocal, which is not the reference's correctly rounded amax / 127
+    s = torch.where(amax == 0, torch.ones_like(amax), amax / torch.full_like(amax, 127.0))
     unit = s * torch.exp2(-d.to(torch.float64))
     r = xb / unit[..., None]
     q = torch.round(r)                                   # half to even, as numpy's rint
@@ -442,7 +448,8 @@ def fake_act(x, D: int = 128, n: int | None = None, row: bool = False,
         q[b] = torch.where(tie[b], qd, q[b])
     vals = (torch.clamp(q, -127, 127) * unit[..., None]).reshape(sh)
     da = d.repeat_interleave(g * NVG // D, dim=-1).reshape(*sh[:-1], K // (D // NVG))
-    return MXAct.of(_host(vals), _host(da))
+    # the reference's offsets are frexp's int32 exponents (row mode: an int64 zero array)
+    return MXAct.of(_host(vals), _host(da).astype(np.int64 if row else np.int32))
 
 
 def mx_matmul(h, w: np.ndarray, dw: np.ndarray | None = None, W: int = 16,

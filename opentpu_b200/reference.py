@@ -84,7 +84,8 @@ def _attention(q, k, v, n_kv_heads):
     G = Hq // n_kv_heads
     kk = k.repeat_interleave(G, dim=0)                       # [Hq, T, d]
     vv = v.repeat_interleave(G, dim=0)
-    s = torch.einsum("htd,hd->ht", kk, q) / np.sqrt(d)
+    s = torch.einsum("htd,hd->ht", kk, q)
+    s = s / torch.full_like(s, float(np.sqrt(d)))   # a true division, as numpy's
     p = (s - s.amax(-1, keepdim=True)).exp()
     return torch.einsum("ht,htd->hd", p / p.sum(-1, keepdim=True), vv)
 

@@ -323,11 +323,42 @@ def mm(q, Sa, da, rows, srows, fmt: str, K: int, *, D: int = 128, k0: int = 0,
     return y, total
 
 
+def mm_plain(q, Sa, da, rows, srows, fmt: str, K: int, *, unit: bool = False,
+             out=None, acc: bool = False):
+    """MM for weights whose multipliers are 1 and offsets 0 (RSC or UNIT rows, any format): the
+    same results as `mm`, by one float64 matrix product. With m = 1 and dw = 0 a group's
+    multiplier 2^(W - da) depends on the activation alone, so the activation bytes are scaled by
+    it (0 where the group is dropped) and acc = A' @ w^T: every product and every partial sum
+    is an integer below 2^53 (|acc| <= 2^16 * 127 * 127 * K), so the float64 product is exact
+    in any summation order. Returns (y fp32 [M, N], acc int64 [M, N])."""
+    q = np.asarray(q, np.int8)
+    M = q.shape[0]
+    W = WINDOW[fmt]
+    N = np.asarray(rows).shape[0]
+    if (1 << W) * 127 * 127 * K >= 2 ** 53:
+        raise ValueError("mm_plain: K too large for an exact float64 product")
+    da = np.asarray(da, np.int64).reshape(M, K // 32)
+    sh = W - da
+    mult = np.where(sh >= 0, np.exp2(np.maximum(sh, 0).astype(np.float64)), 0.0)
+    a = (q.astype(np.float64).reshape(M, K // 32, 32) * mult[..., None]).reshape(M, K)
+    w = elements(rows, fmt, K).astype(np.float64)
+    total = np.rint(a @ w.T).astype(np.int64)
+    Sw = np.ones(N, np.float32) if unit else \
+        np.ascontiguousarray(np.asarray(srows, np.uint8)[:, :4]).view(np.float32).reshape(N)
+    y = F.fmul(F.fmul(F.i2f(total), Sw[None, :]),
+               F.fmul(np.asarray(Sa, np.float32)[:, None], np.float32(2.0 ** -W)))
+    if acc:
+        y = F.fadd(out, y)
+    return y, total
+
+
 def qlinear(x, rows, srows, fmt: str, *, D: int = 128, rsc: bool = False, row_mode: bool = False,
             k0: int = 0):
     """QACT over the whole row (one range) followed by one MM: y fp32 [M, N]."""
     x = np.atleast_2d(np.asarray(x, np.float32))
     q, S, d = F.quantize_rows(x, D // SUB, row_mode)
+    if rsc:
+        return mm_plain(q, S, d, rows, srows, fmt, x.shape[1])[0]
     return mm(q, S, d, rows, srows, fmt, x.shape[1], D=D, rsc=rsc, k0=k0)[0]
 
 

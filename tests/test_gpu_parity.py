@@ -308,28 +308,33 @@ def test_decode_chain_chained_equals_launch_per_projection():
 
 
 # ---------------------------------------------------------------------------- token level
-def _near_tie_check(dev_logits, ref_logits, tokens):
-    """The reference's rule for a greedy run against a golden, teacher forced on the device's
-    tokens (tests/test_validate.py:124-164 _top1_where_clear): at every step whose golden top-1
-    leads its runner-up by more than the noise (here: 8x the largest |device - golden| logit
-    difference of the run, itself bounded by the cosine check), the device's token is the
-    golden's first maximal logit. Returns the number of steps that were clear."""
-    diff = np.abs(dev_logits - ref_logits).max()
+def _token_parity(dev_tokens, dev_logits, ora, prompt, min_cos=0.9999):
+    """The reference's rule for a greedy run against a golden (tests/test_validate.py:124-164
+    _top1_where_clear), teacher forced on the device's tokens: at every step whose golden top-1
+    leads its runner-up by more than the golden's own noise floor (the largest logit change
+    1-ulp input noise causes, tools/validate.py Golden._noisy; a fixed threshold, not the run's
+    own error), the device's token is the golden's first maximal logit. The device's logits
+    must also follow the golden's (cosine). Returns (clear steps, floor)."""
+    from oracle.model import clear_steps, noise_floor
+    ref = ora.forced(prompt, dev_tokens)
+    floor = noise_floor(ora, prompt, dev_tokens, ref)
+    clear = clear_steps(ref, floor)
     cos = [float(np.dot(a, b) / np.linalg.norm(a) / np.linalg.norm(b))
-           for a, b in zip(dev_logits, ref_logits)]
-    assert min(cos) > 0.99999, min(cos)
-    top2 = np.sort(ref_logits, -1)[:, -2:]
-    clear = top2[:, 1] - top2[:, 0] > 8 * diff
-    assert (np.array(tokens)[clear] == ref_logits.argmax(-1)[clear]).all()
-    return int(clear.sum())
+           for a, b in zip(dev_logits.astype(np.float64), ref.astype(np.float64))]
+    assert min(cos) > min_cos, min(cos)
+    tokens = np.array(dev_tokens)
+    bad = np.nonzero(clear & (tokens != ref.argmax(-1)))[0]
+    assert bad.size == 0, f"clear steps {bad.tolist()} differ (floor {floor})"
+    print(f"clear steps {int(clear.sum())} of {len(tokens)}, noise floor {floor:.3g}")
+    return int(clear.sum()), floor
 
 
 @pytest.mark.parametrize("fmt,head_fmt", [("int8-row", "int8-row"), ("int4-g32", "int8-row"),
-                                          ("int4", "int8-row")])
+                                          ("int4", "int8-row"), ("int8", "int8")])
 def test_tiny_decode_tokens_match_oracle(fmt, head_fmt):
     """Greedy decode of the tiny Qwen3 shape (the reference's test model geometry) through the
-    quantized linear layer: every clear step's token is the oracle's (the same model on the CPU
-    with the reference's quantized arithmetic); the logits agree to cos > 0.99999."""
+    quantized linear layer, the prompt prefilled in one pass: every clear step's token is the
+    oracle's (the same model on the CPU with the reference's quantized arithmetic)."""
     from oracle.model import Qwen3Oracle
     from opentpu_b200.model import Qwen3Decoder
     shape = WL.TINY
@@ -338,26 +343,54 @@ def test_tiny_decode_tokens_match_oracle(fmt, head_fmt):
     dec = Qwen3Decoder(shape, W, fmt=fmt, head_fmt=head_fmt, max_pos=64)
     tokens, dev = dec.generate(prompt, 12)
     ora = Qwen3Oracle(shape, W, fmt=fmt, head_fmt=head_fmt, rope=lambda p: WL.rope_tables(shape, p))
-    ref = ora.forced(prompt, tokens)
-    assert _near_tie_check(dev, ref, tokens) >= 10
+    clear, _ = _token_parity(tokens, dev, ora, prompt)
+    assert clear >= 6
 
 
-@pytest.mark.slow
-def test_qwen3_0_6b_4bit_decode_tokens_match_oracle():
-    """The seeded Qwen3-0.6B shape with 4-bit group-32 fp16-scale layers and the int8 per-row
-    LM head (configuration 3's formats), a random prompt then greedy tokens: every clear step's
-    token is the oracle's. (Prompt and generation shortened from 512 + 64 to keep the CPU
-    oracle to about a minute; the arithmetic per step is the configuration's.)"""
+def test_prefill_equals_token_by_token():
+    """The prefill's rows through one launch a projection give the same logits as the prompt fed
+    token by token (QACT per row: each row's bytes are those of the row alone; the fp32 torch
+    attention may differ in its last bits)."""
+    from opentpu_b200.model import Qwen3Decoder
+    shape = WL.TINY
+    W = WL.decoder_weights(shape, seed=4)
+    prompt = WL.prompt_ids(shape, 16, seed=5)
+    dec = Qwen3Decoder(shape, W, max_pos=32)
+    a = dec.prefill(prompt).cpu().numpy()
+    dec.reset()
+    for tk in prompt:
+        b = dec.step(tk)
+    b = b.cpu().numpy()
+    assert np.abs(a - b).max() <= 1e-4 * np.abs(b).max()
+
+
+def _qwen3_full_length(fmt, head_fmt):
+    """BASELINE configurations 2 and 3 at full length: the seeded Qwen3-0.6B shape, a random
+    512-token prompt (prefilled), 64 greedy tokens on the device; the oracle teacher forced on
+    the device's tokens over the same 576 positions."""
     from oracle.model import Qwen3Oracle
     from opentpu_b200.model import Qwen3Decoder
     shape = WL.QWEN3_0_6B
     W = WL.decoder_weights(shape, seed=0)
-    prompt = WL.prompt_ids(shape, 32, seed=0)
-    dec = Qwen3Decoder(shape, W, fmt="int4-g32", head_fmt="int8-row", max_pos=64)
-    tokens, dev = dec.generate(prompt, 16)
+    prompt = WL.prompt_ids(shape, 512, seed=0)
+    dec = Qwen3Decoder(shape, W, fmt=fmt, head_fmt=head_fmt, max_pos=576)
+    tokens, dev = dec.generate(prompt, 64)
     del dec
     torch.cuda.empty_cache()
-    ora = Qwen3Oracle(shape, W, fmt="int4-g32", head_fmt="int8-row",
+    ora = Qwen3Oracle(shape, W, fmt=fmt, head_fmt=head_fmt,
                       rope=lambda p: WL.rope_tables(shape, p))
-    ref = ora.forced(prompt, tokens)
-    assert _near_tie_check(dev, ref, tokens) >= 12
+    return _token_parity(tokens, dev, ora, prompt)
+
+
+@pytest.mark.slow
+def test_qwen3_0_6b_int8_row_decode_512_64_tokens_match_oracle():
+    """Configuration 2: int8 per-row layers and head."""
+    clear, _ = _qwen3_full_length("int8-row", "int8-row")
+    assert clear >= 16
+
+
+@pytest.mark.slow
+def test_qwen3_0_6b_4bit_decode_512_64_tokens_match_oracle():
+    """Configuration 3: int4 group-32 fp16-scale layers (weight-only), int8 per-row head."""
+    clear, _ = _qwen3_full_length("int4-g32", "int8-row")
+    assert clear >= 16
