@@ -28,11 +28,13 @@ Objects of the same line:
   rotating pool of 256 distinct weight copies (257 MB > 2 x L2) and L2-resident.
 - "decode_4bit": configuration 3 (int4-g32 layers, int8-row head) with its own roofline, CPU
   baseline and closed-loop e2e.
+- "phi4_sweep": configuration 5 (Phi-4-mini projections and head, int8-row and int4-g32, batch
+  1 / 8 / 64, row-sharded with an all-gather per output when N > 1).
 - "prefill": configuration 4 (36 SmolLM3-3B-shaped int8-row layers, 512 bf16 tokens, tcgen05
   GEMM); with N > 1 each projection's rows are sharded and its output all-gathered (NCCL) in the
   timed graph, and rank 0 checks layer 0 against the unsharded GEMM within the tolerance.
 
---profile head|step|prefill|g32 runs a few launches and exits (the commands the ncu summaries
+--profile head|step|prefill|g32|stepkernel|stepkernel4 runs a few launches and exits (the commands the ncu summaries
 under profiles/ were captured with). --impl reference times the reference's CPU algorithm (the
 numpy port under oracle/, the same arithmetic as the reference's MM) on a bounded sample.
 """
@@ -485,6 +487,71 @@ def parity_vs_one_gpu(chain, world, rank):
     return res
 
 
+# ------------------------------------------------------------------------------ Phi-4-mini sweep
+def phi4_sweep(args, world, rank, group, hbm):
+    """the Phi-4-mini-shaped quantized linears (one layer's q 3072x3072,
+    k / v 1024x3072, o 3072x3072, gate / up 8192x3072, down 3072x8192, and the 200064x3072 LM
+    head) in int8-row and int4-g32 (head int8-row), batches of 1 / 8 / 64 activation rows
+    N(0, 1), each projection's output rows sharded over the ranks with an NCCL all-gather of its
+    output (in the timed graph) when world > 1. One CUDA graph replays the eight launches (and
+    gathers); value = weight bytes (whole job) / time. Weights are random int8 rows / nibbles (the
+    GEMV's cost does not depend on their values), the same on every rank for its shard."""
+    import torch
+    import torch.distributed as dist
+    from opentpu_b200 import linear
+    shape = WL.PHI4_MINI
+    projs = shape.projections() + [("head", shape.vocab, shape.hidden)]
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    out = []
+    stream = torch.cuda.Stream()
+    for fmt in ("int8-row", "int4-g32"):
+        ws, nbytes = [], 0
+        for name, N, K in projs:
+            f = "int8-row" if name == "head" else fmt
+            n = N // world
+            if f == "int8-row":
+                rows = torch.randint(-127, 128, (n, K), dtype=torch.int8, device="cuda",
+                                     generator=gen).view(torch.uint8)
+                sw = (torch.rand(n, device="cuda", generator=gen) * 1e-3 + 1e-4)
+                w = linear.PackedWeight(f, n, K, rows, sw.view(torch.uint8).reshape(n, 4))
+            else:
+                codes = torch.randint(0, 256, (n, K // 2), dtype=torch.int32, device="cuda",
+                                      generator=gen).to(torch.uint8)
+                sc = (torch.rand((n, K // 32), device="cuda", generator=gen) * 1e-3 + 1e-4).half()
+                w = linear.PackedWeight(f, n, K, codes, sc)
+            ws.append(w)
+            nbytes += w.stream_bytes * world
+        for B in (1, 8, 64):
+            xs = {K: torch.randn((B, K), device="cuda", generator=gen) for _, _, K in projs}
+            ys = [torch.empty((B, w.N), device="cuda") for w in ws]
+            gath = [torch.empty((world, B, w.N), device="cuda") for w in ws] if world > 1 else None
+
+            def run():
+                for i, ((_, N, K), w) in enumerate(zip(projs, ws)):
+                    linear.qlinear(xs[K], w, out=ys[i], pdl=True)
+                    if world > 1:
+                        dist.all_gather_into_tensor(gath[i], ys[i], group=group)
+            g = capture(run, stream, warm=1)
+            graph_ms(g, stream, 2, world)
+            ms = graph_ms(g, stream, max(5, min(args.steps, 20)), world)
+            del g
+            out.append({"format": fmt, "batch": B, "ms": ms,
+                        "GB/s": nbytes / (ms * 1e-3) / 1e9,
+                        "hbm_frac_per_gpu": nbytes / world / (ms * 1e-3) / 1e9 / hbm,
+                        "weights_bytes": nbytes})
+        del ws
+        torch.cuda.synchronize()
+    return {"metric": "quantized linear GB/s (Phi-4-mini shapes)", "unit": "GB/s",
+            "value": max(r["GB/s"] for r in out), "results": out,
+            "config": {"workload": "BASELINE configuration 5: Phi-4-mini projections q 3072x3072, "
+                                   "k/v 1024x3072, o 3072x3072, gate/up 8192x3072, down 3072x8192 "
+                                   "+ head 200064x3072; int8-row and int4-g32 layers (int8-row "
+                                   "head); batch 1/8/64; one CUDA graph of the 8 launches",
+                       "parallelism": f"row-shard x{world}" + (" + NCCL all-gather of every "
+                                                              "output" if world > 1 else "")},
+            "gpu_launches": len(out) * 8}
+
+
 # ------------------------------------------------------------------------------ prefill
 def prefill_layer(shape, world, rank, gen, xs=None):
     """One layer's seven projections for the prefill GEMM: int8-row
@@ -657,6 +724,11 @@ def profile_run(what: str):
         y = torch.empty((1, 65536), device="cuda")
         for _ in range(5):
             linear.qlinear(x, w, out=y)
+    elif what in ("stepkernel", "stepkernel4"):
+        from opentpu_b200.decode import DecodeStep
+        st = DecodeStep(shape, fmt="int4-g32" if what == "stepkernel4" else "int8-row")
+        for _ in range(3):
+            st.step_eager()
     elif what == "prefill":
         items, _ = prefill_layer(WL.SMOLLM3_3B, 1, 0,
                                  torch.Generator(device="cuda").manual_seed(0))
@@ -701,10 +773,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["head", "step", "prefill", "g32"])
+    ap.add_argument("--profile", choices=["head", "step", "prefill", "g32", "stepkernel",
+                                          "stepkernel4"])
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-4bit", action="store_true")
     ap.add_argument("--no-config1", action="store_true")
+    ap.add_argument("--no-phi4", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -757,6 +831,7 @@ def main():
         head = None
         c1 = None if args.no_config1 else config1(world, max(3, min(args.steps, 50)))
         dec4 = None if args.no_4bit else decode_4bit(args, world, rank, group, hbm, peak_kind)
+        phi4 = None if args.no_phi4 else phi4_sweep(args, world, rank, group, hbm)
         prefill = None if args.no_prefill else prefill_bench(
             args, world, rank, local, group, max(3, min(100, args.steps // 4)),
             max(3, min(5, args.warmup)))
@@ -803,6 +878,7 @@ def main():
             "config1": c1,
             "decode_4bit": dec4,
             "prefill": prefill,
+            "phi4_sweep": phi4,
         }), flush=True)
     chain.release()
     if world > 1:

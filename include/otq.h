@@ -221,9 +221,17 @@ OTQ_API int otq_set_wait_limit(uint32_t polls);
 
 /* ------------------------------------------------------------------ the decode step, one launch */
 
-/* Weight formats of otq_decode_step. */
+/* Stage kinds of otq_decode_step: a projection in a weight format, or the attention. */
 #define OTQ_STEP_RSC 0   /* int8 rows with a per-row fp32 scale (MM RSC) or UNIT: QACT + MM */
 #define OTQ_STEP_G32 1   /* 4-bit group-32 fp16-scale rows (otq_pack_g32): weight-only */
+#define OTQ_STEP_ATTN 2  /* no weights: causal softmax attention of one query row over a KV cache */
+
+/* What a projection's input row is. */
+#define OTQ_IN_DEFAULT 0 /* x0 when in == -1, else the first K outputs of projection `in` */
+#define OTQ_IN_NORM 1    /* the residual row (x0 when res == -2, else the residual so far plus
+                            the output of projection `res`), RMSNorm'ed and times gamma */
+#define OTQ_IN_SWIGLU 2  /* silu(y[0:K]) * y[K:2K], y the output of projection `in` */
+#define OTQ_IN_ATTN 3    /* the output of attention stage `in` */
 
 /* One projection of otq_decode_step. */
 typedef struct otq_step_proj {
@@ -235,13 +243,26 @@ typedef struct otq_step_proj {
                             multiple of 16) */
   int64_t srs;
   int64_t N;             /* this rank's rows (with world > 1: its contiguous row shard) */
-  int64_t K;             /* RSC: a multiple of 128; G32: of 256; at most 32640 */
-  int in;                /* -1: the input is x0; else the index of an earlier projection whose
-                            output row (its first K elements) is the input */
-  int fmt;               /* OTQ_STEP_RSC or OTQ_STEP_G32 */
+  int64_t K;             /* RSC: a multiple of 128; G32: of 256; at most 8192 (OTQ_IN_NORM: 4096) */
+  int in;                /* -1: the input is x0; else the index of an earlier stage (see input) */
+  int fmt;               /* OTQ_STEP_RSC, OTQ_STEP_G32 or OTQ_STEP_ATTN */
+  int input;             /* OTQ_IN_* */
+  int res;               /* OTQ_IN_NORM: -2, or the projection added to the residual first */
+  const float* gamma;    /* OTQ_IN_NORM: the norm's gains [K] (16-byte aligned) */
+  /* OTQ_STEP_ATTN: `in` is the QKV projection (q [n_q * hd], k [n_kv * hd], v [n_kv * hd]);
+   * N = n_q * hd + n_q * ceil(max_pos / 64) * (hd + 2) + n_kv words: the attention's output row
+   * (query head major: the input of an OTQ_IN_ATTN projection), the partial results of its
+   * chunks of 64 positions, and an arrival count a KV head; K unused. q and k of the new token:
+   * per-head RMSNorm times q_gain / k_gain (NULL: none), then rotate-half RoPE at *pos; k and v
+   * go into the caches at *pos. At most 2 * (n_q / n_kv) * ceil(max_pos / 64) <= 2048. */
+  const float* q_gain;
+  const float* k_gain;
+  float* kcache;         /* [max_pos][n_kv][hd] fp32 (16-byte aligned) */
+  float* vcache;
+  int n_q, n_kv, head_dim;   /* head_dim 128, n_q / n_kv at most 4 */
 } otq_step_proj;
 
-#define OTQ_STEP_MAX 120
+#define OTQ_STEP_MAX 160
 
 typedef struct otq_step {
   const otq_step_proj* projs;
@@ -257,6 +278,15 @@ typedef struct otq_step {
                             step: steps completed, CTAs done, the greedy token's accumulator */
   int64_t* token;        /* the index of the first maximum of the last projection's full output
                             row (the greedy token), or NULL */
+  /* decoder steps (OTQ_IN_NORM, OTQ_STEP_ATTN): */
+  float eps;             /* RMSNorm epsilon */
+  const float* rope_cos; /* [max_pos][hd / 2] */
+  const float* rope_sin;
+  int max_pos;
+  int* pos;              /* this step's position (device int), advanced at the end of the step */
+  const float* embed;    /* [vocab][K0]: if not NULL, x0 is embed[*token_in] */
+  const int64_t* token_in;
+  int64_t vocab;
 } otq_step;
 
 /* Word offsets of every projection's output row (offsets[count], may be NULL) and the words

@@ -35,17 +35,24 @@ TAGS_COUNTED, TAGS_STEPPED = 0, 1
 class StepProj(ctypes.Structure):
     """struct otq_step_proj of include/otq.h: one projection of otq_decode_step."""
     _fields_ = [("rows", c_void_p), ("rs", c_int64), ("srows", c_void_p), ("srs", c_int64),
-                ("N", c_int64), ("K", c_int64), ("input", c_int), ("fmt", c_int)]
+                ("N", c_int64), ("K", c_int64), ("src", c_int), ("fmt", c_int),
+                ("input", c_int), ("res", c_int), ("gamma", c_void_p), ("q_gain", c_void_p),
+                ("k_gain", c_void_p), ("kcache", c_void_p), ("vcache", c_void_p),
+                ("n_q", c_int), ("n_kv", c_int), ("head_dim", c_int)]
 
 
-STEP_RSC, STEP_G32 = 0, 1
+STEP_RSC, STEP_G32, STEP_ATTN = 0, 1, 2
+IN_DEFAULT, IN_NORM, IN_SWIGLU, IN_ATTN = 0, 1, 2, 3
 
 
 class Step(ctypes.Structure):
     """struct otq_step of include/otq.h: one decode step as one launch."""
     _fields_ = [("projs", c_void_p), ("count", c_int), ("rank", c_int), ("world", c_int),
                 ("delta", c_int64 * 8), ("x0", c_void_p), ("out", c_void_p),
-                ("counters", c_void_p), ("token", c_void_p)]
+                ("counters", c_void_p), ("token", c_void_p), ("eps", ctypes.c_float),
+                ("rope_cos", c_void_p), ("rope_sin", c_void_p), ("max_pos", c_int),
+                ("pos", c_void_p), ("embed", c_void_p), ("token_in", c_void_p),
+                ("vocab", c_int64)]
 
 
 class GemmProj(ctypes.Structure):

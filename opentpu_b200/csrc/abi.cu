@@ -451,9 +451,28 @@ int check_step(const otq_step* s) {
   for (int r = 0; r < s->world; ++r)
     if (s->delta[r] % 16 || (r == s->rank && s->delta[r] != 0)) return kErrAlign;
   if (s->token != nullptr && !aligned(s->token, 8)) return kErrAlign;
-  bool plain_in = false;
+  if (s->embed != nullptr && (s->token_in == nullptr || s->vocab <= 0 || !aligned(s->embed, 16)))
+    return kErrArg;
+  bool plain_in = false, attn = false;
+  auto full = [&](int i) { return s->projs[i].N * s->world; };   // a projection's output row
+  auto is_proj = [&](int j, int i) {
+    return j >= 0 && j < i && s->projs[j].fmt != OTQ_STEP_ATTN;
+  };
   for (int i = 0; i < s->count; ++i) {
     const otq_step_proj& p = s->projs[i];
+    if (p.fmt == OTQ_STEP_ATTN) {
+      attn = true;
+      if (!is_proj(p.in, i) || p.head_dim != 128 || p.n_kv <= 0 || p.n_q <= 0 || p.n_q % p.n_kv ||
+          p.n_q / p.n_kv > 4 || p.kcache == nullptr || p.vcache == nullptr)
+        return kErrArg;
+      if (full(p.in) < static_cast<int64_t>(p.n_q + 2 * p.n_kv) * 128) return kErrArg;
+      // the combined row, the partial results and a count a KV head
+      if (p.N < static_cast<int64_t>(p.n_q) * 128 + static_cast<int64_t>(p.n_q) * ((s->max_pos + 63) / 64) * 130 + p.n_kv)
+        return kErrArg;
+      if (!aligned(p.kcache, 16) || !aligned(p.vcache, 16)) return kErrAlign;
+      if ((p.q_gain && !aligned(p.q_gain, 16)) || (p.k_gain && !aligned(p.k_gain, 16))) return kErrAlign;
+      continue;
+    }
     const bool g32 = p.fmt == OTQ_STEP_G32;
     if (p.fmt != OTQ_STEP_RSC && !g32) return kErrFormat;
     if (p.N <= 0 || p.K <= 0 || p.K % (g32 ? 256 : OTQ_D) || p.K > 255 * OTQ_D) return kErrArg;
@@ -467,12 +486,37 @@ int check_step(const otq_step* s) {
                                       p.srs >= kStrideLimit)) {
       return kErrAlign;
     }
-    if (p.in < -1 || p.in >= i) return kErrArg;   // an earlier projection, or the plain input
-    if (p.in == -1) plain_in = true;
-    else if (s->projs[p.in].N * s->world < p.K) return kErrArg;
+    switch (p.input) {
+      case OTQ_IN_DEFAULT:
+        if (p.in == -1) plain_in = true;
+        else if (!is_proj(p.in, i) || full(p.in) < p.K) return kErrArg;
+        break;
+      case OTQ_IN_NORM:
+        if (p.gamma == nullptr) return kErrArg;
+        if (!aligned(p.gamma, 16)) return kErrAlign;
+        if (p.res == -2) plain_in = plain_in || s->embed == nullptr;
+        else if (!is_proj(p.res, i) || full(p.res) < p.K) return kErrArg;
+        break;
+      case OTQ_IN_SWIGLU:
+        if (!is_proj(p.in, i) || full(p.in) < 2 * p.K) return kErrArg;
+        break;
+      case OTQ_IN_ATTN:
+        if (p.in < 0 || p.in >= i || s->projs[p.in].fmt != OTQ_STEP_ATTN ||
+            p.K != static_cast<int64_t>(s->projs[p.in].n_q) * 128)
+          return kErrArg;
+        break;
+      default:
+        return kErrArg;
+    }
   }
   if (plain_in && s->x0 == nullptr) return kErrArg;
   if (plain_in && !aligned(s->x0, 16)) return kErrAlign;
+  if (attn) {
+    if (s->pos == nullptr || s->rope_cos == nullptr || s->rope_sin == nullptr || s->max_pos < 1 ||
+        s->max_pos > 65536)
+      return kErrArg;
+    if (!aligned(s->pos, 4) || !aligned(s->rope_cos, 16) || !aligned(s->rope_sin, 16)) return kErrAlign;
+  }
   return kOk;
 }
 }  // namespace

@@ -137,7 +137,7 @@ __device__ __forceinline__ uint32_t mag_bits(float v) {
 
 // The same QACT as qact_row for 32-element groups, four elements a thread at a time: one pass
 // reads x (straight from global memory through L2: x may be the output of the kernel launched
-// just before, read after griddepcontrol.wait) into xs, with each 32-element segment's maximum
+// just before, read after griddepcontrol.wait; or, with x and xt null, from xs itself) into xs, with each 32-element segment's maximum
 // from an 8-lane shuffle reduction; one more pass quantizes. n % 128 == 0; all NT threads of
 // the CTA call it. x4: x is 16-byte aligned (else four scalar loads). segm: shared scratch of
 // n/32 words; red: of NT/32 + 3 words. emit(i, q0, q1, q2, q3, d) gets elements 4i..4i+3 and
@@ -156,7 +156,9 @@ __device__ __forceinline__ bool behind(unsigned long long w, uint32_t expect) {
 
 // BAR: 0 -- the whole CTA meets on __syncthreads (NT = the CTA's threads); else the NT threads
 // 0 .. NT - 1 meet on named barrier BAR (the CTA's other threads do something else).
-template <int NT, int BAR = 0, class Emit4>
+// ASYNC: every thread's cp.async copies are completed before the last barrier (the caller's
+// copies issued before the call are then visible to the whole group).
+template <int NT, int BAR = 0, bool ASYNC = false, class Emit4>
 __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, bool x4, float* xs,
                                                    int n, bool row_mode, uint32_t* segm,
                                                    uint32_t* red, Emit4 emit,
@@ -181,6 +183,8 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
       if (xt != nullptr) {
         ld_tagged2(xt + 4 * i, w[b][0], w[b][1]);
         ld_tagged2(xt + 4 * i + 2, w[b][2], w[b][3]);
+      } else if (x == nullptr) {
+        v[b] = *reinterpret_cast<const float4*>(xs + 4 * i);   // the row is in xs already
       } else if (x4) {
         v[b] = ld_cg4(x + 4 * i);
       } else {
@@ -245,6 +249,7 @@ __device__ __forceinline__ QactRowResult qact_row4(const float* __restrict__ x, 
     const float scale = fmul(r.inv, pow2i(d));
     emit(i, q8(fmul(v.x, scale)), q8(fmul(v.y, scale)), q8(fmul(v.z, scale)), q8(fmul(v.w, scale)), d);
   }
+  if constexpr (ASYNC) asm volatile("cp.async.wait_all;" ::: "memory");
   if constexpr (BAR == 0) { __syncthreads(); } else { asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory"); }
   return r;
 }

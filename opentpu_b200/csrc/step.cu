@@ -66,35 +66,54 @@ constexpr int kCT = kCW * 32;                // compute threads (named barrier 1
 constexpr int kTh = kCT + 32;                // + the producer warp
 constexpr int kChunkB = 128;                 // bytes of a row a chunk
 constexpr int kCB = 8;                       // chunks an item at most
-constexpr int kCodeStage = 8 * kCB * kChunkB;    // 8 KB: 8 rows x 8 chunks
-constexpr int kScaleStage = 8 * kCB * 16;        // 1 KB: 8 rows x 8 chunks x 8 fp16 scales
+constexpr int kTR = 16;                      // rows a tile (the M of an mma.sync m16n8k32)
+constexpr int kSub = kTR * kChunkB;          // 2 KB: a tile's chunk, one swizzled sub-stage
+constexpr int kCodeStage = kCB * kSub;       // 16 KB: 16 rows x 8 chunks
+constexpr int kScaleStage = kTR * kCB * 16;  // 2 KB: 16 rows x 8 chunks x 8 fp16 scales
 constexpr int kMaxProj = OTQ_STEP_MAX;
 constexpr uint32_t kTagStride = 1024;
 constexpr int kMaxWorld = 8;
-constexpr int kMaxRedBlocks = 32;            // 8-row blocks a CTA adds up in one pass
-constexpr int kFmtRsc = OTQ_STEP_RSC;
 constexpr int kFmtG32 = OTQ_STEP_G32;
+constexpr int kFmtAttn = OTQ_STEP_ATTN;
+constexpr int kInDefault = OTQ_IN_DEFAULT;
+constexpr int kInNorm = OTQ_IN_NORM;
+constexpr int kInSwiglu = OTQ_IN_SWIGLU;
+constexpr int kInAttn = OTQ_IN_ATTN;
+constexpr int kHd = 128;                     // attention head dimension
+constexpr int kMaxG = 4;                     // query heads a KV head
+constexpr int kAttnChunk = 64;               // positions an attention item
 
 __device__ uint32_t g_step_wait_limit = 1u << 22;
 
-struct SInfo {            // one projection, as the kernel reads it (shared memory)
+struct SInfo {            // one stage, as the kernel reads it (shared memory)
   const uint8_t* srows;   // int8: scale rows, Sw the first fp32 word (null: UNIT)
+  const float* gamma;     // OTQ_IN_NORM: the norm's gains
   int srs;
   int N;                  // this rank's rows
   int K;
   int fmt;
-  int split;              // 8: the warps share each block's chunks; 1: a warp owns blocks
+  int split;              // unused
   int in;                 // -1: the plain input x0; else the projection whose output is x
   int out;                // word offset of this projection's full output row
   int nfull;              // the full row's length (N * world)
   int kch;                // chunks a row
   int cb;                 // chunks an item (min(8, kch))
   int ngr;                // items a block (ceil(kch / cb))
+  int input;              // OTQ_IN_*
+  int res;                // OTQ_IN_NORM: -2 (start from x0) or the projection added first
   int pad[3];
 };
-static_assert(sizeof(SInfo) == 64, "SInfo is 64 bytes");
+static_assert(sizeof(SInfo) == 80, "SInfo is 80 bytes");
 
-struct StepTable {
+struct SAttn {            // an attention stage's operands
+  const float* qg;        // q / k per-head norm gains (null: none)
+  const float* kg;
+  float* kc;              // [max_pos][n_kv][hd]
+  float* vc;
+  int nq, nkv, maxch, pad;
+};
+
+struct alignas(16) StepHead {   // the scalars and pointers of a step (the kernel keeps a copy in shared memory)
   int count, world, rank, ns, kmax, redb, maxrows, stage_bytes;
   const float* x0;
   unsigned long long* words;
@@ -103,7 +122,21 @@ struct StepTable {
   unsigned long long* amax;      // the head's key accumulator (0 between steps)
   long long* token;
   int* status;
+  float eps;
+  int max_pos;
+  const float* rope_cos;         // [max_pos][hd / 2]
+  const float* rope_sin;
+  int* pos;                      // this step's position (null: no attention)
+  const float* embed;            // x0 = embed[*token_in] (null: x0)
+  const long long* token_in;
+  int hmax;                      // the residual row's length (0: none)
+  int ascr;                      // floats of the attention combine's scratch
+};
+static_assert(sizeof(StepHead) % 16 == 0, "StepHead is copied in 16-byte words");
+
+struct StepTable : StepHead {
   SInfo info[kMaxProj];
+  SAttn attn[kMaxProj];
   alignas(128) CUtensorMap map[kMaxProj];    // rows / codes: {128 B, N rows, chunks}
   CUtensorMap smap[kMaxProj];                // 4-bit scales: {K/16 B, N rows}
 };
@@ -117,55 +150,67 @@ struct SSmem {
   float* xsum;       // [kmax/32] 4-bit: each group's sum of x
   uint32_t* segm;    // [kmax/32]
   uint32_t* qred;    // [kCW + 8]
-  long long* red;    // [redb][kCW][8] the warps' row totals (4-bit: floats)
+  long long* red;    // [kCW][16] the warps' row totals of a shared tile (4-bit: floats)
   float* sws;        // [maxrows] Sw of this CTA's rows of the projection
+  float* xr;         // [hmax] the residual row (this CTA's copy)
+  float* aq;         // [kMaxG][kHd] attention: the query heads, normed and rotated
+  float* akv;        // [2][kHd] the new key (normed, rotated) and value
+  float* asc;        // [kMaxG][kAttnChunk] scores, then their exponentials
+  float* ascr;       // [ascr] the attention combine's (m, l) pairs and weights
   uint64_t* full;    // [ns]
   uint64_t* empty;   // [ns]
   uint8_t* ring;     // [ns][stage_bytes], 1024-byte aligned
 };
 
-__host__ __device__ inline size_t step_smem(int count, int kmax, int redb, int maxrows, int ns,
-                                            int stage_bytes, size_t* o) {
-  size_t off = 0;
-  auto take = [&](int i, size_t bytes) {
-    off = (off + 15) & ~size_t(15);
-    if (o) o[i] = off;
-    off += bytes;
-  };
-  take(0, static_cast<size_t>(count) * sizeof(SInfo));
-  take(1, kmax);
-  take(2, kmax / 32);
-  take(3, kmax / 32);
-  take(4, static_cast<size_t>(kmax) * 4);
-  take(5, kmax / 32 * 4);
-  take(6, kmax / 32 * 4);
-  take(7, (kCW + 8) * 4);
-  take(8, static_cast<size_t>(redb) * kCW * 8 * 8);
-  take(9, static_cast<size_t>(maxrows) * 4);
-  take(10, static_cast<size_t>(ns) * 8);
-  take(11, static_cast<size_t>(ns) * 8);
-  take(12, static_cast<size_t>(ns) * stage_bytes + 1024);
-  return off;
-}
+// The shared-memory layout: every region at a fixed offset (sized for the largest step this
+// kernel takes), so that the kernel addresses them as constants off one base; the ring of
+// stages follows, 1024-byte aligned, as many stages as the rest of the 227 KB holds.
+constexpr int kKcap = 8192;       // the longest input row (K)
+constexpr int kHcap = 4096;       // the longest residual row (a norm's K)
+constexpr int kRowsCap = 2048;    // a CTA's rows of one projection
+constexpr int kNScap = 32;        // ring stages
+constexpr int kAscrCap = 2048;    // floats of the attention combine's scratch (2 G maxch)
+constexpr size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
+constexpr size_t kOffInfo = 0;
+constexpr size_t kOffAct = al16(kOffInfo + kMaxProj * sizeof(SInfo));
+constexpr size_t kOffCls = al16(kOffAct + kKcap);
+constexpr size_t kOffDg = al16(kOffCls + kKcap / 32);
+constexpr size_t kOffXs = al16(kOffDg + kKcap / 32);
+constexpr size_t kOffXsum = al16(kOffXs + kKcap * 4);
+constexpr size_t kOffSegm = al16(kOffXsum + kKcap / 32 * 4);
+constexpr size_t kOffQred = al16(kOffSegm + kKcap / 32 * 4);
+constexpr size_t kOffRed = al16(kOffQred + (kCW + 8) * 4);
+constexpr size_t kOffSws = al16(kOffRed + static_cast<size_t>(kCW) * kTR * 8);
+constexpr size_t kOffFull = al16(kOffSws + kRowsCap * 4);
+constexpr size_t kOffEmpty = al16(kOffFull + kNScap * 8);
+constexpr size_t kOffXr = al16(kOffEmpty + kNScap * 8);
+constexpr size_t kOffAttn = al16(kOffXr + kHcap * 4);
+constexpr size_t kOffAscr = al16(kOffAttn + (kMaxG * kHd + 2 * kHd + kMaxG * kAttnChunk) * 4);
+constexpr size_t kOffRing = al16(kOffAscr + kAscrCap * 4);
 
-__device__ __forceinline__ SSmem carve(unsigned char* base, const StepTable& T) {
-  size_t o[13];
-  step_smem(T.count, T.kmax, T.redb, T.maxrows, T.ns, T.stage_bytes, o);
+extern __shared__ __align__(16) unsigned char smem_raw[];   // the step kernel's dynamic shared memory
+
+__device__ __forceinline__ SSmem carve(unsigned char* base) {
   SSmem s;
-  s.info = reinterpret_cast<SInfo*>(base + o[0]);
-  s.act = base + o[1];
-  s.cls = base + o[2];
-  s.dg = base + o[3];
-  s.xs = reinterpret_cast<float*>(base + o[4]);
-  s.xsum = reinterpret_cast<float*>(base + o[5]);
-  s.segm = reinterpret_cast<uint32_t*>(base + o[6]);
-  s.qred = reinterpret_cast<uint32_t*>(base + o[7]);
-  s.red = reinterpret_cast<long long*>(base + o[8]);
-  s.sws = reinterpret_cast<float*>(base + o[9]);
-  s.full = reinterpret_cast<uint64_t*>(base + o[10]);
-  s.empty = reinterpret_cast<uint64_t*>(base + o[11]);
-  const uint32_t r = smem_addr(base + o[12]);
-  s.ring = base + o[12] + (((r + 1023u) & ~1023u) - r);
+  s.info = reinterpret_cast<SInfo*>(base + kOffInfo);
+  s.act = base + kOffAct;
+  s.cls = base + kOffCls;
+  s.dg = base + kOffDg;
+  s.xs = reinterpret_cast<float*>(base + kOffXs);
+  s.xsum = reinterpret_cast<float*>(base + kOffXsum);
+  s.segm = reinterpret_cast<uint32_t*>(base + kOffSegm);
+  s.qred = reinterpret_cast<uint32_t*>(base + kOffQred);
+  s.red = reinterpret_cast<long long*>(base + kOffRed);
+  s.sws = reinterpret_cast<float*>(base + kOffSws);
+  s.full = reinterpret_cast<uint64_t*>(base + kOffFull);
+  s.empty = reinterpret_cast<uint64_t*>(base + kOffEmpty);
+  s.xr = reinterpret_cast<float*>(base + kOffXr);
+  s.aq = reinterpret_cast<float*>(base + kOffAttn);
+  s.akv = s.aq + kMaxG * kHd;
+  s.asc = s.akv + 2 * kHd;
+  s.ascr = reinterpret_cast<float*>(base + kOffAscr);
+  const uint32_t r = smem_addr(base + kOffRing);
+  s.ring = base + kOffRing + (((r + 1023u) & ~1023u) - r);
   return s;
 }
 
@@ -173,9 +218,9 @@ __device__ __forceinline__ void cbar() {   // the compute warps meet (named barr
   asm volatile("bar.sync 1, %0;" ::"n"(kCT) : "memory");
 }
 
-// This CTA's 8-row blocks [b0, b1) of a projection of N rows.
-__device__ __forceinline__ void cta_blocks(int N, int& b0, int& b1) {
-  const int nb = (N + 7) / 8;
+// This CTA's 16-row tiles [b0, b1) of a projection of N rows.
+__device__ __forceinline__ void cta_tiles(int N, int& b0, int& b1) {
+  const int nb = (N + kTR - 1) / kTR;
   b0 = static_cast<int>(static_cast<long long>(nb) * blockIdx.x / gridDim.x);
   b1 = static_cast<int>(static_cast<long long>(nb) * (blockIdx.x + 1) / gridDim.x);
 }
@@ -195,6 +240,16 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int
 }
 __device__ __forceinline__ void mbar_arrive_n(uint32_t bar, uint32_t n) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(n) : "memory");
+}
+// 4 bytes global -> shared, asynchronously (completed by cp.async.wait_all)
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+// 8 bytes of a ring stage (ordered after the stage's barrier wait: volatile)
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
 }
 
 __device__ __forceinline__ void st_word(unsigned long long* p, unsigned long long v, int world,
@@ -221,40 +276,41 @@ __device__ __forceinline__ unsigned long long amax_key(float v, uint32_t i) {
   return (static_cast<unsigned long long>(o) << 32) | (0xFFFFFFFFu - i);
 }
 
-// Sum of the class path over lanes for one 8-row block (gemv.cu class_reduce<1>): the total of
-// row 2t + (lane bit 4), owned by lanes with bits 2 and 3 clear.
-__device__ __forceinline__ long long class_reduce8(long long v0, long long v1, int lane) {
-  const bool b4 = (lane & 16) != 0;
-  long long u = (b4 ? v1 : v0) + __shfl_xor_sync(0xFFFFFFFFu, b4 ? v0 : v1, 16);
-  u += __shfl_xor_sync(0xFFFFFFFFu, u, 8);
-  u += __shfl_xor_sync(0xFFFFFFFFu, u, 4);
-  return u;
+
+// Four tagged words xt[0..3] (16-byte aligned) as floats, read until their tags reach `expect`
+// (bounded: after `limit` polls the status word records a timeout and the values are used).
+__device__ __forceinline__ float4 read_tagged4(const unsigned long long* xt, uint32_t expect,
+                                               int* status, uint32_t limit) {
+  unsigned long long w[4];
+  ld_tagged2(xt, w[0], w[1]);
+  ld_tagged2(xt + 2, w[2], w[3]);
+  for (uint32_t spin = 0;
+       behind(w[0], expect) || behind(w[1], expect) || behind(w[2], expect) || behind(w[3], expect);
+       ++spin) {
+    if (spin >= limit) {
+      atomicOr(status, kStatusTimeout);
+      break;
+    }
+    if (spin >= 64) __nanosleep(32);
+    ld_tagged2(xt, w[0], w[1]);
+    ld_tagged2(xt + 2, w[2], w[3]);
+  }
+  return make_float4(__uint_as_float(static_cast<uint32_t>(w[0])), __uint_as_float(static_cast<uint32_t>(w[1])),
+                     __uint_as_float(static_cast<uint32_t>(w[2])), __uint_as_float(static_cast<uint32_t>(w[3])));
 }
 
-// The 4-bit input row: x' = x * 2^(-4 (k mod 4)) and the groups' sums, from plain fp32 x or from
-// tagged words (read until their tags reach `expect`). The compute threads meet at the end.
+// The 4-bit input row: x' = x * 2^(-4 (k mod 4)) and the groups' sums, from plain fp32 x, from
+// tagged words (read until their tags reach `expect`), or (both null) from xs itself. The
+// compute threads meet at the end.
 __device__ void stage_x4(const float* x, const unsigned long long* xt, uint32_t expect, int K,
                          float* xs, float* xsum, int* status, uint32_t limit) {
   const int tid = threadIdx.x;
   for (int i = tid; i < K / 4; i += kCT) {   // K / 4 is a multiple of 32: whole warps
     float4 v;
     if (xt != nullptr) {
-      unsigned long long w[4];
-      ld_tagged2(xt + 4 * i, w[0], w[1]);
-      ld_tagged2(xt + 4 * i + 2, w[2], w[3]);
-      for (uint32_t spin = 0; behind(w[0], expect) || behind(w[1], expect) || behind(w[2], expect) ||
-                              behind(w[3], expect);
-           ++spin) {
-        if (spin >= limit) {
-          atomicOr(status, kStatusTimeout);
-          break;
-        }
-        if (spin >= 16) __nanosleep(32);
-        ld_tagged2(xt + 4 * i, w[0], w[1]);
-        ld_tagged2(xt + 4 * i + 2, w[2], w[3]);
-      }
-      v = make_float4(__uint_as_float(static_cast<uint32_t>(w[0])), __uint_as_float(static_cast<uint32_t>(w[1])),
-                      __uint_as_float(static_cast<uint32_t>(w[2])), __uint_as_float(static_cast<uint32_t>(w[3])));
+      v = read_tagged4(xt + 4 * i, expect, status, limit);
+    } else if (x == nullptr) {
+      v = *reinterpret_cast<const float4*>(xs + 4 * i);
     } else {
       v = ld_cg4(x + 4 * i);
     }
@@ -310,23 +366,283 @@ __device__ __forceinline__ float half_to_float(uint16_t h) {
   return f;
 }
 
+// The compute threads' sum of one float each, in a fixed order (warp shuffles, then the warps'
+// sums in warp order): the same bits in every CTA. scratch: kCW floats.
+__device__ __forceinline__ float cta_sum(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  cbar();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t += scratch[w];
+  cbar();   // scratch is free again
+  return t;
+}
+
+// OTQ_IN_NORM: the residual row xr (x0 when res == -2: the embedding row of *token_in, or x0;
+// else xr + the output words of the projection at word offset `res_out`), then
+// xs = (xr / sqrt(mean(xr^2) + eps)) * gamma (the reference's rmsnorm, qwen3.py:715-716).
+__device__ void norm_prologue(const StepHead& T, const SSmem& s, const SInfo& d, int res_out,
+                              uint32_t expect, uint32_t limit) {
+  const int K = d.K;
+  const float* x0 = T.embed != nullptr ? T.embed + (*T.token_in) * static_cast<long long>(K) : T.x0;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < K / 4; i += kCT) {
+    float4 r;
+    if (d.res == -2) {
+      r = ld_cg4(x0 + 4 * i);
+    } else {
+      r = *reinterpret_cast<const float4*>(s.xr + 4 * i);
+      const float4 y = read_tagged4(T.words + res_out + 4 * i, expect, T.status, limit);
+      r = make_float4(r.x + y.x, r.y + y.y, r.z + y.z, r.w + y.w);
+    }
+    *reinterpret_cast<float4*>(s.xr + 4 * i) = r;
+    ss += (r.x * r.x + r.y * r.y) + (r.z * r.z + r.w * r.w);
+  }
+  const float den = sqrtf(cta_sum(ss, reinterpret_cast<float*>(s.qred)) / static_cast<float>(K) + T.eps);
+  for (int i = threadIdx.x; i < K / 4; i += kCT) {
+    const float4 r = *reinterpret_cast<const float4*>(s.xr + 4 * i);
+    const float4 g = __ldg(reinterpret_cast<const float4*>(d.gamma) + i);
+    *reinterpret_cast<float4*>(s.xs + 4 * i) =
+        make_float4((r.x / den) * g.x, (r.y / den) * g.y, (r.z / den) * g.z, (r.w / den) * g.w);
+  }
+  cbar();
+}
+
+// OTQ_IN_SWIGLU: xs = silu(y[0:K]) * y[K:2K] of the output words at `in_out`
+// (the reference's (g / (1 + exp(-g))) * u, qwen3.py:741).
+__device__ void swiglu_prologue(const StepHead& T, const SSmem& s, int K, int in_out, uint32_t expect,
+                                uint32_t limit) {
+  for (int i = threadIdx.x; i < K / 4; i += kCT) {
+    const float4 g = read_tagged4(T.words + in_out + 4 * i, expect, T.status, limit);
+    const float4 u = read_tagged4(T.words + in_out + K + 4 * i, expect, T.status, limit);
+    *reinterpret_cast<float4*>(s.xs + 4 * i) =
+        make_float4((g.x / (1.0f + expf(-g.x))) * u.x, (g.y / (1.0f + expf(-g.y))) * u.y,
+                    (g.z / (1.0f + expf(-g.z))) * u.z, (g.w / (1.0f + expf(-g.w))) * u.w);
+  }
+  cbar();
+}
+
+
+// rmsnorm of one head (hd values in smem v, a warp) times gains g (null: none), then
+// rotate-half RoPE with this position's tables (qwen3.py:719-724, 335-346).
+__device__ __forceinline__ void head_norm_rope(float* v, const float* g, const float* cs,
+                                               const float* sn, float eps, int lane) {
+  float4 x = *reinterpret_cast<const float4*>(v + 4 * lane);
+  if (g != nullptr) {
+    float ss = (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    const float den = sqrtf(ss / static_cast<float>(kHd) + eps);
+    const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + lane);
+    x = make_float4((x.x / den) * gg.x, (x.y / den) * gg.y, (x.z / den) * gg.z, (x.w / den) * gg.w);
+  }
+  // lanes 0..15 hold elements 0..63 (v1), lanes 16..31 elements 64..127 (v2)
+  const float4 other = make_float4(__shfl_xor_sync(0xFFFFFFFFu, x.x, 16), __shfl_xor_sync(0xFFFFFFFFu, x.y, 16),
+                                   __shfl_xor_sync(0xFFFFFFFFu, x.z, 16), __shfl_xor_sync(0xFFFFFFFFu, x.w, 16));
+  const int j = 4 * (lane & 15);
+  const float4 c = __ldg(reinterpret_cast<const float4*>(cs + j));
+  const float4 sv = __ldg(reinterpret_cast<const float4*>(sn + j));
+  float4 r;
+  if (lane < 16) {   // v1 * c - v2 * s
+    r = make_float4(x.x * c.x - other.x * sv.x, x.y * c.y - other.y * sv.y, x.z * c.z - other.z * sv.z,
+                    x.w * c.w - other.w * sv.w);
+  } else {           // v2 * c + v1 * s
+    r = make_float4(x.x * c.x + other.x * sv.x, x.y * c.y + other.y * sv.y, x.z * c.z + other.z * sv.z,
+                    x.w * c.w + other.w * sv.w);
+  }
+  __syncwarp();
+  *reinterpret_cast<float4*>(v + 4 * lane) = r;
+  __syncwarp();
+}
+
+// The combine of KV head h's nch chunks for its G query heads (flash-decoding): with M the
+// largest chunk maximum, chunk c weighs e_c = exp(m_c - M) / L, L = sum_c exp(m_c - M) l_c, and
+// the output row of query head h G + g is sum_c e_c o_c, in chunk order. Written as tagged
+// words at `out` (query head major, hd each): the O projection's input. The whole CTA, after
+// the head's count came to nch (every chunk's partial words are written and fenced before its
+// count: they are read here through L2 without waiting on their tags).
+__device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, int h, int G,
+                             int nch, int part_out, int out, uint32_t tag, bool ok) {
+  float* ml = s.ascr;   // [G][nch] (m, l), then the chunks' weights
+  const long long stride = kHd + 2;
+  for (int i = threadIdx.x; i < G * nch; i += kCT) {
+    const int g = i / nch, c = i % nch;
+    unsigned long long w0, w1;
+    ld_tagged2(T.words + part_out + (static_cast<long long>(h * G + g) * a.maxch + c) * stride, w0, w1);
+    ml[2 * i] = __uint_as_float(static_cast<uint32_t>(w0));
+    ml[2 * i + 1] = __uint_as_float(static_cast<uint32_t>(w1));
+  }
+  cbar();
+  for (int g = threadIdx.x; g < G; g += kCT) {
+    float* hm = ml + 2 * g * nch;
+    float M = -INFINITY, L = 0.0f;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, hm[2 * c]);
+    for (int c = 0; c < nch; ++c) {
+      const float e = expf(hm[2 * c] - M);
+      hm[2 * c] = e;
+      L += e * hm[2 * c + 1];
+    }
+    for (int c = 0; c < nch; ++c) hm[2 * c] = hm[2 * c] / L;
+  }
+  cbar();
+  constexpr int kBatch = 8;
+  for (int i = threadIdx.x; i < G * kHd; i += kCT) {
+    const int g = i / kHd, dd = i % kHd;
+    const unsigned long long* pb = T.words + part_out + static_cast<long long>(h * G + g) * a.maxch * stride + 2 + dd;
+    const float* wt = ml + 2 * g * nch;
+    float o = 0.0f;
+    for (int c0 = 0; c0 < nch; c0 += kBatch) {
+      uint32_t w[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (c0 + u < nch) w[u] = __ldcg(reinterpret_cast<const unsigned int*>(pb + (c0 + u) * stride));
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (c0 + u < nch) o += wt[2 * (c0 + u)] * __uint_as_float(w[u]);
+    }
+    if (ok) {
+      unsigned long long* dst = T.words + out + static_cast<long long>(h * G + g) * kHd + dd;
+      asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(dst), "l"(__float_as_uint(o) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
+    }
+  }
+}
+
+// An attention stage: items (KV head h, chunk c of kAttnChunk positions) dealt to the CTAs.
+// Each reads its query heads, the new key and value (the QKV projection's words), normalises
+// and rotates q and k, scores positions [64 c, min(64 c + 64, pos + 1)) against the cache (the
+// new token's key from shared memory), and stores per query head (m, l, o) as tagged words;
+// the item holding position pos stores the new key and value into the caches.
+__device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int qkv_out, int out,
+                                       int pos, uint32_t expect, uint32_t tag, uint32_t limit,
+                                       bool ok) {
+  __shared__ int s_last;
+  const SSmem s = carve(smem_raw);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int part_out = out + a.nq * kHd;                                 // the partial results
+  const int cnt_out = part_out + a.nq * a.maxch * (kHd + 2);             // a count a KV head
+  const int G = a.nq / a.nkv;
+  const int nch = pos / kAttnChunk + 1;
+  const float* cs = T.rope_cos + static_cast<long long>(pos) * (kHd / 2);
+  const float* sn = T.rope_sin + static_cast<long long>(pos) * (kHd / 2);
+  const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(kHd));
+  for (int item = blockIdx.x; item < a.nkv * nch; item += gridDim.x) {
+    const int h = item / nch, c = item % nch;
+    const int j0 = c * kAttnChunk, j1 = min(j0 + kAttnChunk, pos + 1);
+    // the query heads h G .. h G + G - 1, the new key and value
+    for (int i = threadIdx.x; i < (G + 2) * kHd / 4; i += kCT) {
+      const int part = (4 * i) / kHd, e = (4 * i) % kHd;
+      const long long w = part < G ? static_cast<long long>(h * G + part) * kHd + e
+                                   : static_cast<long long>(a.nq + (part - G) * a.nkv + h) * kHd + e;
+      const float4 v = read_tagged4(T.words + qkv_out + w, expect, T.status, limit);
+      float* dst = part < G ? s.aq + part * kHd + e : s.akv + (part - G) * kHd + e;
+      *reinterpret_cast<float4*>(dst) = v;
+    }
+    cbar();
+    if (warp <= G) head_norm_rope(warp < G ? s.aq + warp * kHd : s.akv, warp < G ? a.qg : a.kg, cs, sn,
+                                  T.eps, lane);
+    cbar();
+    // scores: warp w takes positions j0 + w, j0 + w + 8, ...
+    for (int j = j0 + warp; j < j1; j += kCW) {
+      const float4 kv = j == pos ? *reinterpret_cast<const float4*>(s.akv + 4 * lane)
+                                 : ld_cg4(a.kc + (static_cast<long long>(j) * a.nkv + h) * kHd + 4 * lane);
+      for (int g = 0; g < G; ++g) {
+        const float4 q = *reinterpret_cast<const float4*>(s.aq + g * kHd + 4 * lane);
+        float d = (q.x * kv.x + q.y * kv.y) + (q.z * kv.z + q.w * kv.w);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
+        if (lane == 0) s.asc[g * kAttnChunk + (j - j0)] = d * inv_sqrt;
+      }
+    }
+    cbar();
+    // per query head: the chunk's largest score and the sum of the exponentials (warp g)
+    if (warp < G) {
+      const int n = j1 - j0;
+      float* sc = s.asc + warp * kAttnChunk;
+      float m = -INFINITY;
+      for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[j]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+      float l = 0.0f;
+      for (int j = lane; j < n; j += 32) {
+        const float e = expf(sc[j] - m);
+        sc[j] = e;
+        l += e;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+      if (lane == 0 && ok) {
+        unsigned long long* out = T.words + part_out + (static_cast<long long>(h * G + warp) * a.maxch + c) * (kHd + 2);
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(out), "l"(__float_as_uint(m) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(out + 1), "l"(__float_as_uint(l) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
+      }
+    }
+    cbar();
+    // the unnormalised outputs: thread (g, dd)
+    for (int i = threadIdx.x; i < G * kHd; i += kCT) {
+      const int g = i / kHd, dd = i % kHd;
+      float o = 0.0f;
+      for (int j = j0; j < j1; ++j) {
+        const float v = j == pos ? s.akv[kHd + dd]
+                                 : __ldcg(a.vc + (static_cast<long long>(j) * a.nkv + h) * kHd + dd);
+        o += s.asc[g * kAttnChunk + (j - j0)] * v;
+      }
+      if (ok) {
+        unsigned long long* out = T.words + part_out + (static_cast<long long>(h * G + g) * a.maxch + c) * (kHd + 2) + 2 + dd;
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(out), "l"(__float_as_uint(o) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
+      }
+    }
+    // the new key and value into the caches
+    if (c == nch - 1 && ok)
+      for (int i = threadIdx.x; i < 2 * kHd; i += kCT) {
+        float* cache = i < kHd ? a.kc : a.vc;
+        cache[(static_cast<long long>(pos) * a.nkv + h) * kHd + (i % kHd)] = s.akv[i];
+      }
+    // the head's count: the CTA that brings it to nch combines the head's chunks (its partial
+    // words, fenced before every count, are then all written)
+    cbar();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      unsigned int* cnt = reinterpret_cast<unsigned int*>(T.words + cnt_out + h);
+      const bool last = atomicAdd(cnt, 1u) == static_cast<unsigned int>(nch - 1);
+      if (last) {
+        atomicExch(cnt, 0u);   // the next step counts from zero
+        __threadfence();
+      }
+      s_last = last;
+    }
+    cbar();
+    if (s_last) attn_combine(T, s, a, h, G, nch, part_out, out, tag, ok);
+    cbar();   // aq / akv / asc / ascr are rewritten by the next item
+  }
+}
+
 __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restrict__ Tp) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ long long s_delta[kMaxWorld];
   __shared__ float s_Sa;
-  __shared__ int s_flag;
   __shared__ unsigned int s_seq;
-  const StepTable& T = *Tp;
-  const SSmem s = carve(smem_raw, T);
+  __shared__ int s_issued;   // items the producer has issued (or given up on)
+  __shared__ int s_pos;      // this step's position (attention)
+  // the table's scalars and pointers, read from shared memory from here on (the table itself is
+  // read for the stages' descriptors and tensor maps)
+  __shared__ __align__(16) StepHead sT;
+  for (int i = threadIdx.x; i < static_cast<int>(sizeof(StepHead) / 16); i += kTh)
+    reinterpret_cast<uint4*>(&sT)[i] = __ldg(reinterpret_cast<const uint4*>(Tp) + i);
+  __syncthreads();
+  const StepHead& T = sT;
+  const SSmem s = carve(smem_raw);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int NS = T.ns, SB = T.stage_bytes;
   const int count = T.count;
 
-  for (int i = threadIdx.x; i < count * 16; i += kTh)
-    reinterpret_cast<uint32_t*>(s.info)[i] = __ldg(reinterpret_cast<const uint32_t*>(T.info) + i);
+  for (int i = threadIdx.x; i < count * static_cast<int>(sizeof(SInfo) / 4); i += kTh)
+    reinterpret_cast<uint32_t*>(s.info)[i] = __ldg(reinterpret_cast<const uint32_t*>(Tp->info) + i);
   if (threadIdx.x < kMaxWorld) s_delta[threadIdx.x] = threadIdx.x < T.world ? T.delta[threadIdx.x] : 0;
   if (threadIdx.x == 0) {
+    s_issued = 0;
     s_seq = *reinterpret_cast<volatile unsigned int*>(T.counters);
+    s_pos = T.pos != nullptr ? *reinterpret_cast<volatile int*>(T.pos) : 0;
     for (int i = 0; i < NS; ++i) {
       mbar_init(smem_addr(s.full + i), 1);
       mbar_init(smem_addr(s.empty + i), kCW);
@@ -342,19 +658,22 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
       int item = 0;
       for (int p = 0; p < count; ++p) {
         const SInfo& d = s.info[p];
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&T.map[p])) : "memory");
+        if (d.fmt == kFmtAttn) continue;   // no weights
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&Tp->map[p])) : "memory");
         int b0, b1;
-        cta_blocks(d.N, b0, b1);
-        const uint32_t bytes = 8u * d.cb * (kChunkB + (d.fmt == kFmtG32 ? 16u : 0u));
+        cta_tiles(d.N, b0, b1);
+        const uint32_t bytes = static_cast<uint32_t>(kTR) * d.cb * (kChunkB + (d.fmt == kFmtG32 ? 16u : 0u));
         for (int b = b0; b < b1; ++b)
           for (int cg = 0; cg < d.ngr; ++cg, ++item) {
             const int st = item % NS, use = item / NS;
-            if (use > 0 && !mbar_wait(smem_addr(s.empty + st), static_cast<uint32_t>((use - 1) & 1), T.status))
-              continue;   // a consumer never released the stage: this item is skipped (status set)
-            const uint32_t fb = smem_addr(s.full + st);
-            mbar_arrive_expect_tx(fb, bytes);
-            tma_3d(ring_s + st * SB, &T.map[p], 0, b * 8, cg * kCB, fb);
-            if (d.fmt == kFmtG32) tma_2d(ring_s + st * SB + kCodeStage, &T.smap[p], cg * kCB * 16, b * 8, fb);
+            if (use == 0 || mbar_wait(smem_addr(s.empty + st), static_cast<uint32_t>((use - 1) & 1), T.status)) {
+              const uint32_t fb = smem_addr(s.full + st);
+              mbar_arrive_expect_tx(fb, bytes);
+              tma_3d(ring_s + st * SB, &Tp->map[p], 0, b * kTR, cg * kCB, fb);
+              if (d.fmt == kFmtG32) tma_2d(ring_s + st * SB + kCodeStage, &Tp->smap[p], cg * kCB * 16, b * kTR, fb);
+            }   // else a consumer never released the stage: the item is given up (status set)
+            // after the stage's previous use is released: a consumer may now wait on its parity
+            *reinterpret_cast<volatile int*>(&s_issued) = item + 1;
           }
       }
     }
@@ -363,6 +682,12 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
 
   // ------------------------------------------------------------------ the compute warps
   const int g = lane >> 2, t = lane & 3;
+  // the split mode's per-lane offsets of its B fragments within a 1 KB swizzled sub-stage
+  uint32_t boff[4];
+#pragma unroll
+  for (int sg = 0; sg < 4; ++sg) boff[sg] = g * kChunkB + 16 * ((2 * sg + (t >> 1)) ^ g) + 8 * (t & 1);
+  const uint32_t full_s = smem_addr(s.full), empty_s = smem_addr(s.empty);
+  const uint32_t mNS = 0xFFFFFFFFu / static_cast<uint32_t>(NS) + 1u;   // j / NS = umulhi(j, mNS), j < 2^16
   const uint32_t base = s_seq * kTagStride;
   const uint32_t limit = g_step_wait_limit;
   const bool fused_amax = T.token != nullptr && T.world == 1;
@@ -372,83 +697,177 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
 
   for (int p = 0; p < count; ++p) {
     const SInfo& d = s.info[p];
+    if (d.fmt == kFmtAttn) {   // the attention of this step's token (its items on some CTAs)
+      attn_stage(T, Tp->attn[p], s.info[d.in].out, d.out, s_pos, base + static_cast<uint32_t>(d.in + 1),
+                 base + static_cast<uint32_t>(p + 1), limit, ok);
+      continue;
+    }
     const int K = d.K, N = d.N;
     int b0, b1;
-    cta_blocks(N, b0, b1);
-    if (b0 == b1) continue;   // no rows here: this CTA neither reads the input nor computes
+    cta_tiles(N, b0, b1);
+    const bool norm = d.input == kInNorm;
+    // no rows here: this CTA neither reads the input nor computes -- but every CTA keeps its
+    // copy of the residual row, so a norm's input is read all the same
+    if (b0 == b1 && !norm) continue;
     const bool g32 = d.fmt == kFmtG32;
     const bool unit = d.srows == nullptr;
-    // the row scales of this CTA's rows (they never depend on the input: loaded while it is
-    // awaited; ordered before their use by the barriers below)
-    const int row0 = b0 * 8, nrows = min(b1 * 8, N) - row0;
-    if (!g32)
-      for (int i = threadIdx.x; i < nrows; i += kCT)
-        s.sws[i] = unit ? 1.0f : __ldg(reinterpret_cast<const float*>(d.srows + static_cast<long long>(row0 + i) * d.srs));
-    // ---- the input row
-    const bool tagged = d.in >= 0;
-    const unsigned long long* xt = tagged ? T.words + s.info[d.in].out : nullptr;
-    const uint32_t expect = base + static_cast<uint32_t>(d.in + 1);
-    float Sa = 0.0f;
-    bool cls_path = true;
-    if (g32) {
-      stage_x4(T.x0, xt, expect, K, s.xs, s.xsum, T.status, limit);
+    // the row scales of this CTA's rows: they never depend on the input, so they are copied
+    // asynchronously while it is awaited (complete, and visible to every thread, once the
+    // quantization's last barrier has passed)
+    const int row0 = b0 * kTR, nrows = min(b1 * kTR, N) - row0;
+    if (!g32) {
+      const uint32_t sws_s = smem_addr(s.sws);
+      for (int i = threadIdx.x; i < nrows; i += kCT) {
+        if (unit) s.sws[i] = 1.0f;
+        else cp_async4(sws_s + 4u * static_cast<uint32_t>(i), d.srows + static_cast<long long>(row0 + i) * d.srs);
+      }
+    }
+    // ---- the input row: x0, a projection's output words, or a decoder prologue into xs
+    const float* xsrc = T.x0;
+    const unsigned long long* xt = nullptr;
+    uint32_t expect = 0;
+    if (d.input == kInDefault || d.input == kInAttn) {   // the attention's output: its combined row
+      if (d.in >= 0) {
+        xt = T.words + s.info[d.in].out;
+        expect = base + static_cast<uint32_t>(d.in + 1);
+      }
     } else {
-      if (threadIdx.x == 0) s_flag = 0;
-      qact_row4<kCT, 1>(
-          T.x0, true, s.xs, K, false, s.segm, s.qred,
+      if (norm) {
+        norm_prologue(T, s, d, d.res >= 0 ? s.info[d.res].out : 0, base + static_cast<uint32_t>(d.res + 1), limit);
+      } else if (d.input == kInSwiglu) {
+        swiglu_prologue(T, s, K, s.info[d.in].out, base + static_cast<uint32_t>(d.in + 1), limit);
+      }
+      xsrc = nullptr;   // the row is in xs
+      if (b0 == b1) continue;
+    }
+    float Sa = 0.0f;
+    if (g32) {
+      stage_x4(xsrc, xt, expect, K, s.xs, s.xsum, T.status, limit);
+    } else {
+      qact_row4<kCT, 1, true>(
+          xsrc, true, s.xs, K, false, s.segm, s.qred,
           [&](int i, int q0, int q1, int q2, int q3, int da) {
             const int G = i >> 3;
-            if ((threadIdx.x & 7) == 0) {
-              s.cls[G] = static_cast<uint8_t>(da < 16 ? da : 255);
-              s.dg[G] = static_cast<uint8_t>(da);
-              if (da == 16) s_flag = 1;
-            }
+            if ((threadIdx.x & 7) == 0) s.dg[G] = static_cast<uint8_t>(da);
             *reinterpret_cast<uint32_t*>(s.act + 4 * i) =
                 (q0 & 0xFFu) | ((q1 & 0xFFu) << 8) | ((q2 & 0xFFu) << 16) | (static_cast<uint32_t>(q3 & 0xFF) << 24);
           },
           xt, expect, T.status, &s_Sa, limit);
       Sa = s_Sa;
-      cls_path = s_flag == 0;
     }
     const uint32_t tag = base + static_cast<uint32_t>(p + 1);
     unsigned long long* const yw = T.words + d.out + static_cast<long long>(T.rank) * N;
     const bool last = p == count - 1;
 
-    // one item's stage: wait for it, and release it to the producer
-    auto item_wait = [&](int it) -> const uint8_t* {
-      const int st = it % NS;
-      if (!mbar_wait(smem_addr(s.full + st), static_cast<uint32_t>((it / NS) & 1), T.status)) ok = false;
-      return s.ring + static_cast<size_t>(st) * SB;
+    auto store_row = [&](int row, float y) {
+      if (ok) st_word(yw + row, __float_as_uint(y) | (static_cast<unsigned long long>(tag) << 32), T.world, T.rank, s_delta);
+      if (fused_amax && last) {
+        const unsigned long long k = amax_key(y, static_cast<uint32_t>(T.rank * N + row));
+        best = k > best ? k : best;
+      }
     };
-    auto item_release = [&](int it, uint32_t n) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive_n(smem_addr(s.empty + it % NS), n);
+    // ---- the MMA phase over this CTA's tiles [b0, b1): an item is a tile's cb chunks, one 2 KB
+    // swizzled sub-stage (16 rows x 128 bytes) a chunk. The projection's it-th item is the CTA's
+    // (item_base + it)-th: its stage and parity follow from the running count.
+    const int nt = b1 - b0, ngr = d.ngr, cbn = d.cb, kch = d.kch;
+    const uint32_t bslot = static_cast<uint32_t>(item_base % NS), bph = static_cast<uint32_t>(item_base / NS) & 1u;
+    auto stage_of = [&](int it, uint32_t& par) -> uint32_t {
+      const uint32_t j = bslot + static_cast<uint32_t>(it);
+      const uint32_t q = __umulhi(j, mNS);
+      par = bph ^ (q & 1u);
+      return j - q * static_cast<uint32_t>(NS);
     };
-    // int8 chunk k (a 1 KB swizzled sub-stage) into the class / general accumulators
-    auto chunk8 = [&](const uint8_t* st, int k, int (&D)[4], long long (&acc)[2]) {
-      const uint8_t* row = st + g * kChunkB;
+    // A stage's full barrier is waited on by parity, which cannot tell its current use from the
+    // one before: so first wait (bounded) until the producer has issued the item, i.e. until the
+    // stage's previous use has been released (a warp may reach an item before the warps that
+    // read the stage's previous item are done with it).
+    auto wait_item = [&](int it, uint32_t sl, uint32_t par) {
+      for (uint32_t i = 0; *reinterpret_cast<volatile int*>(&s_issued) <= item_base + it; ++i) {
+        if (i >= kSpinLimit) {
+          atomicOr(T.status, kStatusTimeout);
+          ok = false;
+          break;
+        }
+        if (i >= 16) __nanosleep(32);
+      }
+      const uint32_t fb = full_s + 8u * sl;
+      if (!mbar_try_wait(fb, par) && !mbar_wait(fb, par, T.status)) ok = false;
+    };
+    // int8: the B fragment of group G is its activation bytes (k slots permuted alike in A and B:
+    // bytes 8t .. 8t + 7 of the group in lane t) in column (offset & 7) of accumulator set
+    // offset >> 3: the A fragment (the weights: rows g and g + 8 of the tile) is then multiplied
+    // by 2^(16 - offset) per column, exactly in int32 per set. Offsets above 16 are dropped (the
+    // product shifts out of the 16-bit window); offset 16 is set 2, column 0.
+    auto bfrag = [&](int G, uint32_t& bv0, uint32_t& bv1) -> int {
+      const int c = s.dg[G];
+      const uint2 qv = *reinterpret_cast<const uint2*>(s.act + 32 * G + 8 * t);
+      const bool on = (c & 7) == g;
+      bv0 = on ? qv.x : 0u;
+      bv1 = on ? qv.y : 0u;
+      return c;
+    };
+    // int8 chunk k of a tile (sub: its sub-stage) into the accumulators; set 0 alternates between
+    // two accumulators for a shorter dependence chain
+    auto mma_chunk = [&](uint32_t sub, int k, int (&Da)[4], int (&Db)[4], int (&D1)[4], int (&D2)[4]) {
 #pragma unroll
       for (int sg = 0; sg < 4; ++sg) {
-        const int G = k * 4 + sg;
-        const uint2 qv = *reinterpret_cast<const uint2*>(s.act + 32 * G + 8 * t);
-        const int piece = (2 * sg + (t >> 1)) ^ g;
-        const uint2 bv = *reinterpret_cast<const uint2*>(row + 16 * piece + 8 * (t & 1));
-        if (cls_path) {
-          const int c = s.cls[G];
-          imma_acc(c == g ? qv.x : 0u, c == g + 8 ? qv.x : 0u, c == g ? qv.y : 0u,
-                   c == g + 8 ? qv.y : 0u, bv.x, bv.y, D);
+        uint32_t bv0, bv1;
+        const int c = bfrag(4 * k + sg, bv0, bv1);
+        if (c > 16) continue;
+        const uint2 r0 = lds64(sub + boff[sg]), r1 = lds64(sub + 1024u + boff[sg]);
+        if (c < 8) {
+          if (sg & 1) imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Db);
+          else imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Da);
+        } else if (c < 16) {
+          imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, D1);
         } else {
-          int dd[4] = {0, 0, 0, 0};
-          imma_acc(g == 0 ? qv.x : 0u, 0u, g == 0 ? qv.y : 0u, 0u, bv.x, bv.y, dd);
-          const int sh = 16 - static_cast<int>(s.dg[G]);
-          const long long m = sh >= 0 ? (1ll << sh) : 0ll;
-          acc[0] += static_cast<long long>(dd[0]) * m;
-          acc[1] += static_cast<long long>(dd[1]) * m;
+          imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, D2);
         }
       }
     };
-    // 4-bit chunk k (codes sub-stage st; sc: this lane's two fp16 scales) for lane (row g,
-    // quarter t: bytes 32t .. 32t + 31 of the row's chunk, groups 2t and 2t + 1)
+    // two tiles' chunk k, sharing the B fragments
+    auto mma_chunk2 = [&](uint32_t subA, uint32_t subB, int k, int (&Da)[4], int (&Db)[4], int (&D1)[4], int (&D2)[4],
+                          int (&Ea)[4], int (&Eb)[4], int (&E1)[4], int (&E2)[4]) {
+#pragma unroll
+      for (int sg = 0; sg < 4; ++sg) {
+        uint32_t bv0, bv1;
+        const int c = bfrag(4 * k + sg, bv0, bv1);
+        if (c > 16) continue;
+        const uint2 r0 = lds64(subA + boff[sg]), r1 = lds64(subA + 1024u + boff[sg]);
+        const uint2 q0 = lds64(subB + boff[sg]), q1 = lds64(subB + 1024u + boff[sg]);
+        if (c < 8) {
+          if (sg & 1) {
+            imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Db);
+            imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, Eb);
+          } else {
+            imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Da);
+            imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, Ea);
+          }
+        } else if (c < 16) {
+          imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, D1);
+          imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, E1);
+        } else {
+          imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, D2);
+          imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, E2);
+        }
+      }
+    };
+    // a tile's exact row totals: rows g (rg) and g + 8 (rg8), complete in lane t = 0 of the quad
+    auto totals = [&](const int (&Da)[4], const int (&Db)[4], const int (&D1)[4], const int (&D2)[4],
+                      long long& rg, long long& rg8) {
+      const long long m0 = 1ll << (16 - 2 * t), m1 = 1ll << (15 - 2 * t);
+      const long long n0 = 1ll << (8 - 2 * t), n1 = 1ll << (7 - 2 * t);
+      rg = static_cast<long long>(Da[0] + Db[0]) * m0 + static_cast<long long>(Da[1] + Db[1]) * m1 +
+           static_cast<long long>(D1[0]) * n0 + static_cast<long long>(D1[1]) * n1 + (t == 0 ? static_cast<long long>(D2[0]) : 0ll);
+      rg8 = static_cast<long long>(Da[2] + Db[2]) * m0 + static_cast<long long>(Da[3] + Db[3]) * m1 +
+            static_cast<long long>(D1[2]) * n0 + static_cast<long long>(D1[3]) * n1 + (t == 0 ? static_cast<long long>(D2[2]) : 0ll);
+      rg += __shfl_xor_sync(0xFFFFFFFFu, rg, 1);
+      rg8 += __shfl_xor_sync(0xFFFFFFFFu, rg8, 1);
+      rg += __shfl_xor_sync(0xFFFFFFFFu, rg, 2);
+      rg8 += __shfl_xor_sync(0xFFFFFFFFu, rg8, 2);
+    };
+    // 4-bit chunk k for rows g (st: the chunk's sub-stage, sc: the lane's two fp16 scales of the
+    // row) and g + 8: lane quarter t is bytes 32t .. 32t + 31 of a row's chunk, groups 2t, 2t + 1
     auto chunk4 = [&](const uint8_t* st, const uint8_t* sc, int k, float& acc) {
       const uint8_t* row = st + g * kChunkB;
       const uint4 c0 = *reinterpret_cast<const uint4*>(row + 16 * ((2 * t) ^ g));
@@ -461,105 +880,151 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
       acc = fmaf(half_to_float(static_cast<uint16_t>(sw & 0xFFFFu)), s0, acc);
       acc = fmaf(half_to_float(static_cast<uint16_t>(sw >> 16)), s1, acc);
     };
-    auto store_row = [&](int row, float y) {
-      if (ok) st_word(yw + row, __float_as_uint(y) | (static_cast<unsigned long long>(tag) << 32), T.world, T.rank, s_delta);
-      if (fused_amax && last) {
-        const unsigned long long k = amax_key(y, static_cast<uint32_t>(T.rank * N + row));
-        best = k > best ? k : best;
+    auto chunk4x2 = [&](uint32_t stg, int jj, int k, float& fg, float& fg8) {
+      const uint8_t* st = s.ring + (stg - ring_s) + jj * kSub;
+      const uint8_t* sc = s.ring + (stg - ring_s) + kCodeStage + g * (16 * cbn) + jj * 16 + 4 * t;
+      chunk4(st, sc, k, fg);
+      chunk4(st + 1024, sc + 8 * (16 * cbn), k, fg8);
+    };
+    auto quad_sum = [&](float& f) {
+      f += __shfl_xor_sync(0xFFFFFFFFu, f, 1);
+      f += __shfl_xor_sync(0xFFFFFFFFu, f, 2);
+    };
+    auto emit_rows = [&](int tile, long long rg, long long rg8, float fg, float fg8) {   // lane t = 0
+      for (int h = 0; h < 2; ++h) {
+        const int row = (b0 + tile) * kTR + g + 8 * h;
+        if (row >= N) continue;
+        store_row(row, g32 ? (h ? fg8 : fg) : mm_epilogue(h ? rg8 : rg, s.sws[row - row0], Sa, 16));
       }
     };
 
-    if (d.split == 8) {
-      // the warps share each block's chunks: warp w takes sub-stage w of every item
-      for (int pass0 = b0; pass0 < b1; pass0 += kMaxRedBlocks) {
-        const int pass1 = min(b1, pass0 + kMaxRedBlocks);
-        for (int b = pass0; b < pass1; ++b) {
-          int D[4] = {0, 0, 0, 0};
-          long long acc[2] = {0, 0};
-          float facc = 0.0f;
-          for (int cg = 0; cg < d.ngr; ++cg) {
-            const int it = item_base + (b - b0) * d.ngr + cg;
-            const uint8_t* stg = item_wait(it);
-            const int k = cg * kCB + warp;
-            if (warp < d.cb && k < d.kch && ok) {
-              if (g32) chunk4(stg + warp * 1024, stg + kCodeStage + g * (16 * d.cb) + warp * 16 + 4 * t, k, facc);
-              else chunk8(stg + warp * 1024, k, D, acc);
+    if (nt < kCW) {
+      // ---- few tiles: the S = 8 / TP warps of tile w % TP share its chunks (slice w / TP takes
+      // chunks j = slice mod S of every item), and their row totals meet in shared memory
+      const int TP = nt <= 1 ? 1 : nt <= 2 ? 2 : nt <= 4 ? 4 : 8;
+      const int S = kCW / TP, tile = warp % TP, slice = warp / TP;
+      if (tile < nt) {
+        int Da[4] = {}, Db[4] = {}, D1[4] = {}, D2[4] = {};
+        float fg = 0.0f, fg8 = 0.0f;
+        for (int cg = 0; cg < ngr; ++cg) {
+          const int it = tile * ngr + cg;
+          uint32_t par;
+          const uint32_t sl = stage_of(it, par);
+          wait_item(it, sl, par);
+          const uint32_t stg = ring_s + sl * static_cast<uint32_t>(SB);
+          if (ok)
+            for (int jj = slice; jj < cbn; jj += S) {
+              const int k = cg * kCB + jj;
+              if (k >= kch) break;
+              if (g32) chunk4x2(stg, jj, k, fg, fg8);
+              else mma_chunk(stg + static_cast<uint32_t>(jj * kSub), k, Da, Db, D1, D2);
             }
-            item_release(it, 1);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_n(empty_s + 8u * sl, static_cast<uint32_t>(kCW / S));
+        }
+        long long* red = s.red + warp * kTR;
+        if (g32) {
+          quad_sum(fg);
+          quad_sum(fg8);
+          if (t == 0) {
+            reinterpret_cast<float*>(red)[g] = fg;
+            reinterpret_cast<float*>(red)[g + 8] = fg8;
           }
-          long long* red = s.red + (static_cast<size_t>(b - pass0) * kCW + warp) * 8;
-          if (g32) {
-            facc += __shfl_xor_sync(0xFFFFFFFFu, facc, 1);
-            facc += __shfl_xor_sync(0xFFFFFFFFu, facc, 2);
-            if (t == 0) reinterpret_cast<float*>(red)[g] = facc;
-          } else if (cls_path) {
-            const long long mlo = 1ll << (16 - g), mhi = 1ll << (8 - g);
-            const long long v0 = static_cast<long long>(D[0]) * mlo + static_cast<long long>(D[2]) * mhi;
-            const long long v1 = static_cast<long long>(D[1]) * mlo + static_cast<long long>(D[3]) * mhi;
-            const long long tot = class_reduce8(v0, v1, lane);
-            if ((lane & 12) == 0) red[2 * t + ((lane >> 4) & 1)] = tot;
-          } else if (g == 0) {
-            red[2 * t] = acc[0];
-            red[2 * t + 1] = acc[1];
+        } else {
+          long long rg, rg8;
+          totals(Da, Db, D1, D2, rg, rg8);
+          if (t == 0) {
+            red[g] = rg;
+            red[g + 8] = rg8;
           }
         }
-        cbar();
-        for (int i = threadIdx.x; i < (pass1 - pass0) * 8; i += kCT) {
-          const int bl = i >> 3, r = i & 7;
-          const int row = (pass0 + bl) * 8 + r;
-          if (row >= N) continue;
-          float y;
-          if (g32) {
-            float tot = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kCW; ++w) tot += reinterpret_cast<const float*>(s.red + (static_cast<size_t>(bl) * kCW + w) * 8)[r];
-            y = tot;
-          } else {
-            long long tot = 0;
-#pragma unroll
-            for (int w = 0; w < kCW; ++w) tot += s.red[(static_cast<size_t>(bl) * kCW + w) * 8 + r];
-            y = mm_epilogue(tot, s.sws[row - row0], Sa, 16);
-          }
-          store_row(row, y);
+      }
+      cbar();
+      for (int i = threadIdx.x; i < nt * kTR; i += kCT) {
+        const int tl = i / kTR, r = i % kTR;
+        const int row = (b0 + tl) * kTR + r;
+        if (row >= N) continue;
+        float y;
+        if (g32) {
+          float f = 0.0f;
+          for (int sl2 = 0; sl2 < S; ++sl2) f += reinterpret_cast<const float*>(s.red + (sl2 * TP + tl) * kTR)[r];
+          y = f;
+        } else {
+          long long tot = 0;
+          for (int sl2 = 0; sl2 < S; ++sl2) tot += s.red[(sl2 * TP + tl) * kTR + r];
+          y = mm_epilogue(tot, s.sws[row - row0], Sa, 16);
         }
-        cbar();   // red is reused by the next pass
+        store_row(row, y);
+      }
+    } else if (!g32 && 2 * ngr < NS) {
+      // ---- many tiles (int8): warp w owns tiles 2w, 2w + 1 of each round of 16, both at once (a
+      // warp holds an item while it waits for one ngr further on: ngr < NS keeps that wait
+      // satisfiable)
+      for (int ta = 2 * warp; ta < nt; ta += 2 * kCW) {
+        const int tb = ta + 1;
+        const bool two = tb < nt;
+        int Da[4] = {}, Db[4] = {}, D1[4] = {}, D2[4] = {};
+        int Ea[4] = {}, Eb[4] = {}, E1[4] = {}, E2[4] = {};
+        for (int cg = 0; cg < ngr; ++cg) {
+          uint32_t pa, pb = 0;
+          const uint32_t sa = stage_of(ta * ngr + cg, pa);
+          const uint32_t sb = two ? stage_of(tb * ngr + cg, pb) : sa;
+          wait_item(ta * ngr + cg, sa, pa);
+          if (two) wait_item(tb * ngr + cg, sb, pb);
+          const uint32_t stga = ring_s + sa * static_cast<uint32_t>(SB), stgb = ring_s + sb * static_cast<uint32_t>(SB);
+          if (ok)
+            for (int jj = 0; jj < cbn; ++jj) {
+              const int k = cg * kCB + jj;
+              if (k >= kch) break;
+              if (two) {
+                mma_chunk2(stga + static_cast<uint32_t>(jj * kSub), stgb + static_cast<uint32_t>(jj * kSub), k,
+                           Da, Db, D1, D2, Ea, Eb, E1, E2);
+              } else {
+                mma_chunk(stga + static_cast<uint32_t>(jj * kSub), k, Da, Db, D1, D2);
+              }
+            }
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive_n(empty_s + 8u * sa, kCW);
+            if (two) mbar_arrive_n(empty_s + 8u * sb, kCW);
+          }
+        }
+        long long rg, rg8, qg, qg8;
+        totals(Da, Db, D1, D2, rg, rg8);
+        totals(Ea, Eb, E1, E2, qg, qg8);
+        if (t == 0) {
+          emit_rows(ta, rg, rg8, 0.0f, 0.0f);
+          if (two) emit_rows(tb, qg, qg8, 0.0f, 0.0f);
+        }
       }
     } else {
-      // a warp owns whole blocks
-      for (int b = b0 + warp; b < b1; b += kCW) {
-        int D[4] = {0, 0, 0, 0};
-        long long acc[2] = {0, 0};
-        float facc = 0.0f;
-        for (int cg = 0; cg < d.ngr; ++cg) {
-          const int it = item_base + (b - b0) * d.ngr + cg;
-          const uint8_t* stg = item_wait(it);
-          if (ok) {
-            for (int j = 0; j < d.cb; ++j) {
-              const int k = cg * kCB + j;
-              if (k >= d.kch) break;
-              if (g32) chunk4(stg + j * 1024, stg + kCodeStage + g * (16 * d.cb) + j * 16 + 4 * t, k, facc);
-              else chunk8(stg + j * 1024, k, D, acc);
+      // ---- many tiles, long rows: one tile at a time
+      for (int ta = warp; ta < nt; ta += kCW) {
+        int Da[4] = {}, Db[4] = {}, D1[4] = {}, D2[4] = {};
+        float fa = 0.0f, fa8 = 0.0f;
+        for (int cg = 0; cg < ngr; ++cg) {
+          uint32_t pa;
+          const uint32_t sa = stage_of(ta * ngr + cg, pa);
+          wait_item(ta * ngr + cg, sa, pa);
+          const uint32_t stga = ring_s + sa * static_cast<uint32_t>(SB);
+          if (ok)
+            for (int jj = 0; jj < cbn; ++jj) {
+              const int k = cg * kCB + jj;
+              if (k >= kch) break;
+              if (g32) chunk4x2(stga, jj, k, fa, fa8);
+              else mma_chunk(stga + static_cast<uint32_t>(jj * kSub), k, Da, Db, D1, D2);
             }
-          }
-          item_release(it, kCW);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_n(empty_s + 8u * sa, kCW);
         }
+        long long rg = 0, rg8 = 0;
         if (g32) {
-          facc += __shfl_xor_sync(0xFFFFFFFFu, facc, 1);
-          facc += __shfl_xor_sync(0xFFFFFFFFu, facc, 2);
-          if (t == 0 && b * 8 + g < N) store_row(b * 8 + g, facc);
-        } else if (cls_path) {
-          const long long mlo = 1ll << (16 - g), mhi = 1ll << (8 - g);
-          const long long v0 = static_cast<long long>(D[0]) * mlo + static_cast<long long>(D[2]) * mhi;
-          const long long v1 = static_cast<long long>(D[1]) * mlo + static_cast<long long>(D[3]) * mhi;
-          const long long tot = class_reduce8(v0, v1, lane);
-          const int row = b * 8 + 2 * t + ((lane >> 4) & 1);
-          if ((lane & 12) == 0 && row < N) store_row(row, mm_epilogue(tot, s.sws[row - row0], Sa, 16));
-        } else if (g == 0) {
-          for (int h = 0; h < 2; ++h) {
-            const int row = b * 8 + 2 * t + h;
-            if (row < N) store_row(row, mm_epilogue(acc[h], s.sws[row - row0], Sa, 16));
-          }
+          quad_sum(fa);
+          quad_sum(fa8);
+        } else {
+          totals(Da, Db, D1, D2, rg, rg8);
         }
+        if (t == 0) emit_rows(ta, rg, rg8, fa, fa8);
       }
     }
     item_base += (b1 - b0) * d.ngr;
@@ -611,6 +1076,7 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
         *T.token = static_cast<long long>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
       }
       T.counters[1] = 0;
+      if (T.pos != nullptr) *T.pos = s_pos + 1;
       __threadfence();
       *reinterpret_cast<volatile int*>(T.counters) = static_cast<int>(s_seq + 1);
     }
@@ -639,7 +1105,7 @@ bool encode_rows3(CUtensorMap* map, const uint8_t* rows, int64_t row_bytes, int6
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kChunkB), static_cast<cuuint64_t>(N),
                               static_cast<cuuint64_t>(row_bytes / kChunkB)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(rs), static_cast<cuuint64_t>(kChunkB)};
-  const cuuint32_t box[3] = {kChunkB, 8, static_cast<cuuint32_t>(cb)};
+  const cuuint32_t box[3] = {kChunkB, kTR, static_cast<cuuint32_t>(cb)};
   const cuuint32_t estr[3] = {1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(rows), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -653,7 +1119,7 @@ bool encode_scales(CUtensorMap* map, const uint8_t* sc, int64_t K, int64_t N, in
   if (enc == nullptr) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 16), static_cast<cuuint64_t>(N)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ss)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(16 * cb), 8};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(16 * cb), kTR};
   const cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(sc), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -661,36 +1127,44 @@ bool encode_scales(CUtensorMap* map, const uint8_t* sc, int64_t K, int64_t N, in
 }
 
 struct Layout {
-  int kmax, redb, maxrows, stage_bytes, ns;
+  int kmax, redb, maxrows, hmax, ascr, stage_bytes, ns;
   size_t smem;
 };
 
 // The shared-memory layout of a step (computed alike at prepare and at launch).
 int step_layout_of(const otq_step* st, int sms, Layout* L) {
-  int kmax = 128, redb = 1, maxrows = 8;
+  int kmax = 128, redb = 1, maxrows = 8, hmax = 0, ascr = 0;
   bool any4 = false;
   for (int i = 0; i < st->count; ++i) {
     const otq_step_proj& q = st->projs[i];
-    const int nb = static_cast<int>((q.N + 7) / 8);
+    if (q.fmt == OTQ_STEP_ATTN) {
+      const int maxch = (st->max_pos + kAttnChunk - 1) / kAttnChunk;
+      const int G = q.n_kv > 0 ? q.n_q / q.n_kv : 0;
+      ascr = ascr > 2 * G * maxch ? ascr : 2 * G * maxch;
+      continue;
+    }
+    if (q.input == OTQ_IN_NORM) hmax = hmax > q.K ? hmax : static_cast<int>(q.K);
+    const int nb = static_cast<int>((q.N + kTR - 1) / kTR);
     const int per_cta = (nb + sms - 1) / sms;
-    const bool owner = per_cta >= 2 * kCW;
     kmax = kmax > q.K ? kmax : static_cast<int>(q.K);
-    if (!owner) redb = redb > per_cta ? redb : per_cta;
-    maxrows = maxrows > per_cta * 8 ? maxrows : per_cta * 8;
+    maxrows = maxrows > per_cta * kTR ? maxrows : per_cta * kTR;
     any4 = any4 || q.fmt == OTQ_STEP_G32;
   }
+  // the fixed regions' capacities
+  if (kmax > kKcap || hmax > kHcap || maxrows > kRowsCap || ascr > kAscrCap) return kErrArg;
   L->kmax = kmax;
-  L->redb = redb < kMaxRedBlocks ? redb : kMaxRedBlocks;
+  L->redb = redb;
   L->maxrows = maxrows;
+  L->hmax = hmax;
+  L->ascr = ascr;
   L->stage_bytes = kCodeStage + (any4 ? kScaleStage : 0);
   const size_t budget = 227 * 1024 - 512;   // dynamic + the kernel's static shared memory
-  const size_t fixed = step_smem(st->count, kmax, L->redb, maxrows, 0, L->stage_bytes, nullptr);
-  if (fixed + 2 * (L->stage_bytes + 16) > budget) return kErrArg;
-  int ns = static_cast<int>((budget - fixed) / (L->stage_bytes + 16));
-  while (ns > 2 && step_smem(st->count, kmax, L->redb, maxrows, ns, L->stage_bytes, nullptr) > budget) --ns;
-  if (ns < 2) return kErrArg;
+  const size_t fixed = kOffRing + 1024;     // + the ring's alignment
+  if (fixed + 4 * static_cast<size_t>(L->stage_bytes) > budget) return kErrArg;
+  int ns = static_cast<int>((budget - fixed) / L->stage_bytes);
+  ns = ns < kNScap ? ns : kNScap;
   L->ns = ns;
-  L->smem = step_smem(st->count, kmax, L->redb, maxrows, ns, L->stage_bytes, nullptr);
+  L->smem = fixed + static_cast<size_t>(ns) * L->stage_bytes;
   return kOk;
 }
 
@@ -703,7 +1177,9 @@ int step_layout(const otq_step_proj* pr, int count, int world, int64_t* offsets,
   int64_t off = 0;
   for (int i = 0; i < count; ++i) {
     if (offsets) offsets[i] = off;
-    off += ((pr[i].N * world + 1) / 2) * 2;
+    // an attention stage's partial results stay on each rank (every rank computes them)
+    const int64_t n = pr[i].fmt == OTQ_STEP_ATTN ? pr[i].N : pr[i].N * world;
+    off += ((n + 1) / 2) * 2;
   }
   *total = off;
   return kOk;
@@ -732,6 +1208,21 @@ int step_prepare(const otq_step* st, void* table) {
   for (int i = 0; i < count; ++i) {
     const otq_step_proj& q = st->projs[i];
     SInfo& d = T.info[i];
+    if (q.fmt == OTQ_STEP_ATTN) {
+      d.fmt = q.fmt;
+      d.in = q.in;
+      d.N = static_cast<int>(q.N);
+      d.out = static_cast<int>(offs[i]);
+      SAttn& a = T.attn[i];
+      a.qg = q.q_gain;
+      a.kg = q.k_gain;
+      a.kc = q.kcache;
+      a.vc = q.vcache;
+      a.nq = q.n_q;
+      a.nkv = q.n_kv;
+      a.maxch = (st->max_pos + kAttnChunk - 1) / kAttnChunk;
+      continue;
+    }
     const bool g32 = q.fmt == OTQ_STEP_G32;
     const int64_t row_bytes = g32 ? q.K / 2 : q.K;
     d.kch = static_cast<int>(row_bytes / kChunkB);
@@ -745,10 +1236,11 @@ int step_prepare(const otq_step* st, void* table) {
     d.K = static_cast<int>(q.K);
     d.fmt = q.fmt;
     d.in = q.in;
+    d.input = q.input;
+    d.res = q.res;
+    d.gamma = q.gamma;
     d.out = static_cast<int>(offs[i]);
     d.nfull = static_cast<int>(q.N * st->world);
-    const int nb = static_cast<int>((q.N + 7) / 8);
-    d.split = (nb + sms - 1) / sms >= 2 * kCW ? 1 : 8;
   }
   T.count = count;
   T.world = st->world;
@@ -764,6 +1256,15 @@ int step_prepare(const otq_step* st, void* table) {
   T.counters = st->counters;
   T.amax = reinterpret_cast<unsigned long long*>(st->counters + 2);
   T.token = reinterpret_cast<long long*>(st->token);
+  T.eps = st->eps;
+  T.max_pos = st->max_pos;
+  T.rope_cos = st->rope_cos;
+  T.rope_sin = st->rope_sin;
+  T.pos = st->pos;
+  T.embed = st->embed;
+  T.token_in = reinterpret_cast<const long long*>(st->token_in);
+  T.hmax = L.hmax;
+  T.ascr = L.ascr;
   T.status = status_word();
   if (T.status == nullptr) return kErrCuda;
   return cudaMemcpy(table, &T, sizeof(T), cudaMemcpyHostToDevice) == cudaSuccess ? kOk : kErrCuda;
@@ -781,6 +1282,14 @@ int step_launch(const otq_step* st, const void* table, cudaStream_t stream) {
                              static_cast<int>(L.smem)) != cudaSuccess)
       return kErrCuda;
     configured[dev] = L.smem;
+  }
+  static int occupancy[kMaxDevices] = {0};
+  if (occupancy[dev] == 0) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel, kTh, L.smem) != cudaSuccess)
+      return kErrCuda;
+    if (occ < 1) return kErrArg;   // the step's shared memory does not fit an SM
+    occupancy[dev] = occ;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(sms), 1, 1);   // one CTA an SM, all resident

@@ -119,7 +119,7 @@ class DecodeStep:
             p.rows, p.rs = w.rows.data_ptr(), w.rows.stride(0)
             p.srows = w.srows.data_ptr()
             p.srs = w.srows.stride(0) * w.srows.element_size()
-            p.N, p.K, p.input = w.N, w.K, i - 1
+            p.N, p.K, p.src = w.N, w.K, i - 1
             p.fmt = L.STEP_G32 if w.fmt == "int4-g32" else L.STEP_RSC
         offs = (ctypes.c_int64 * n)()
         total = ctypes.c_int64(0)

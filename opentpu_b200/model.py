@@ -210,3 +210,142 @@ class Qwen3Decoder:
                 rows.append(logits.float().cpu().numpy())
             logits = self.step(tk)
         return out, (np.stack(rows) if keep_logits else None)
+
+
+class FusedDecoder:
+    """The decode step of a Qwen3Decoder as ONE persistent launch (otq_decode_step with decoder
+    stages): per layer the QKV projection on RMSNorm(residual) (the residual the embedding row
+    of the token, or plus the previous layer's down projection), the attention of the token over
+    the KV cache (per-head q / k norms, RoPE, causal softmax; the new key and value appended),
+    the O projection on the attention output, GateUp on RMSNorm(residual + O), Down on
+    SwiGLU(GateUp); then the head on RMSNorm(residual + Down) and the greedy token, which is
+    also the next step's input: steps run back to back on the device with no host round trip.
+
+    Shares the decoder's packed weights, norms, RoPE tables and KV cache (so a prompt prefilled
+    by Qwen3Decoder.prefill continues here). The down projection's input is one QACT range; the
+    decoder should be built with down_chunk=None for the two paths to agree. The float math
+    (norms, attention, SwiGLU) is fp32 in another order than the torch path's: equal to fp32
+    rounding, then the quantized projections amplify what QACT's rounding makes of it."""
+
+    def __init__(self, dec: "Qwen3Decoder"):
+        import ctypes
+        from . import _lib as L
+        if dec.down_chunk is not None:
+            raise ValueError("the fused step quantizes the down projection's input as one range: "
+                             "build the decoder with down_chunk=None")
+        sh, d = dec.shape, dec.d
+        if d != 128 or sh.n_q % sh.n_kv or sh.n_q // sh.n_kv > 4:
+            raise ValueError("the fused step takes head_dim 128 and at most 4 query heads a KV head")
+        self.dec = dec
+        maxch = -(-dec.max_pos // 64)
+        stages = []          # (kind, fields)
+
+        def proj(w, **kw):
+            stages.append(("proj", w, kw))
+            return len(stages) - 1
+
+        prev_down = -2
+        for i, Lr in enumerate(dec.layers):
+            qkv = proj(Lr["qkv"], input=L.IN_NORM, res=prev_down, gamma=Lr["in"])
+            stages.append(("attn", None, dict(src=qkv, layer=i)))
+            att = len(stages) - 1
+            o = proj(Lr["o"], input=L.IN_ATTN, src=att)
+            gu = proj(Lr["gateup"], input=L.IN_NORM, res=o, gamma=Lr["post"])
+            prev_down = proj(Lr["down"], input=L.IN_SWIGLU, src=gu)
+        proj(dec.head, input=L.IN_NORM, res=prev_down, gamma=dec.norm)
+        n = len(stages)
+        if n > 160:
+            raise ValueError(f"{n} stages: more than the step takes")
+        self.projs = (L.StepProj * n)()
+        self._keep = []
+        for k, (kind, w, kw) in enumerate(stages):
+            p = self.projs[k]
+            if kind == "attn":
+                Lr = dec.layers[kw["layer"]]
+                p.fmt, p.src = L.STEP_ATTN, kw["src"]
+                p.N, p.K = sh.n_q * d + sh.n_q * maxch * (d + 2) + sh.n_kv, 0
+                p.q_gain = Lr["qn"].data_ptr() if sh.qk_norm else None
+                p.k_gain = Lr["kn"].data_ptr() if sh.qk_norm else None
+                p.kcache = dec.K[kw["layer"]].data_ptr()
+                p.vcache = dec.V[kw["layer"]].data_ptr()
+                p.n_q, p.n_kv, p.head_dim = sh.n_q, sh.n_kv, d
+                continue
+            p.rows, p.rs = w.rows.data_ptr(), w.rows.stride(0)
+            p.srows = w.srows.data_ptr()
+            p.srs = w.srows.stride(0) * w.srows.element_size()
+            p.N, p.K = w.N, w.K
+            p.fmt = L.STEP_G32 if w.fmt == "int4-g32" else L.STEP_RSC
+            p.input = kw["input"]
+            p.src = kw.get("src", -1)
+            p.res = kw.get("res", -1)
+            if "gamma" in kw:
+                p.gamma = kw["gamma"].data_ptr()
+        offs = (ctypes.c_int64 * n)()
+        total = ctypes.c_int64(0)
+        L.call("otq_step_layout", ctypes.addressof(self.projs), n, 1, ctypes.addressof(offs),
+               ctypes.byref(total))
+        self.offsets, self.stages = list(offs), stages
+        dev = dec.embed.device
+        self.words = torch.zeros(2 * total.value, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.token = torch.zeros(2, dtype=torch.int64, device=dev)   # in and out: self-feeding
+        st = L.Step()
+        st.projs, st.count, st.rank, st.world = ctypes.addressof(self.projs), n, 0, 1
+        st.x0, st.out = None, self.words.data_ptr()
+        st.counters, st.token = self.counters.data_ptr(), self.token.data_ptr()
+        st.eps = sh.eps
+        st.rope_cos, st.rope_sin = dec.cos.data_ptr(), dec.sin.data_ptr()
+        st.max_pos, st.pos = dec.max_pos, self.pos.data_ptr()
+        st.embed, st.token_in, st.vocab = dec.embed.data_ptr(), self.token.data_ptr(), sh.vocab
+        self.step_args = st
+        nb = ctypes.c_int64(0)
+        L.call("otq_step_table_bytes", ctypes.byref(nb))
+        self.table = torch.empty(nb.value, dtype=torch.uint8, device=dev)
+        L.call("otq_step_prepare", ctypes.addressof(st), self.table.data_ptr())
+        self.graph = None
+        self.stream = torch.cuda.Stream()
+
+    def logits(self) -> torch.Tensor:
+        """The last step's logits [vocab] (the head's output words)."""
+        k = len(self.stages) - 1
+        N = self.dec.shape.vocab
+        o = self.offsets[k]
+        return self.words[2 * o:2 * (o + N)].view(N, 2)[:, 0]
+
+    def launch(self):
+        import ctypes
+        from . import _lib as L
+        L.call("otq_decode_step", ctypes.addressof(self.step_args), self.table.data_ptr(),
+               torch.cuda.current_stream().cuda_stream)
+
+    def start(self, token: int, pos: int):
+        """The next step decodes `token` at position `pos` (the KV cache holds positions < pos)."""
+        if not 0 <= pos < self.dec.max_pos:
+            raise ValueError(f"position {pos} past the cache ({self.dec.max_pos})")
+        self.token[0] = token
+        self.pos[0] = pos
+
+    def capture(self):
+        """A CUDA graph of one step (the step's state lives on the device: replays continue)."""
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.launch()
+        torch.cuda.synchronize()
+
+    def generate(self, prompt: list, n_new: int, keep_logits: bool = True):
+        """Greedy decoding: the prompt through the decoder's prefill, then n_new fused steps,
+        each feeding its greedy token to the next on the device. Returns (tokens, logits of
+        every step that chose one [n_new, vocab] or None)."""
+        logits = self.dec.prefill(prompt)
+        first = int(torch.argmax(logits).item())
+        rows = [logits.float().cpu().numpy()] if keep_logits else None
+        out = [first]
+        self.start(first, len(prompt))
+        for _ in range(n_new - 1):
+            self.launch()
+            tk = int(self.token[0].item())
+            out.append(tk)
+            if keep_logits:
+                rows.append(self.logits().cpu().numpy())
+        return out, (np.stack(rows) if keep_logits else None)

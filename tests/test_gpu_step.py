@@ -101,7 +101,7 @@ def test_step_wait_runs_out_when_a_rank_never_writes(lib):
         p = projs[i]
         p.rows, p.rs, p.srows, p.srs = w.rows.data_ptr(), w.rows.stride(0), w.srows.data_ptr(), \
             w.srows.stride(0)
-        p.N, p.K, p.input, p.fmt = w.N // 2, w.K, i - 1, L.STEP_RSC   # this rank's half
+        p.N, p.K, p.src, p.fmt = w.N // 2, w.K, i - 1, L.STEP_RSC   # this rank's half
     total = ctypes.c_int64(0)
     L.call("otq_step_layout", ctypes.addressof(projs), n, 2, None, ctypes.byref(total))
     mine = torch.zeros(2 * total.value, device="cuda")
