@@ -241,6 +241,14 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int
 __device__ __forceinline__ void mbar_arrive_n(uint32_t bar, uint32_t n) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(n) : "memory");
 }
+// imma_acc when p != 0 (p the same in every lane: the mma is executed or skipped by the whole warp)
+__device__ __forceinline__ void imma_acc_if(uint32_t p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1, int (&d)[4]) {
+  asm("{ .reg .pred q; setp.ne.b32 q, %10, 0;\n"
+      "@q mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3}; }"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(p));
+}
 // 4 bytes global -> shared, asynchronously (completed by cp.async.wait_all)
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
@@ -798,60 +806,83 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
     // offset >> 3: the A fragment (the weights: rows g and g + 8 of the tile) is then multiplied
     // by 2^(16 - offset) per column, exactly in int32 per set. Offsets above 16 are dropped (the
     // product shifts out of the 16-bit window); offset 16 is set 2, column 0.
-    auto bfrag = [&](int G, uint32_t& bv0, uint32_t& bv1) -> int {
-      const int c = s.dg[G];
-      const uint2 qv = *reinterpret_cast<const uint2*>(s.act + 32 * G + 8 * t);
-      const bool on = (c & 7) == g;
-      bv0 = on ? qv.x : 0u;
-      bv1 = on ? qv.y : 0u;
-      return c;
-    };
     // int8 chunk k of a tile (sub: its sub-stage) into the accumulators; set 0 alternates between
     // two accumulators for a shorter dependence chain
     auto mma_chunk = [&](uint32_t sub, int k, int (&Da)[4], int (&Db)[4], int (&D1)[4], int (&D2)[4]) {
+      // every load of the chunk first (the four groups' offsets in one word), then the MMAs: all
+      // into set 0 when every offset is below 8 (the usual case), else each group's mma
+      // predicated on its set (no branch between the loads and the MMAs)
+      const uint32_t c4 = *reinterpret_cast<const uint32_t*>(s.dg + 4 * k);
+      uint2 qv[4], r0v[4], r1v[4];
 #pragma unroll
       for (int sg = 0; sg < 4; ++sg) {
-        uint32_t bv0, bv1;
-        const int c = bfrag(4 * k + sg, bv0, bv1);
-        if (c > 16) continue;
-        const uint2 r0 = lds64(sub + boff[sg]), r1 = lds64(sub + 1024u + boff[sg]);
-        if (c < 8) {
-          if (sg & 1) imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Db);
-          else imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Da);
-        } else if (c < 16) {
-          imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, D1);
-        } else {
-          imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, D2);
+        qv[sg] = *reinterpret_cast<const uint2*>(s.act + 32 * (4 * k + sg) + 8 * t);
+        r0v[sg] = lds64(sub + boff[sg]);
+        r1v[sg] = lds64(sub + 1024u + boff[sg]);
+      }
+      if ((c4 & 0xF8F8F8F8u) == 0u) {
+#pragma unroll
+        for (int sg = 0; sg < 4; ++sg) {
+          const bool on = static_cast<int>((c4 >> (8 * sg)) & 7u) == g;
+          const uint32_t bv0 = on ? qv[sg].x : 0u, bv1 = on ? qv[sg].y : 0u;
+          if (sg & 1) imma_acc(r0v[sg].x, r1v[sg].x, r0v[sg].y, r1v[sg].y, bv0, bv1, Db);
+          else imma_acc(r0v[sg].x, r1v[sg].x, r0v[sg].y, r1v[sg].y, bv0, bv1, Da);
+        }
+      } else {
+#pragma unroll
+        for (int sg = 0; sg < 4; ++sg) {
+          const uint32_t c = (c4 >> (8 * sg)) & 0xFFu;
+          const bool on = static_cast<int>(c & 7u) == g;
+          const uint32_t bv0 = on ? qv[sg].x : 0u, bv1 = on ? qv[sg].y : 0u;
+          imma_acc_if(c < 8u, r0v[sg].x, r1v[sg].x, r0v[sg].y, r1v[sg].y, bv0, bv1, Da);
+          imma_acc_if(c - 8u < 8u, r0v[sg].x, r1v[sg].x, r0v[sg].y, r1v[sg].y, bv0, bv1, D1);
+          imma_acc_if(c == 16u, r0v[sg].x, r1v[sg].x, r0v[sg].y, r1v[sg].y, bv0, bv1, D2);
         }
       }
     };
-    // two tiles' chunk k, sharing the B fragments
     auto mma_chunk2 = [&](uint32_t subA, uint32_t subB, int k, int (&Da)[4], int (&Db)[4], int (&D1)[4], int (&D2)[4],
                           int (&Ea)[4], int (&Eb)[4], int (&E1)[4], int (&E2)[4]) {
+      const uint32_t c4 = *reinterpret_cast<const uint32_t*>(s.dg + 4 * k);
+      const bool low = (c4 & 0xF8F8F8F8u) == 0u;
 #pragma unroll
-      for (int sg = 0; sg < 4; ++sg) {
-        uint32_t bv0, bv1;
-        const int c = bfrag(4 * k + sg, bv0, bv1);
-        if (c > 16) continue;
-        const uint2 r0 = lds64(subA + boff[sg]), r1 = lds64(subA + 1024u + boff[sg]);
-        const uint2 q0 = lds64(subB + boff[sg]), q1 = lds64(subB + 1024u + boff[sg]);
-        if (c < 8) {
-          if (sg & 1) {
-            imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Db);
-            imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, Eb);
+      for (int h = 0; h < 2; ++h) {   // two groups' loads at a time
+        uint2 qv[2], r0v[2], r1v[2], q0v[2], q1v[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int sg = 2 * h + u;
+          qv[u] = *reinterpret_cast<const uint2*>(s.act + 32 * (4 * k + sg) + 8 * t);
+          r0v[u] = lds64(subA + boff[sg]);
+          r1v[u] = lds64(subA + 1024u + boff[sg]);
+          q0v[u] = lds64(subB + boff[sg]);
+          q1v[u] = lds64(subB + 1024u + boff[sg]);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int sg = 2 * h + u;
+          const uint32_t c = (c4 >> (8 * sg)) & 0xFFu;
+          const bool on = static_cast<int>(c & 7u) == g;
+          const uint32_t bv0 = on ? qv[u].x : 0u, bv1 = on ? qv[u].y : 0u;
+          const uint2 r0 = r0v[u], r1 = r1v[u], q0 = q0v[u], q1 = q1v[u];
+          if (low) {
+            if (u) {
+              imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Db);
+              imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, Eb);
+            } else {
+              imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Da);
+              imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, Ea);
+            }
           } else {
-            imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, Da);
-            imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, Ea);
+            imma_acc_if(c < 8u, r0.x, r1.x, r0.y, r1.y, bv0, bv1, Da);
+            imma_acc_if(c < 8u, q0.x, q1.x, q0.y, q1.y, bv0, bv1, Ea);
+            imma_acc_if(c - 8u < 8u, r0.x, r1.x, r0.y, r1.y, bv0, bv1, D1);
+            imma_acc_if(c - 8u < 8u, q0.x, q1.x, q0.y, q1.y, bv0, bv1, E1);
+            imma_acc_if(c == 16u, r0.x, r1.x, r0.y, r1.y, bv0, bv1, D2);
+            imma_acc_if(c == 16u, q0.x, q1.x, q0.y, q1.y, bv0, bv1, E2);
           }
-        } else if (c < 16) {
-          imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, D1);
-          imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, E1);
-        } else {
-          imma_acc(r0.x, r1.x, r0.y, r1.y, bv0, bv1, D2);
-          imma_acc(q0.x, q1.x, q0.y, q1.y, bv0, bv1, E2);
         }
       }
     };
+
     // a tile's exact row totals: rows g (rg) and g + 8 (rg8), complete in lane t = 0 of the quad
     auto totals = [&](const int (&Da)[4], const int (&Db)[4], const int (&D1)[4], const int (&D2)[4],
                       long long& rg, long long& rg8) {
