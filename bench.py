@@ -553,6 +553,81 @@ def phi4_sweep(args, world, rank, group, hbm):
 
 
 # ------------------------------------------------------------------------------ prefill
+def decoder_bench(args, hbm, peak_kind):
+    """BASELINE configuration 2 as the model runs it: the Qwen3-0.6B-shaped decoder with
+    random-init N(0, 0.02) weights quantized int8 per row, a seeded random 512-token prompt
+    through the decoder's prefill, then fused decode steps -- one launch a token doing both
+    norms, QKV, q/k norms and RoPE, attention over the KV cache, O, the SwiGLU MLP, the LM head
+    and the greedy token, fed to the next step on the device. Timed: a CUDA graph of one step
+    replayed (each replay decodes the next position). e2e: steps launched from the host, each
+    step's token written from pinned host memory and read back (generate()'s loop)."""
+    import torch
+    from opentpu_b200.model import FusedDecoder, Qwen3Decoder
+    shape = WL.QWEN3_0_6B
+    n_e2e = 32
+    prompt_len = 512
+    max_pos = prompt_len + args.warmup + args.steps + n_e2e + 8
+    W = WL.decoder_weights(shape, seed=0)
+    dec = Qwen3Decoder(shape, W, fmt="int8-row", max_pos=max_pos, down_chunk=None)
+    del W
+    fd = FusedDecoder(dec)
+    prompt = np.random.default_rng(1).integers(0, shape.vocab, prompt_len).tolist()
+    first = int(torch.argmax(dec.prefill(prompt)).item())
+    fd.start(first, prompt_len)
+    fd.capture()
+    with torch.cuda.stream(fd.stream):
+        for _ in range(args.warmup):
+            fd.graph.replay()
+    torch.cuda.synchronize()
+    pos0 = int(fd.pos[0].item())
+    ms = graph_ms(fd.graph, fd.stream, args.steps, 1)
+    # bytes a step: every packed weight (int8 rows + fp32 row scales) and the KV cache read by
+    # the attention (both caches, every layer, at the timed region's mean position)
+    wbytes = 0
+    for L in dec.layers:
+        for k in ("qkv", "o", "gateup", "down"):
+            w = L[k]
+            wbytes += w.N * w.K + 4 * w.N
+    wbytes += dec.head.N * dec.head.K + 4 * dec.head.N
+    mean_pos = pos0 + args.steps / 2
+    kv = 2 * shape.layers * mean_pos * shape.n_kv * shape.head_dim * 4
+    tok_host = torch.zeros(1, dtype=torch.int64).pin_memory()
+    tok = int(fd.token[0].item())
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        tok_host[0] = tok
+        fd.token[0:1].copy_(tok_host, non_blocking=True)
+        fd.launch()
+        tok_host.copy_(fd.token[0:1], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        tok = int(tok_host[0])
+    e2e_ms = (time.perf_counter() - t0) / n_e2e * 1e3
+    ach = (wbytes + kv) / (ms * 1e-3) / 1e9
+    out = {
+        "workload": "Qwen3-0.6B-shaped int8 per-row decoder (28 layers, hidden 1024, 16/8 heads "
+                    "of 128, SwiGLU 3072, vocab 151936, random N(0, 0.02) weights): 512-token "
+                    "seeded prompt, then fused greedy steps",
+        "tok_s": 1e3 / ms, "ms_per_token": ms, "weight_gb_s": wbytes / (ms * 1e-3) / 1e9,
+        "weights_bytes_per_token": wbytes, "positions": [pos0, pos0 + args.steps],
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                     "frac": ach / hbm, "traffic": None,
+                     "kernel": "step_kernel (the whole decoder step, 141 stages, one launch)",
+                     "bytes_per_launch": wbytes + kv, "us_per_launch": ms * 1e3,
+                     "peak_kind": f"{peak_kind} (copy)"},
+        "e2e": {"ms_per_token": e2e_ms, "tok_s": 1e3 / e2e_ms,
+                "value": wbytes / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
+                "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
+                "api": "FusedDecoder.launch with the token written from and read to pinned host "
+                       "memory every step"},
+        "gpu_launches": args.steps + n_e2e,
+    }
+    fd.graph = None
+    del fd, dec
+    torch.cuda.empty_cache()
+    return out
+
+
 def prefill_layer(shape, world, rank, gen, xs=None):
     """One layer's seven projections for the prefill GEMM: int8-row
     weights (uniform int8 rows, Sw ~ 1e-3: the GEMM's cost does not depend on the values),
@@ -779,6 +854,7 @@ def main():
     ap.add_argument("--no-4bit", action="store_true")
     ap.add_argument("--no-config1", action="store_true")
     ap.add_argument("--no-phi4", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -829,6 +905,7 @@ def main():
                 "bytes_per_launch": per_rank, "us_per_launch": ms * 1e3,
                 "peak_kind": f"{peak_kind} (copy)"}
         head = None
+        decoder = None if (args.no_decoder or world > 1) else decoder_bench(args, hbm, peak_kind)
         c1 = None if args.no_config1 else config1(world, max(3, min(args.steps, 50)))
         dec4 = None if args.no_4bit else decode_4bit(args, world, rank, group, hbm, peak_kind)
         phi4 = None if args.no_phi4 else phi4_sweep(args, world, rank, group, hbm)
@@ -875,6 +952,7 @@ def main():
             "parity": parity,
             "gpu_launches": chain.launches * args.steps,
             "clocks": clocks.summary(),
+            "decoder": decoder,
             "config1": c1,
             "decode_4bit": dec4,
             "prefill": prefill,

@@ -81,7 +81,7 @@ constexpr int kInSwiglu = OTQ_IN_SWIGLU;
 constexpr int kInAttn = OTQ_IN_ATTN;
 constexpr int kHd = 128;                     // attention head dimension
 constexpr int kMaxG = 4;                     // query heads a KV head
-constexpr int kAttnChunk = 64;               // positions an attention item
+constexpr int kAttnChunk = 32;               // positions an attention item
 
 __device__ uint32_t g_step_wait_limit = 1u << 22;
 
@@ -187,6 +187,7 @@ constexpr size_t kOffXr = al16(kOffEmpty + kNScap * 8);
 constexpr size_t kOffAttn = al16(kOffXr + kHcap * 4);
 constexpr size_t kOffAscr = al16(kOffAttn + (kMaxG * kHd + 2 * kHd + kMaxG * kAttnChunk) * 4);
 constexpr size_t kOffRing = al16(kOffAscr + kAscrCap * 4);
+static_assert(2 * kAttnChunk * kHd <= kKcap, "an attention chunk's keys and values fit the row staging");
 
 extern __shared__ __align__(16) unsigned char smem_raw[];   // the step kernel's dynamic shared memory
 
@@ -538,6 +539,18 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
   for (int item = blockIdx.x; item < a.nkv * nch; item += gridDim.x) {
     const int h = item / nch, c = item % nch;
     const int j0 = c * kAttnChunk, j1 = min(j0 + kAttnChunk, pos + 1);
+    // the chunk's cached keys and values (positions before pos) into shared memory, every copy
+    // in flight at once: keys at xs[0 ..), values at xs[kAttnChunk * hd ..)
+    {
+      const int nold = min(j1, pos) - j0;
+      const uint32_t kv_s = smem_addr(s.xs);
+      for (int i = threadIdx.x; i < 2 * nold * (kHd / 4); i += kCT) {
+        const int which = i / (nold * (kHd / 4)), r = (i / (kHd / 4)) % nold, q4 = i % (kHd / 4);
+        const float* src = (which ? a.vc : a.kc) + (static_cast<long long>(j0 + r) * a.nkv + h) * kHd + 4 * q4;
+        const uint32_t dst = kv_s + 4u * static_cast<uint32_t>((which * kAttnChunk + r) * kHd + 4 * q4);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+      }
+    }
     // the query heads h G .. h G + G - 1, the new key and value
     for (int i = threadIdx.x; i < (G + 2) * kHd / 4; i += kCT) {
       const int part = (4 * i) / kHd, e = (4 * i) % kHd;
@@ -550,11 +563,13 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
     cbar();
     if (warp <= G) head_norm_rope(warp < G ? s.aq + warp * kHd : s.akv, warp < G ? a.qg : a.kg, cs, sn,
                                   T.eps, lane);
+    asm volatile("cp.async.wait_all;" ::: "memory");
     cbar();
+    const float* sk = s.xs;
+    const float* sv = s.xs + kAttnChunk * kHd;
     // scores: warp w takes positions j0 + w, j0 + w + 8, ...
     for (int j = j0 + warp; j < j1; j += kCW) {
-      const float4 kv = j == pos ? *reinterpret_cast<const float4*>(s.akv + 4 * lane)
-                                 : ld_cg4(a.kc + (static_cast<long long>(j) * a.nkv + h) * kHd + 4 * lane);
+      const float4 kv = *reinterpret_cast<const float4*>((j == pos ? s.akv : sk + (j - j0) * kHd) + 4 * lane);
       for (int g = 0; g < G; ++g) {
         const float4 q = *reinterpret_cast<const float4*>(s.aq + g * kHd + 4 * lane);
         float d = (q.x * kv.x + q.y * kv.y) + (q.z * kv.z + q.w * kv.w);
@@ -592,8 +607,7 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
       const int g = i / kHd, dd = i % kHd;
       float o = 0.0f;
       for (int j = j0; j < j1; ++j) {
-        const float v = j == pos ? s.akv[kHd + dd]
-                                 : __ldcg(a.vc + (static_cast<long long>(j) * a.nkv + h) * kHd + dd);
+        const float v = j == pos ? s.akv[kHd + dd] : sv[(j - j0) * kHd + dd];
         o += s.asc[g * kAttnChunk + (j - j0)] * v;
       }
       if (ok) {

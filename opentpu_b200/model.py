@@ -237,7 +237,7 @@ class FusedDecoder:
         if d != 128 or sh.n_q % sh.n_kv or sh.n_q // sh.n_kv > 4:
             raise ValueError("the fused step takes head_dim 128 and at most 4 query heads a KV head")
         self.dec = dec
-        maxch = -(-dec.max_pos // 64)
+        maxch = -(-dec.max_pos // 32)
         stages = []          # (kind, fields)
 
         def proj(w, **kw):
