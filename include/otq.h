@@ -250,9 +250,9 @@ typedef struct otq_step_proj {
   int res;               /* OTQ_IN_NORM: -2, or the projection added to the residual first */
   const float* gamma;    /* OTQ_IN_NORM: the norm's gains [K] (16-byte aligned) */
   /* OTQ_STEP_ATTN: `in` is the QKV projection (q [n_q * hd], k [n_kv * hd], v [n_kv * hd]);
-   * N = n_q * hd + n_q * ceil(max_pos / 32) * (hd + 2) + n_kv words: the attention's output row
-   * (query head major: the input of an OTQ_IN_ATTN projection), the partial results of its
-   * chunks of 32 positions, and an arrival count a KV head; K unused. q and k of the new token:
+   * N = n_q * hd + n_q * ceil(max_pos / 32) * (hd + 2) words: the attention's output row (query
+   * head major: the input of an OTQ_IN_ATTN projection) and the partial results of its chunks of
+   * 32 positions; K unused. q and k of the new token:
    * per-head RMSNorm times q_gain / k_gain (NULL: none), then rotate-half RoPE at *pos; k and v
    * go into the caches at *pos. At most 2 * (n_q / n_kv) * ceil(max_pos / 32) <= 2048. */
   const float* q_gain;

@@ -466,8 +466,8 @@ int check_step(const otq_step* s) {
           p.n_q / p.n_kv > 4 || p.kcache == nullptr || p.vcache == nullptr)
         return kErrArg;
       if (full(p.in) < static_cast<int64_t>(p.n_q + 2 * p.n_kv) * 128) return kErrArg;
-      // the combined row, the partial results and a count a KV head
-      if (p.N < static_cast<int64_t>(p.n_q) * 128 + static_cast<int64_t>(p.n_q) * ((s->max_pos + 31) / 32) * 130 + p.n_kv)
+      // the combined row and the partial results
+      if (p.N < static_cast<int64_t>(p.n_q) * 128 + static_cast<int64_t>(p.n_q) * ((s->max_pos + 31) / 32) * 130)
         return kErrArg;
       if (!aligned(p.kcache, 16) || !aligned(p.vcache, 16)) return kErrAlign;
       if ((p.q_gain && !aligned(p.q_gain, 16)) || (p.k_gain && !aligned(p.k_gain, 16))) return kErrAlign;

@@ -434,25 +434,22 @@ __device__ void swiglu_prologue(const StepHead& T, const SSmem& s, int K, int in
 }
 
 
-// rmsnorm of one head (hd values in smem v, a warp) times gains g (null: none), then
-// rotate-half RoPE with this position's tables (qwen3.py:719-724, 335-346).
-__device__ __forceinline__ void head_norm_rope(float* v, const float* g, const float* cs,
-                                               const float* sn, float eps, int lane) {
+// rmsnorm of one head (hd values in smem v, a warp) times gains gn (has_g false: none), then
+// rotate-half RoPE with this position's tables (lane l holds cos / sin [4 (l & 15) ..])
+// (qwen3.py:719-724, 335-346).
+__device__ __forceinline__ void head_norm_rope(float* v, bool has_g, float4 gn, float4 c, float4 sv,
+                                               float eps, int lane) {
   float4 x = *reinterpret_cast<const float4*>(v + 4 * lane);
-  if (g != nullptr) {
+  if (has_g) {
     float ss = (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
     const float den = sqrtf(ss / static_cast<float>(kHd) + eps);
-    const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + lane);
-    x = make_float4((x.x / den) * gg.x, (x.y / den) * gg.y, (x.z / den) * gg.z, (x.w / den) * gg.w);
+    x = make_float4((x.x / den) * gn.x, (x.y / den) * gn.y, (x.z / den) * gn.z, (x.w / den) * gn.w);
   }
   // lanes 0..15 hold elements 0..63 (v1), lanes 16..31 elements 64..127 (v2)
   const float4 other = make_float4(__shfl_xor_sync(0xFFFFFFFFu, x.x, 16), __shfl_xor_sync(0xFFFFFFFFu, x.y, 16),
                                    __shfl_xor_sync(0xFFFFFFFFu, x.z, 16), __shfl_xor_sync(0xFFFFFFFFu, x.w, 16));
-  const int j = 4 * (lane & 15);
-  const float4 c = __ldg(reinterpret_cast<const float4*>(cs + j));
-  const float4 sv = __ldg(reinterpret_cast<const float4*>(sn + j));
   float4 r;
   if (lane < 16) {   // v1 * c - v2 * s
     r = make_float4(x.x * c.x - other.x * sv.x, x.y * c.y - other.y * sv.y, x.z * c.z - other.z * sv.z,
@@ -469,47 +466,77 @@ __device__ __forceinline__ void head_norm_rope(float* v, const float* g, const f
 // The combine of KV head h's nch chunks for its G query heads (flash-decoding): with M the
 // largest chunk maximum, chunk c weighs e_c = exp(m_c - M) / L, L = sum_c exp(m_c - M) l_c, and
 // the output row of query head h G + g is sum_c e_c o_c, in chunk order. Written as tagged
-// words at `out` (query head major, hd each): the O projection's input. The whole CTA, after
-// the head's count came to nch (every chunk's partial words are written and fenced before its
-// count: they are read here through L2 without waiting on their tags).
+// words at `out` (query head major, hd each): the O projection's input. The whole CTA; the
+// chunks' partial words are awaited by their tags (bounded).
 __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, int h, int G,
-                             int nch, int part_out, int out, uint32_t tag, bool ok) {
-  float* ml = s.ascr;   // [G][nch] (m, l), then the chunks' weights
+                             int nch, int part_out, int out, uint32_t tag, uint32_t limit, bool ok) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* wt = s.ascr;   // [G][nch] the chunks' weights
   const long long stride = kHd + 2;
-  for (int i = threadIdx.x; i < G * nch; i += kCT) {
-    const int g = i / nch, c = i % nch;
-    unsigned long long w0, w1;
-    ld_tagged2(T.words + part_out + (static_cast<long long>(h * G + g) * a.maxch + c) * stride, w0, w1);
-    ml[2 * i] = __uint_as_float(static_cast<uint32_t>(w0));
-    ml[2 * i + 1] = __uint_as_float(static_cast<uint32_t>(w1));
-  }
-  cbar();
-  for (int g = threadIdx.x; g < G; g += kCT) {
-    float* hm = ml + 2 * g * nch;
-    float M = -INFINITY, L = 0.0f;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, hm[2 * c]);
-    for (int c = 0; c < nch; ++c) {
-      const float e = expf(hm[2 * c] - M);
-      hm[2 * c] = e;
-      L += e * hm[2 * c + 1];
+  if (warp < G) {   // warp g: lane c takes chunks c, c + 32, ...
+    const unsigned long long* ph = T.words + part_out + static_cast<long long>(h * G + warp) * a.maxch * stride;
+    float M = -INFINITY;
+    for (int c = lane; c < nch; c += 32) {
+      unsigned long long w0, w1;
+      ld_tagged2(ph + c * stride, w0, w1);
+      for (uint32_t spin = 0; behind(w0, tag) || behind(w1, tag); ++spin) {
+        if (spin >= limit) {
+          atomicOr(T.status, kStatusTimeout);
+          break;
+        }
+        if (spin >= 64) __nanosleep(32);
+        ld_tagged2(ph + c * stride, w0, w1);
+      }
+      const float m = __uint_as_float(static_cast<uint32_t>(w0));
+      wt[warp * nch + c] = m;
+      if (c < 32) s.asc[warp * kAttnChunk + c] = __uint_as_float(static_cast<uint32_t>(w1));   // l, first pass
+      M = fmaxf(M, m);
     }
-    for (int c = 0; c < nch; ++c) hm[2 * c] = hm[2 * c] / L;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    float L = 0.0f;
+    for (int c = lane; c < nch; c += 32) {
+      unsigned long long w0, w1;
+      if (c >= 32) ld_tagged2(ph + c * stride, w0, w1);   // past the first pass: l again
+      const float l = c < 32 ? s.asc[warp * kAttnChunk + c] : __uint_as_float(static_cast<uint32_t>(w1));
+      const float e = expf(wt[warp * nch + c] - M);
+      wt[warp * nch + c] = e;
+      L += e * l;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
+    for (int c = lane; c < nch; c += 32) wt[warp * nch + c] = wt[warp * nch + c] / L;
   }
   cbar();
-  constexpr int kBatch = 8;
+  constexpr int kBatch = 4;   // (more in flight costs the step kernel registers at its call)
   for (int i = threadIdx.x; i < G * kHd; i += kCT) {
     const int g = i / kHd, dd = i % kHd;
     const unsigned long long* pb = T.words + part_out + static_cast<long long>(h * G + g) * a.maxch * stride + 2 + dd;
-    const float* wt = ml + 2 * g * nch;
+    const float* w = wt + g * nch;
     float o = 0.0f;
     for (int c0 = 0; c0 < nch; c0 += kBatch) {
-      uint32_t w[kBatch];
+      unsigned long long v[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u)
-        if (c0 + u < nch) w[u] = __ldcg(reinterpret_cast<const unsigned int*>(pb + (c0 + u) * stride));
+        if (c0 + u < nch) v[u] = *reinterpret_cast<const volatile unsigned long long*>(pb + (c0 + u) * stride);
+      for (uint32_t spin = 0;; ++spin) {   // the batch, until every word carries this step's tag
+        bool late = false;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          if (c0 + u < nch && behind(v[u], tag)) {
+            late = true;
+            v[u] = *reinterpret_cast<const volatile unsigned long long*>(pb + (c0 + u) * stride);
+          }
+        if (!late) break;
+        if (spin >= limit) {
+          atomicOr(T.status, kStatusTimeout);
+          break;
+        }
+        if (spin >= 64) __nanosleep(32);
+      }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u)
-        if (c0 + u < nch) o += wt[2 * (c0 + u)] * __uint_as_float(w[u]);
+        if (c0 + u < nch) o += w[c0 + u] * __uint_as_float(static_cast<uint32_t>(v[u]));
     }
     if (ok) {
       unsigned long long* dst = T.words + out + static_cast<long long>(h * G + g) * kHd + dd;
@@ -518,38 +545,48 @@ __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, 
   }
 }
 
-// An attention stage: items (KV head h, chunk c of kAttnChunk positions) dealt to the CTAs.
-// Each reads its query heads, the new key and value (the QKV projection's words), normalises
-// and rotates q and k, scores positions [64 c, min(64 c + 64, pos + 1)) against the cache (the
-// new token's key from shared memory), and stores per query head (m, l, o) as tagged words;
-// the item holding position pos stores the new key and value into the caches.
+// An attention stage: items (chunk c of kAttnChunk positions, KV head h), chunk-major, dealt to
+// the CTAs in order. Each reads its query heads, the new key and value (the QKV projection's
+// words), normalises and rotates q and k, scores positions [32 c, min(32 c + 32, pos + 1))
+// against the cache (the new token's key from shared memory), and stores per query head
+// (m, l, o) as tagged words. The item of a head's last chunk also stores the new key and value
+// into the caches and then combines the head's chunks. Combining items come after every other
+// item (chunk-major order) and a CTA takes its items in order, so a combine only ever waits on
+// items that run ahead of it.
 __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int qkv_out, int out,
                                        int pos, uint32_t expect, uint32_t tag, uint32_t limit,
                                        bool ok) {
-  __shared__ int s_last;
   const SSmem s = carve(smem_raw);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int part_out = out + a.nq * kHd;                                 // the partial results
-  const int cnt_out = part_out + a.nq * a.maxch * (kHd + 2);             // a count a KV head
+  const int part_out = out + a.nq * kHd;   // the partial results
   const int G = a.nq / a.nkv;
   const int nch = pos / kAttnChunk + 1;
   const float* cs = T.rope_cos + static_cast<long long>(pos) * (kHd / 2);
   const float* sn = T.rope_sin + static_cast<long long>(pos) * (kHd / 2);
   const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(kHd));
   for (int item = blockIdx.x; item < a.nkv * nch; item += gridDim.x) {
-    const int h = item / nch, c = item % nch;
+    const int c = item / a.nkv, h = item % a.nkv;
     const int j0 = c * kAttnChunk, j1 = min(j0 + kAttnChunk, pos + 1);
     // the chunk's cached keys and values (positions before pos) into shared memory, every copy
-    // in flight at once: keys at xs[0 ..), values at xs[kAttnChunk * hd ..)
+    // in flight at once: keys at xs[0 ..), values at xs[kAttnChunk * hd ..); a row is 32 copies
     {
       const int nold = min(j1, pos) - j0;
       const uint32_t kv_s = smem_addr(s.xs);
-      for (int i = threadIdx.x; i < 2 * nold * (kHd / 4); i += kCT) {
-        const int which = i / (nold * (kHd / 4)), r = (i / (kHd / 4)) % nold, q4 = i % (kHd / 4);
+      for (int i = threadIdx.x; i < 64 * nold; i += kCT) {
+        const int rr = i >> 5, q4 = i & 31;
+        const int which = rr >= nold ? 1 : 0, r = rr - which * nold;
         const float* src = (which ? a.vc : a.kc) + (static_cast<long long>(j0 + r) * a.nkv + h) * kHd + 4 * q4;
-        const uint32_t dst = kv_s + 4u * static_cast<uint32_t>((which * kAttnChunk + r) * kHd + 4 * q4);
+        const uint32_t dst = kv_s + 16u * static_cast<uint32_t>((which * kAttnChunk + r) * (kHd / 4) + q4);
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
       }
+    }
+    // the head norm's gains and this position's rotation, ahead of their use
+    float4 gn = make_float4(1.0f, 1.0f, 1.0f, 1.0f), rc = gn, rs = gn;
+    if (warp <= G) {
+      const float* gp = warp < G ? a.qg : a.kg;
+      if (gp != nullptr) gn = __ldg(reinterpret_cast<const float4*>(gp) + lane);
+      rc = __ldg(reinterpret_cast<const float4*>(cs + 4 * (lane & 15)));
+      rs = __ldg(reinterpret_cast<const float4*>(sn + 4 * (lane & 15)));
     }
     // the query heads h G .. h G + G - 1, the new key and value
     for (int i = threadIdx.x; i < (G + 2) * kHd / 4; i += kCT) {
@@ -561,22 +598,33 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
       *reinterpret_cast<float4*>(dst) = v;
     }
     cbar();
-    if (warp <= G) head_norm_rope(warp < G ? s.aq + warp * kHd : s.akv, warp < G ? a.qg : a.kg, cs, sn,
-                                  T.eps, lane);
+    if (warp <= G)
+      head_norm_rope(warp < G ? s.aq + warp * kHd : s.akv, (warp < G ? a.qg : a.kg) != nullptr, gn, rc, rs,
+                     T.eps, lane);
     asm volatile("cp.async.wait_all;" ::: "memory");
     cbar();
     const float* sk = s.xs;
     const float* sv = s.xs + kAttnChunk * kHd;
-    // scores: warp w takes positions j0 + w, j0 + w + 8, ...
-    for (int j = j0 + warp; j < j1; j += kCW) {
-      const float4 kv = *reinterpret_cast<const float4*>((j == pos ? s.akv : sk + (j - j0) * kHd) + 4 * lane);
-      for (int g = 0; g < G; ++g) {
-        const float4 q = *reinterpret_cast<const float4*>(s.aq + g * kHd + 4 * lane);
-        float d = (q.x * kv.x + q.y * kv.y) + (q.z * kv.z + q.w * kv.w);
+    // scores: thread (g, j, quarter) takes 32 of position j's dims (float4 index skewed by lane:
+    // conflict-free rows), the quarters meet by two shuffles
+    for (int u = threadIdx.x; u < G * kAttnChunk * 4; u += kCT) {
+      const int g = u / (kAttnChunk * 4), j = (u >> 2) % kAttnChunk, qt = u & 3;
+      const bool valid = j0 + j < j1;
+      const float* kr = (j0 + j == pos ? s.akv : sk + j * kHd) + 32 * qt;
+      const float* qr = s.aq + g * kHd + 32 * qt;
+      float d = 0.0f;
+      if (valid) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
-        if (lane == 0) s.asc[g * kAttnChunk + (j - j0)] = d * inv_sqrt;
+        for (int e = 0; e < 8; ++e) {
+          const int f = (e + lane) & 7;
+          const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * f);
+          const float4 q = *reinterpret_cast<const float4*>(qr + 4 * f);
+          d += (q.x * kv.x + q.y * kv.y) + (q.z * kv.z + q.w * kv.w);
+        }
       }
+      d += __shfl_xor_sync(0xFFFFFFFFu, d, 1);
+      d += __shfl_xor_sync(0xFFFFFFFFu, d, 2);
+      if (qt == 0 && valid) s.asc[g * kAttnChunk + j] = d * inv_sqrt;
     }
     cbar();
     // per query head: the chunk's largest score and the sum of the exponentials (warp g)
@@ -596,47 +644,40 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
       if (lane == 0 && ok) {
-        unsigned long long* out = T.words + part_out + (static_cast<long long>(h * G + warp) * a.maxch + c) * (kHd + 2);
-        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(out), "l"(__float_as_uint(m) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
-        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(out + 1), "l"(__float_as_uint(l) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
+        unsigned long long* o = T.words + part_out + (static_cast<long long>(h * G + warp) * a.maxch + c) * (kHd + 2);
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(o), "l"(__float_as_uint(m) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(o + 1), "l"(__float_as_uint(l) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
       }
     }
     cbar();
-    // the unnormalised outputs: thread (g, dd)
+    // the unnormalised outputs: thread (g, dd), four partial sums over the positions
     for (int i = threadIdx.x; i < G * kHd; i += kCT) {
       const int g = i / kHd, dd = i % kHd;
-      float o = 0.0f;
-      for (int j = j0; j < j1; ++j) {
-        const float v = j == pos ? s.akv[kHd + dd] : sv[(j - j0) * kHd + dd];
-        o += s.asc[g * kAttnChunk + (j - j0)] * v;
+      const float* p = s.asc + g * kAttnChunk;
+      const int n = j1 - j0;
+      float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+      for (int j = 0; j < n; ++j) {
+        const float v = j0 + j == pos ? s.akv[kHd + dd] : sv[j * kHd + dd];
+        o4[j & 3] += p[j] * v;
       }
+      const float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
       if (ok) {
-        unsigned long long* out = T.words + part_out + (static_cast<long long>(h * G + g) * a.maxch + c) * (kHd + 2) + 2 + dd;
-        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(out), "l"(__float_as_uint(o) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
+        unsigned long long* dst = T.words + part_out + (static_cast<long long>(h * G + g) * a.maxch + c) * (kHd + 2) + 2 + dd;
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(dst), "l"(__float_as_uint(o) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
       }
     }
-    // the new key and value into the caches
-    if (c == nch - 1 && ok)
-      for (int i = threadIdx.x; i < 2 * kHd; i += kCT) {
-        float* cache = i < kHd ? a.kc : a.vc;
-        cache[(static_cast<long long>(pos) * a.nkv + h) * kHd + (i % kHd)] = s.akv[i];
-      }
-    // the head's count: the CTA that brings it to nch combines the head's chunks (its partial
-    // words, fenced before every count, are then all written)
-    cbar();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      unsigned int* cnt = reinterpret_cast<unsigned int*>(T.words + cnt_out + h);
-      const bool last = atomicAdd(cnt, 1u) == static_cast<unsigned int>(nch - 1);
-      if (last) {
-        atomicExch(cnt, 0u);   // the next step counts from zero
-        __threadfence();
-      }
-      s_last = last;
+    if (c == nch - 1) {
+      // the new key and value into the caches, then the head's combine
+      if (ok)
+        for (int i = threadIdx.x; i < 2 * kHd; i += kCT) {
+          float* cache = i < kHd ? a.kc : a.vc;
+          cache[(static_cast<long long>(pos) * a.nkv + h) * kHd + (i % kHd)] = s.akv[i];
+        }
+      cbar();
+      attn_combine(T, s, a, h, G, nch, part_out, out, tag, limit, ok);
     }
-    cbar();
-    if (s_last) attn_combine(T, s, a, h, G, nch, part_out, out, tag, ok);
-    cbar();   // aq / akv / asc / ascr are rewritten by the next item
+    cbar();   // xs / aq / akv / asc / ascr are rewritten by the next item
   }
 }
 

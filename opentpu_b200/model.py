@@ -263,7 +263,7 @@ class FusedDecoder:
             if kind == "attn":
                 Lr = dec.layers[kw["layer"]]
                 p.fmt, p.src = L.STEP_ATTN, kw["src"]
-                p.N, p.K = sh.n_q * d + sh.n_q * maxch * (d + 2) + sh.n_kv, 0
+                p.N, p.K = sh.n_q * d + sh.n_q * maxch * (d + 2), 0
                 p.q_gain = Lr["qn"].data_ptr() if sh.qk_norm else None
                 p.k_gain = Lr["kn"].data_ptr() if sh.qk_norm else None
                 p.kcache = dec.K[kw["layer"]].data_ptr()
