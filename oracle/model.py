@@ -188,6 +188,15 @@ def noise_floor(oracle: Qwen3Oracle, prompt: list, tokens: list, clean=None) -> 
     return float(np.abs(a.astype(np.float64) - b).max())
 
 
+def noise_run(oracle: Qwen3Oracle, prompt: list, tokens: list, clean) -> tuple:
+    """The 1-ulp input noise run against the clean logits: (its largest |logit| change -- the
+    noise floor --, its smallest per-step cosine to the clean logits)."""
+    b = oracle.forced(prompt, tokens, noise=True).astype(np.float64)
+    a = np.asarray(clean, np.float64)
+    cos = (a * b).sum(-1) / np.linalg.norm(a, axis=-1) / np.linalg.norm(b, axis=-1)
+    return float(np.abs(a - b).max()), float(cos.min())
+
+
 def clear_steps(ref_logits, noise: float) -> np.ndarray:
     """Steps whose top-1 leads its runner-up by more than the noise floor (not near ties)."""
     top2 = np.sort(np.asarray(ref_logits), -1)[:, -2:]
