@@ -422,24 +422,26 @@ def config1(world: int, reps: int):
 
 
 def decode_4bit(args, world, rank, group, hbm, peak_kind):
-    """the Qwen3-0.6B step with int4-g32 layers (fp16 group scales,
-    weight-only, fp32 activations) and the int8-row head."""
+    """BASELINE configuration 3's decode step: the Qwen3-0.6B step with int4-g32 layers (fp16
+    group scales, weight-only, fp32 activations) and the int8-row head, as one persistent launch
+    a step (row shards over the ranks, every projection's output words stored to every rank)."""
     import torch
-    from opentpu_b200.decode import DecodeChain
+    from opentpu_b200.decode import DecodeStep
     shape = WL.QWEN3_0_6B
-    # int4-g32 is weight-only (no MM, so no fused gather): NCCL all-gathers with world > 1
-    c4 = DecodeChain(shape, fmt="int4-g32", head_fmt="int8-row", world=world, rank=rank,
-                     group=group, gather="nccl")
+    c4 = DecodeStep(shape, fmt="int4-g32", head_fmt="int8-row", world=world, rank=rank,
+                    group=group)
     c4.capture()
     c4.replay(args.warmup)
     torch.cuda.synchronize()
     n4 = max(10, args.steps)
     ms4 = graph_ms(c4.graph, c4.stream, n4, world)
-    roof = None
-    if world == 1:
-        roof = layers_roofline(c4, world, max(10, args.steps), hbm, peak_kind,
-                               "linear_g32_row_kernel / linear_g32_kernel (the 112 layer "
-                               "projections of a step, int4-g32, M=1)")
+    per_rank = c4.weight_bytes / world + sum(4 * K + 8 * N for _, N, K, _ in c4.plan)
+    ach = per_rank / (ms4 * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+            "traffic": read_traffic("step_kernel_qwen3_0_6b_int4g32.md", world),
+            "kernel": "step_kernel (the whole 4-bit decode step, one persistent launch)",
+            "bytes_per_launch": per_rank, "us_per_launch": ms4 * 1e3,
+            "peak_kind": f"{peak_kind} (copy)"}
     e2e_ms, h2d, d2h, _ = closed_loop(c4, max(10, min(args.steps, 200)), world)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -451,12 +453,14 @@ def decode_4bit(args, world, rank, group, hbm, peak_kind):
                                   "scales (weight-only, fp32 activations), 151936x1024 "
                                   "int8-row LM head, M=1 (BASELINE configuration 3)",
                       "weights_bytes_per_step": c4.weight_bytes,
-                      "parallelism": f"row-shard x{world}" + (" + NCCL all-gather per "
-                                                             "projection" if world > 1 else "")},
+                      "parallelism": f"row-shard x{world}" + (" + each projection's output "
+                                                             "words stored to every rank "
+                                                             "inside the step kernel"
+                                                             if world > 1 else "")},
            "roofline": roof, "cpu_baseline": cpu,
            "e2e": {"value": c4.weight_bytes / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
                    "ms_per_token": e2e_ms, "h2d_bytes_per_step": h2d,
-                   "d2h_bytes_per_step": d2h, "api": "DecodeChain.run_host, closed loop"},
+                   "d2h_bytes_per_step": d2h, "api": "DecodeStep.run_host, closed loop"},
            "gpu_launches": c4.launches * n4}
     c4.release()
     del c4
@@ -553,9 +557,10 @@ def phi4_sweep(args, world, rank, group, hbm):
 
 
 # ------------------------------------------------------------------------------ prefill
-def decoder_bench(args, hbm, peak_kind):
-    """BASELINE configuration 2 as the model runs it: the Qwen3-0.6B-shaped decoder with
-    random-init N(0, 0.02) weights quantized int8 per row, a seeded random 512-token prompt
+def decoder_bench(args, hbm, peak_kind, fmt="int8-row"):
+    """BASELINE configurations 2 (fmt int8-row) and 3 (int4-g32 layers, int8-row head) as the
+    model runs them: the Qwen3-0.6B-shaped decoder with random-init N(0, 0.02) weights
+    quantized, a seeded random 512-token prompt
     through the decoder's prefill, then fused decode steps -- one launch a token doing both
     norms, QKV, q/k norms and RoPE, attention over the KV cache, O, the SwiGLU MLP, the LM head
     and the greedy token, fed to the next step on the device. Timed: a CUDA graph of one step
@@ -568,7 +573,7 @@ def decoder_bench(args, hbm, peak_kind):
     prompt_len = 512
     max_pos = prompt_len + args.warmup + args.steps + n_e2e + 8
     W = WL.decoder_weights(shape, seed=0)
-    dec = Qwen3Decoder(shape, W, fmt="int8-row", max_pos=max_pos, down_chunk=None)
+    dec = Qwen3Decoder(shape, W, fmt=fmt, head_fmt="int8-row", max_pos=max_pos, down_chunk=None)
     del W
     fd = FusedDecoder(dec)
     prompt = np.random.default_rng(1).integers(0, shape.vocab, prompt_len).tolist()
@@ -583,12 +588,10 @@ def decoder_bench(args, hbm, peak_kind):
     ms = graph_ms(fd.graph, fd.stream, args.steps, 1)
     # bytes a step: every packed weight (int8 rows + fp32 row scales) and the KV cache read by
     # the attention (both caches, every layer, at the timed region's mean position)
-    wbytes = 0
-    for L in dec.layers:
-        for k in ("qkv", "o", "gateup", "down"):
-            w = L[k]
-            wbytes += w.N * w.K + 4 * w.N
-    wbytes += dec.head.N * dec.head.K + 4 * dec.head.N
+    def packed(w):   # int8 rows + an fp32 scale a row, or nibbles + an fp16 scale a group
+        return w.N * w.K // 2 + w.N * (w.K // 32) * 2 if w.fmt == "int4-g32" else w.N * w.K + 4 * w.N
+    wbytes = sum(packed(L[k]) for L in dec.layers for k in ("qkv", "o", "gateup", "down"))
+    wbytes += packed(dec.head)
     mean_pos = pos0 + args.steps / 2
     kv = 2 * shape.layers * mean_pos * shape.n_kv * shape.head_dim * 4
     tok_host = torch.zeros(1, dtype=torch.int64).pin_memory()
@@ -605,13 +608,16 @@ def decoder_bench(args, hbm, peak_kind):
     e2e_ms = (time.perf_counter() - t0) / n_e2e * 1e3
     ach = (wbytes + kv) / (ms * 1e-3) / 1e9
     out = {
-        "workload": "Qwen3-0.6B-shaped int8 per-row decoder (28 layers, hidden 1024, 16/8 heads "
-                    "of 128, SwiGLU 3072, vocab 151936, random N(0, 0.02) weights): 512-token "
-                    "seeded prompt, then fused greedy steps",
+        "workload": f"Qwen3-0.6B-shaped decoder, layers {fmt}, int8-row head (28 layers, hidden "
+                    "1024, 16/8 heads of 128, SwiGLU 3072, vocab 151936, random N(0, 0.02) "
+                    "weights): 512-token seeded prompt, then fused greedy steps",
         "tok_s": 1e3 / ms, "ms_per_token": ms, "weight_gb_s": wbytes / (ms * 1e-3) / 1e9,
         "weights_bytes_per_token": wbytes, "positions": [pos0, pos0 + args.steps],
         "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
-                     "frac": ach / hbm, "traffic": None,
+                     "frac": ach / hbm,
+                     "traffic": read_traffic("step_kernel_qwen3_0_6b_decoder_int8row_pos512.md", 1)
+                     if fmt == "int8-row" else None,
+                     "traffic_note": "ncu capture of one step at position 513 (KV cache 117 MB)",
                      "kernel": "step_kernel (the whole decoder step, 141 stages, one launch)",
                      "bytes_per_launch": wbytes + kv, "us_per_launch": ms * 1e3,
                      "peak_kind": f"{peak_kind} (copy)"},
@@ -776,8 +782,9 @@ def prefill_bench(args, world, rank, local, group, steps, warmup):
 # ------------------------------------------------------------------------------ profile runs
 def profile_run(what: str):
     """A few launches for an ncu capture: the LM head GEMV alone, two decode steps, three
-    grouped prefill launches of one SmolLM3-3B layer, or five int4-g32 GEMVs of one activation
-    row over a 65536 x 4096 matrix (144 MB of codes and scales, more than L2)."""
+    grouped prefill launches of one SmolLM3-3B layer, five int4-g32 GEMVs of one activation
+    row over a 65536 x 4096 matrix (144 MB of codes and scales, more than L2), three one-launch
+    decode steps (int8-row or int4-g32 layers), or three fused decoder steps at position 512."""
     import torch
     from opentpu_b200 import linear
     from opentpu_b200.decode import DecodeChain
@@ -804,6 +811,16 @@ def profile_run(what: str):
         st = DecodeStep(shape, fmt="int4-g32" if what == "stepkernel4" else "int8-row")
         for _ in range(3):
             st.step_eager()
+    elif what == "decoderkernel":
+        from opentpu_b200.model import FusedDecoder, Qwen3Decoder
+        W = WL.decoder_weights(shape, seed=0)
+        dec = Qwen3Decoder(shape, W, fmt="int8-row", max_pos=640, down_chunk=None)
+        del W
+        fd = FusedDecoder(dec)
+        prompt = np.random.default_rng(1).integers(0, shape.vocab, 512).tolist()
+        fd.start(int(torch.argmax(dec.prefill(prompt)).item()), 512)
+        for _ in range(3):
+            fd.launch()
     elif what == "prefill":
         items, _ = prefill_layer(WL.SMOLLM3_3B, 1, 0,
                                  torch.Generator(device="cuda").manual_seed(0))
@@ -849,7 +866,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["head", "step", "prefill", "g32", "stepkernel",
-                                          "stepkernel4"])
+                                          "stepkernel4", "decoderkernel"])
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-4bit", action="store_true")
     ap.add_argument("--no-config1", action="store_true")
@@ -890,8 +907,9 @@ def main():
     with Clocks(local) as clocks:
         ms = graph_ms(chain.graph, chain.stream, args.steps, world)
         value = total_bytes / (ms * 1e-3) / 1e9
-        e2e_ms, h2d, d2h, _ = closed_loop(chain, max(10, min(args.steps, 200)), world)
+        # (before the closed loop, which replaces the step's seeded input)
         parity = parity_vs_one_gpu(chain, world, rank) if world > 1 else None
+        e2e_ms, h2d, d2h, _ = closed_loop(chain, max(10, min(args.steps, 200)), world)
         # the dominant (only) kernel: the step's one launch; its bytes are this rank's weights
         # and scales plus every projection's input row and output words
         per_rank = total_bytes / world + sum(4 * K + 8 * N for _, N, K, _ in chain.plan)
@@ -905,7 +923,10 @@ def main():
                 "bytes_per_launch": per_rank, "us_per_launch": ms * 1e3,
                 "peak_kind": f"{peak_kind} (copy)"}
         head = None
-        decoder = None if (args.no_decoder or world > 1) else decoder_bench(args, hbm, peak_kind)
+        decoder = decoder4 = None
+        if not args.no_decoder and world == 1:
+            decoder = decoder_bench(args, hbm, peak_kind, "int8-row")
+            decoder4 = decoder_bench(args, hbm, peak_kind, "int4-g32")
         c1 = None if args.no_config1 else config1(world, max(3, min(args.steps, 50)))
         dec4 = None if args.no_4bit else decode_4bit(args, world, rank, group, hbm, peak_kind)
         phi4 = None if args.no_phi4 else phi4_sweep(args, world, rank, group, hbm)
@@ -953,6 +974,7 @@ def main():
             "gpu_launches": chain.launches * args.steps,
             "clocks": clocks.summary(),
             "decoder": decoder,
+            "decoder_4bit": decoder4,
             "config1": c1,
             "decode_4bit": dec4,
             "prefill": prefill,

@@ -143,7 +143,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* st
   if (status != nullptr) atomicOr(status, 1);   // kStatusTimeout
   return false;
 }
-// [src, src + bytes) -> shared dst, completing `bytes` of transaction on bar (no multicast).
+// [src, src + bytes) -> shared dst (this CTA only), completing `bytes` of transaction on bar.
 __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
