@@ -233,6 +233,13 @@ OTQ_API int otq_set_wait_limit(uint32_t polls);
 #define OTQ_IN_SWIGLU 2  /* silu(y[0:K]) * y[K:2K], y the output of projection `in` */
 #define OTQ_IN_ATTN 3    /* the output of attention stage `in` */
 
+/* What a projection writes. */
+#define OTQ_EPI_NONE 0   /* its N output rows */
+#define OTQ_EPI_SWIGLU 1 /* rows are gate and up rows interleaved in blocks of 8 (rows 16j .. 16j + 7
+                            gate rows 8j .. 8j + 7, rows 16j + 8 .. 16j + 15 the up rows 8j ..
+                            8j + 7; N a multiple of 16, at most 112 rows an SM); it writes
+                            silu(gate) * up, N / 2 words */
+
 /* One projection of otq_decode_step. */
 typedef struct otq_step_proj {
   const uint8_t* rows;   /* RSC: int8 rows [N][rs]; G32: codes [N][rs] (K/2 bytes used).
@@ -260,6 +267,7 @@ typedef struct otq_step_proj {
   float* kcache;         /* [max_pos][n_kv][hd] fp32 (16-byte aligned) */
   float* vcache;
   int n_q, n_kv, head_dim;   /* head_dim 128, n_q / n_kv at most 4 */
+  int epilogue;          /* OTQ_EPI_* (projections; not the last stage) */
 } otq_step_proj;
 
 #define OTQ_STEP_MAX 160

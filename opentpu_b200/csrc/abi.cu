@@ -454,7 +454,10 @@ int check_step(const otq_step* s) {
   if (s->embed != nullptr && (s->token_in == nullptr || s->vocab <= 0 || !aligned(s->embed, 16)))
     return kErrArg;
   bool plain_in = false, attn = false;
-  auto full = [&](int i) { return s->projs[i].N * s->world; };   // a projection's output row
+  auto full = [&](int i) {   // a projection's output row
+    const otq_step_proj& q = s->projs[i];
+    return (q.epilogue == OTQ_EPI_SWIGLU ? q.N / 2 : q.N) * s->world;
+  };
   auto is_proj = [&](int j, int i) {
     return j >= 0 && j < i && s->projs[j].fmt != OTQ_STEP_ATTN;
   };
@@ -475,6 +478,9 @@ int check_step(const otq_step* s) {
     }
     const bool g32 = p.fmt == OTQ_STEP_G32;
     if (p.fmt != OTQ_STEP_RSC && !g32) return kErrFormat;
+    if (p.epilogue != OTQ_EPI_NONE &&
+        (p.epilogue != OTQ_EPI_SWIGLU || p.N % 16 || i == s->count - 1))
+      return kErrArg;
     if (p.N <= 0 || p.K <= 0 || p.K % (g32 ? 256 : OTQ_D) || p.K > 255 * OTQ_D) return kErrArg;
     if (p.N * s->world >= (int64_t{1} << 30)) return kErrArg;
     if (p.rows == nullptr || p.rs < (g32 ? p.K / 2 : p.K) || p.rs >= kStrideLimit) return kErrArg;

@@ -79,6 +79,7 @@ constexpr int kInDefault = OTQ_IN_DEFAULT;
 constexpr int kInNorm = OTQ_IN_NORM;
 constexpr int kInSwiglu = OTQ_IN_SWIGLU;
 constexpr int kInAttn = OTQ_IN_ATTN;
+constexpr int kEpiSwiglu = OTQ_EPI_SWIGLU;
 constexpr int kHd = 128;                     // attention head dimension
 constexpr int kMaxG = 4;                     // query heads a KV head
 constexpr int kAttnChunk = 32;               // positions an attention item
@@ -101,7 +102,8 @@ struct SInfo {            // one stage, as the kernel reads it (shared memory)
   int ngr;                // items a block (ceil(kch / cb))
   int input;              // OTQ_IN_*
   int res;                // OTQ_IN_NORM: -2 (start from x0) or the projection added first
-  int pad[3];
+  int epi;                // OTQ_EPI_*
+  int pad[2];
 };
 static_assert(sizeof(SInfo) == 80, "SInfo is 80 bytes");
 
@@ -819,7 +821,11 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
       Sa = s_Sa;
     }
     const uint32_t tag = base + static_cast<uint32_t>(p + 1);
-    unsigned long long* const yw = T.words + d.out + static_cast<long long>(T.rank) * N;
+    // OTQ_EPI_SWIGLU: rows 16j .. 16j + 7 gate, 16j + 8 .. 16j + 15 up; output word 8j + r is
+    // silu(gate) * up of tile rows r and r + 8 (the formula of the SwiGLU prologue)
+    const bool swi = d.epi == kEpiSwiglu;
+    unsigned long long* const yw = T.words + d.out + static_cast<long long>(T.rank) * (swi ? N / 2 : N);
+    auto swiglu = [](float gv, float uv) { return (gv / (1.0f + expf(-gv))) * uv; };
     const bool last = p == count - 1;
 
     auto store_row = [&](int row, float y) {
@@ -1026,21 +1032,28 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
         }
       }
       cbar();
-      for (int i = threadIdx.x; i < nt * kTR; i += kCT) {
-        const int tl = i / kTR, r = i % kTR;
-        const int row = (b0 + tl) * kTR + r;
-        if (row >= N) continue;
-        float y;
+      auto row_value = [&](int tl, int r) -> float {   // tile tl's row r: the slices' sum
         if (g32) {
           float f = 0.0f;
           for (int sl2 = 0; sl2 < S; ++sl2) f += reinterpret_cast<const float*>(s.red + (sl2 * TP + tl) * kTR)[r];
-          y = f;
-        } else {
-          long long tot = 0;
-          for (int sl2 = 0; sl2 < S; ++sl2) tot += s.red[(sl2 * TP + tl) * kTR + r];
-          y = mm_epilogue(tot, s.sws[row - row0], Sa, 16);
+          return f;
         }
-        store_row(row, y);
+        long long tot = 0;
+        for (int sl2 = 0; sl2 < S; ++sl2) tot += s.red[(sl2 * TP + tl) * kTR + r];
+        return mm_epilogue(tot, s.sws[(b0 + tl) * kTR + r - row0], Sa, 16);
+      };
+      if (swi) {
+        for (int i = threadIdx.x; i < nt * 8; i += kCT) {
+          const int tl = i >> 3, r = i & 7;
+          store_row((b0 + tl) * 8 + r, swiglu(row_value(tl, r), row_value(tl, r + 8)));
+        }
+      } else {
+        for (int i = threadIdx.x; i < nt * kTR; i += kCT) {
+          const int tl = i / kTR, r = i % kTR;
+          const int row = (b0 + tl) * kTR + r;
+          if (row >= N) continue;
+          store_row(row, row_value(tl, r));
+        }
       }
     } else if (!g32 && 2 * ngr < NS) {
       // ---- many tiles (int8): warp w owns tiles 2w, 2w + 1 of each round of 16, both at once (a
@@ -1232,6 +1245,8 @@ int step_layout_of(const otq_step* st, int sms, Layout* L) {
     if (q.input == OTQ_IN_NORM) hmax = hmax > q.K ? hmax : static_cast<int>(q.K);
     const int nb = static_cast<int>((q.N + kTR - 1) / kTR);
     const int per_cta = (nb + sms - 1) / sms;
+    // the SwiGLU epilogue is written where a CTA's warps share its tiles (fewer than 8 a CTA)
+    if (q.epilogue == OTQ_EPI_SWIGLU && per_cta >= kCW) return kErrArg;
     kmax = kmax > q.K ? kmax : static_cast<int>(q.K);
     maxrows = maxrows > per_cta * kTR ? maxrows : per_cta * kTR;
     any4 = any4 || q.fmt == OTQ_STEP_G32;
@@ -1264,7 +1279,8 @@ int step_layout(const otq_step_proj* pr, int count, int world, int64_t* offsets,
   for (int i = 0; i < count; ++i) {
     if (offsets) offsets[i] = off;
     // an attention stage's partial results stay on each rank (every rank computes them)
-    const int64_t n = pr[i].fmt == OTQ_STEP_ATTN ? pr[i].N : pr[i].N * world;
+    const int64_t n = pr[i].fmt == OTQ_STEP_ATTN ? pr[i].N
+                      : (pr[i].epilogue == OTQ_EPI_SWIGLU ? pr[i].N / 2 : pr[i].N) * world;
     off += ((n + 1) / 2) * 2;
   }
   *total = off;
@@ -1326,7 +1342,8 @@ int step_prepare(const otq_step* st, void* table) {
     d.res = q.res;
     d.gamma = q.gamma;
     d.out = static_cast<int>(offs[i]);
-    d.nfull = static_cast<int>(q.N * st->world);
+    d.epi = q.epilogue;
+    d.nfull = static_cast<int>((q.epilogue == OTQ_EPI_SWIGLU ? q.N / 2 : q.N) * st->world);
   }
   T.count = count;
   T.world = st->world;

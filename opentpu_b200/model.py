@@ -212,6 +212,19 @@ class Qwen3Decoder:
         return out, (np.stack(rows) if keep_logits else None)
 
 
+def interleave_gate_up(w: linear.PackedWeight) -> linear.PackedWeight:
+    """The fused [gate; up] projection's rows reordered for the step kernel's SwiGLU epilogue:
+    blocks of 8 gate rows then the matching 8 up rows (rows 16j .. 16j + 7 = gate 8j .. 8j + 7,
+    16j + 8 .. 16j + 15 = up 8j .. 8j + 7), scale rows alike; a copy on the GPU."""
+    F = w.N // 2
+    if w.N % 16:
+        raise ValueError("the gate/up projection's rows must be a multiple of 16")
+    idx = torch.arange(w.N, device=w.rows.device).view(2, F // 8, 8).permute(1, 0, 2).reshape(-1)
+    srows = None if w.srows is None else w.srows.index_select(0, idx).contiguous()
+    return linear.PackedWeight(w.fmt, w.N, w.K, w.rows.index_select(0, idx).contiguous(), srows,
+                               w.k0, w.rsc)
+
+
 class FusedDecoder:
     """The decode step of a Qwen3Decoder as ONE persistent launch (otq_decode_step with decoder
     stages): per layer the QKV projection on RMSNorm(residual) (the residual the embedding row
@@ -227,7 +240,7 @@ class FusedDecoder:
     (norms, attention, SwiGLU) is fp32 in another order than the torch path's: equal to fp32
     rounding, then the quantized projections amplify what QACT's rounding makes of it."""
 
-    def __init__(self, dec: "Qwen3Decoder"):
+    def __init__(self, dec: "Qwen3Decoder", swiglu_epilogue: bool = True):
         import ctypes
         from . import _lib as L
         if dec.down_chunk is not None:
@@ -250,8 +263,13 @@ class FusedDecoder:
             stages.append(("attn", None, dict(src=qkv, layer=i)))
             att = len(stages) - 1
             o = proj(Lr["o"], input=L.IN_ATTN, src=att)
-            gu = proj(Lr["gateup"], input=L.IN_NORM, res=o, gamma=Lr["post"])
-            prev_down = proj(Lr["down"], input=L.IN_SWIGLU, src=gu)
+            if swiglu_epilogue:   # silu(gate) * up written by the GateUp projection itself
+                gu = proj(interleave_gate_up(Lr["gateup"]), input=L.IN_NORM, res=o,
+                          gamma=Lr["post"], epilogue=L.EPI_SWIGLU)
+                prev_down = proj(Lr["down"], input=L.IN_DEFAULT, src=gu)
+            else:                 # ... or computed by the Down projection from both halves
+                gu = proj(Lr["gateup"], input=L.IN_NORM, res=o, gamma=Lr["post"])
+                prev_down = proj(Lr["down"], input=L.IN_SWIGLU, src=gu)
         proj(dec.head, input=L.IN_NORM, res=prev_down, gamma=dec.norm)
         n = len(stages)
         if n > 160:
@@ -278,6 +296,8 @@ class FusedDecoder:
             p.input = kw["input"]
             p.src = kw.get("src", -1)
             p.res = kw.get("res", -1)
+            p.epilogue = kw.get("epilogue", L.EPI_NONE)
+            self._keep.append(w)
             if "gamma" in kw:
                 p.gamma = kw["gamma"].data_ptr()
         offs = (ctypes.c_int64 * n)()

@@ -64,6 +64,23 @@ def test_fused_step_graph_replays_continue():
     assert torch.equal(a.logits(), b.logits())
 
 
+@pytest.mark.parametrize("fmt", ["int8-row", "int4-g32"])
+def test_swiglu_epilogue_equals_prologue(fmt):
+    """SwiGLU written by the GateUp projection's epilogue (gate / up rows interleaved) and SwiGLU
+    read by the Down projection's prologue give the same steps bit for bit."""
+    from opentpu_b200.model import FusedDecoder, Qwen3Decoder
+    shape = WL.TINY
+    W = WL.decoder_weights(shape, seed=5)
+    prompt = WL.prompt_ids(shape, 20, seed=6)
+    a = FusedDecoder(Qwen3Decoder(shape, W, fmt=fmt, max_pos=64, down_chunk=None))
+    b = FusedDecoder(Qwen3Decoder(shape, W, fmt=fmt, max_pos=64, down_chunk=None),
+                     swiglu_epilogue=False)
+    ta, la = a.generate(prompt, 8)
+    tb, lb = b.generate(prompt, 8)
+    assert ta == tb
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+
+
 @pytest.mark.slow
 def test_fused_qwen3_0_6b_int8_row_512_64():
     """Configuration 2 through the fused step."""

@@ -315,14 +315,15 @@ def _token_parity(dev_tokens, dev_logits, ora, prompt):
     1-ulp input noise causes, tools/validate.py Golden._noisy; a fixed threshold, not the run's
     own error), the device's token is the golden's first maximal logit. The device's logits
     must also follow the golden's: their smallest per-step cosine to the golden departs from 1
-    by at most twice as much as the 1-ulp noise run's does. Returns (clear steps, floor)."""
+    by at most twice as much as the 1-ulp noise run's does, or 2e-4, whichever is larger (on a
+    small model the noise run may flip no quantization at all). Returns (clear steps, floor)."""
     from oracle.model import clear_steps, noise_run
     ref = ora.forced(prompt, dev_tokens)
     floor, noise_cos = noise_run(ora, prompt, dev_tokens, ref)
     clear = clear_steps(ref, floor)
     cos = [float(np.dot(a, b) / np.linalg.norm(a) / np.linalg.norm(b))
            for a, b in zip(dev_logits.astype(np.float64), ref.astype(np.float64))]
-    assert min(cos) >= 1.0 - 2.0 * (1.0 - noise_cos), (min(cos), noise_cos)
+    assert min(cos) >= 1.0 - max(2.0 * (1.0 - noise_cos), 2e-4), (min(cos), noise_cos)
     tokens = np.array(dev_tokens)
     bad = np.nonzero(clear & (tokens != ref.argmax(-1)))[0]
     assert bad.size == 0, f"clear steps {bad.tolist()} differ (floor {floor})"
