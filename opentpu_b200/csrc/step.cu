@@ -467,11 +467,13 @@ __device__ __forceinline__ void head_norm_rope(float* v, bool has_g, float4 gn, 
 
 // The combine of KV head h's nch chunks for its G query heads (flash-decoding): with M the
 // largest chunk maximum, chunk c weighs e_c = exp(m_c - M) / L, L = sum_c exp(m_c - M) l_c, and
-// the output row of query head h G + g is sum_c e_c o_c, in chunk order. Written as tagged
-// words at `out` (query head major, hd each): the O projection's input. The whole CTA; the
-// chunks' partial words are awaited by their tags (bounded).
+// output o = g hd + dd (query head h G + g) is sum_c e_c o_c, in chunk order. This CTA writes
+// outputs [o0, o1) as tagged words at `out` (query head major): the O projection's input. The
+// chunks' words are awaited by their tags (bounded); every (output, chunk) word is one load of
+// one thread, all of a pass in flight at once, and the products meet in shared memory.
 __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, int h, int G,
-                             int nch, int part_out, int out, uint32_t tag, uint32_t limit, bool ok) {
+                             int nch, int part_out, int out, uint32_t tag, uint32_t limit, bool ok,
+                             int o0, int o1) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* wt = s.ascr;   // [G][nch] the chunks' weights
   const long long stride = kHd + 2;
@@ -510,40 +512,40 @@ __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, 
     for (int c = lane; c < nch; c += 32) wt[warp * nch + c] = wt[warp * nch + c] / L;
   }
   cbar();
-  constexpr int kBatch = 4;   // (more in flight costs the step kernel registers at its call)
-  for (int i = threadIdx.x; i < G * kHd; i += kCT) {
-    const int g = i / kHd, dd = i % kHd;
-    const unsigned long long* pb = T.words + part_out + static_cast<long long>(h * G + g) * a.maxch * stride + 2 + dd;
-    const float* w = wt + g * nch;
-    float o = 0.0f;
-    for (int c0 = 0; c0 < nch; c0 += kBatch) {
-      unsigned long long v[kBatch];
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u)
-        if (c0 + u < nch) v[u] = *reinterpret_cast<const volatile unsigned long long*>(pb + (c0 + u) * stride);
-      for (uint32_t spin = 0;; ++spin) {   // the batch, until every word carries this step's tag
-        bool late = false;
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u)
-          if (c0 + u < nch && behind(v[u], tag)) {
-            late = true;
-            v[u] = *reinterpret_cast<const volatile unsigned long long*>(pb + (c0 + u) * stride);
-          }
-        if (!late) break;
+  const int no = o1 - o0;
+  const int per = max(1, kKcap / max(no, 1));   // chunks a pass (the products fit xs)
+  float acc[2] = {0.0f, 0.0f};                  // thread i's outputs o0 + i, o0 + i + kCT
+  for (int c0 = 0; c0 < nch; c0 += per) {
+    const int nc = min(per, nch - c0);
+    for (int u = threadIdx.x; u < no * nc; u += kCT) {
+      const int oi = u / nc, c = c0 + u % nc;
+      const int g = (o0 + oi) / kHd, dd = (o0 + oi) % kHd;
+      const unsigned long long* pw = T.words + part_out + (static_cast<long long>(h * G + g) * a.maxch + c) * stride + 2 + dd;
+      unsigned long long w = *reinterpret_cast<const volatile unsigned long long*>(pw);
+      for (uint32_t spin = 0; behind(w, tag); ++spin) {
         if (spin >= limit) {
           atomicOr(T.status, kStatusTimeout);
           break;
         }
         if (spin >= 64) __nanosleep(32);
+        w = *reinterpret_cast<const volatile unsigned long long*>(pw);
       }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u)
-        if (c0 + u < nch) o += w[c0 + u] * __uint_as_float(static_cast<uint32_t>(v[u]));
+      s.xs[u] = wt[g * nch + c] * __uint_as_float(static_cast<uint32_t>(w));
     }
-    if (ok) {
-      unsigned long long* dst = T.words + out + static_cast<long long>(h * G + g) * kHd + dd;
-      asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(dst), "l"(__float_as_uint(o) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
+    cbar();
+    for (int v = 0; v < 2; ++v) {
+      const int oi = threadIdx.x + v * kCT;
+      if (oi >= no) break;
+      for (int c = 0; c < nc; ++c) acc[v] += s.xs[oi * nc + c];
     }
+    cbar();   // xs is refilled by the next pass
+  }
+  for (int v = 0; v < 2; ++v) {
+    const int oi = threadIdx.x + v * kCT;
+    if (oi >= no || !ok) break;
+    const int g = (o0 + oi) / kHd, dd = (o0 + oi) % kHd;
+    unsigned long long* dst = T.words + out + static_cast<long long>(h * G + g) * kHd + dd;
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(dst), "l"(__float_as_uint(acc[v]) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
   }
 }
 
@@ -552,7 +554,9 @@ __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, 
 // words), normalises and rotates q and k, scores positions [32 c, min(32 c + 32, pos + 1))
 // against the cache (the new token's key from shared memory), and stores per query head
 // (m, l, o) as tagged words. The item of a head's last chunk also stores the new key and value
-// into the caches and then combines the head's chunks. Combining items come after every other
+// into the caches. Then the combine: when every item has a CTA of its own, each item combines
+// a slice of its head's outputs (waiting on the head's other items, all running); otherwise
+// the item of the head's last chunk combines all of them -- such items come after every other
 // item (chunk-major order) and a CTA takes its items in order, so a combine only ever waits on
 // items that run ahead of it.
 __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int qkv_out, int out,
@@ -669,15 +673,24 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
         asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(dst), "l"(__float_as_uint(o) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
       }
     }
-    if (c == nch - 1) {
-      // the new key and value into the caches, then the head's combine
-      if (ok)
-        for (int i = threadIdx.x; i < 2 * kHd; i += kCT) {
-          float* cache = i < kHd ? a.kc : a.vc;
-          cache[(static_cast<long long>(pos) * a.nkv + h) * kHd + (i % kHd)] = s.akv[i];
-        }
+    if (c == nch - 1 && ok)   // the new key and value into the caches
+      for (int i = threadIdx.x; i < 2 * kHd; i += kCT) {
+        float* cache = i < kHd ? a.kc : a.vc;
+        cache[(static_cast<long long>(pos) * a.nkv + h) * kHd + (i % kHd)] = s.akv[i];
+      }
+    int o0 = 0, o1 = 0;
+    if (a.nkv * nch <= static_cast<int>(gridDim.x)) {
+      // every item is in flight at once: each combines a slice of the head's outputs
+      const int per = (G * kHd + nch - 1) / nch;
+      o0 = min(c * per, G * kHd);
+      o1 = min(o0 + per, G * kHd);
+    } else if (c == nch - 1) {
+      // the head's last chunk (an item no other item waits behind) combines all of it
+      o1 = G * kHd;
+    }
+    if (o1 > o0) {
       cbar();
-      attn_combine(T, s, a, h, G, nch, part_out, out, tag, limit, ok);
+      attn_combine(T, s, a, h, G, nch, part_out, out, tag, limit, ok, o0, o1);
     }
     cbar();   // xs / aq / akv / asc / ascr are rewritten by the next item
   }
