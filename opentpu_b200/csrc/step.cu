@@ -465,20 +465,20 @@ __device__ __forceinline__ void head_norm_rope(float* v, bool has_g, float4 gn, 
   __syncwarp();
 }
 
-// The combine of KV head h's nch chunks for its G query heads (flash-decoding): with M the
-// largest chunk maximum, chunk c weighs e_c = exp(m_c - M) / L, L = sum_c exp(m_c - M) l_c, and
-// output o = g hd + dd (query head h G + g) is sum_c e_c o_c, in chunk order. This CTA writes
-// outputs [o0, o1) as tagged words at `out` (query head major): the O projection's input. The
+// The combine of the attention's nch chunks (flash-decoding), outputs [o0, o1) of the n_q hd
+// (o = hq hd + dd, query head hq): with M the largest of query head hq's chunk maxima, chunk c
+// weighs e_c = exp(m_c - M) / L, L = sum_c exp(m_c - M) l_c, and output o is sum_c e_c o_c, in
+// chunk order. Written as tagged words at `out`: the O projection's input. The whole CTA; the
 // chunks' words are awaited by their tags (bounded); every (output, chunk) word is one load of
 // one thread, all of a pass in flight at once, and the products meet in shared memory.
-__device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, int h, int G,
-                             int nch, int part_out, int out, uint32_t tag, uint32_t limit, bool ok,
-                             int o0, int o1) {
+__device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, int nch, int part_out,
+                             int out, uint32_t tag, uint32_t limit, bool ok, int o0, int o1) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float* wt = s.ascr;   // [G][nch] the chunks' weights
+  const int hq0 = o0 / kHd, nh = (o1 - 1) / kHd - hq0 + 1;   // the query heads touched (<= kCW)
+  float* wt = s.ascr;   // [nh][nch] the chunks' weights
   const long long stride = kHd + 2;
-  if (warp < G) {   // warp g: lane c takes chunks c, c + 32, ...
-    const unsigned long long* ph = T.words + part_out + static_cast<long long>(h * G + warp) * a.maxch * stride;
+  if (warp < nh) {   // warp w, query head hq0 + w: lane c takes chunks c, c + 32, ...
+    const unsigned long long* ph = T.words + part_out + static_cast<long long>(hq0 + warp) * a.maxch * stride;
     float M = -INFINITY;
     for (int c = lane; c < nch; c += 32) {
       unsigned long long w0, w1;
@@ -513,14 +513,14 @@ __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, 
   }
   cbar();
   const int no = o1 - o0;
-  const int per = max(1, kKcap / max(no, 1));   // chunks a pass (the products fit xs)
-  float acc[2] = {0.0f, 0.0f};                  // thread i's outputs o0 + i, o0 + i + kCT
+  const int per = max(1, kKcap / no);   // chunks a pass (the products fit xs)
+  float acc[2] = {0.0f, 0.0f};          // thread i's outputs o0 + i, o0 + i + kCT
   for (int c0 = 0; c0 < nch; c0 += per) {
     const int nc = min(per, nch - c0);
     for (int u = threadIdx.x; u < no * nc; u += kCT) {
-      const int oi = u / nc, c = c0 + u % nc;
-      const int g = (o0 + oi) / kHd, dd = (o0 + oi) % kHd;
-      const unsigned long long* pw = T.words + part_out + (static_cast<long long>(h * G + g) * a.maxch + c) * stride + 2 + dd;
+      const int o = o0 + u / nc, c = c0 + u % nc;
+      const int hq = o / kHd, dd = o % kHd;
+      const unsigned long long* pw = T.words + part_out + (static_cast<long long>(hq) * a.maxch + c) * stride + 2 + dd;
       unsigned long long w = *reinterpret_cast<const volatile unsigned long long*>(pw);
       for (uint32_t spin = 0; behind(w, tag); ++spin) {
         if (spin >= limit) {
@@ -530,7 +530,7 @@ __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, 
         if (spin >= 64) __nanosleep(32);
         w = *reinterpret_cast<const volatile unsigned long long*>(pw);
       }
-      s.xs[u] = wt[g * nch + c] * __uint_as_float(static_cast<uint32_t>(w));
+      s.xs[u] = wt[(hq - hq0) * nch + c] * __uint_as_float(static_cast<uint32_t>(w));
     }
     cbar();
     for (int v = 0; v < 2; ++v) {
@@ -543,8 +543,7 @@ __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, 
   for (int v = 0; v < 2; ++v) {
     const int oi = threadIdx.x + v * kCT;
     if (oi >= no || !ok) break;
-    const int g = (o0 + oi) / kHd, dd = (o0 + oi) % kHd;
-    unsigned long long* dst = T.words + out + static_cast<long long>(h * G + g) * kHd + dd;
+    unsigned long long* dst = T.words + out + o0 + oi;
     asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(dst), "l"(__float_as_uint(acc[v]) | (static_cast<unsigned long long>(tag) << 32)) : "memory");
   }
 }
@@ -554,11 +553,7 @@ __device__ void attn_combine(const StepHead& T, const SSmem& s, const SAttn& a, 
 // words), normalises and rotates q and k, scores positions [32 c, min(32 c + 32, pos + 1))
 // against the cache (the new token's key from shared memory), and stores per query head
 // (m, l, o) as tagged words. The item of a head's last chunk also stores the new key and value
-// into the caches. Then the combine: when every item has a CTA of its own, each item combines
-// a slice of its head's outputs (waiting on the head's other items, all running); otherwise
-// the item of the head's last chunk combines all of them -- such items come after every other
-// item (chunk-major order) and a CTA takes its items in order, so a combine only ever waits on
-// items that run ahead of it.
+// into the caches. Then every CTA combines a slice of the outputs.
 __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int qkv_out, int out,
                                        int pos, uint32_t expect, uint32_t tag, uint32_t limit,
                                        bool ok) {
@@ -678,21 +673,16 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
         float* cache = i < kHd ? a.kc : a.vc;
         cache[(static_cast<long long>(pos) * a.nkv + h) * kHd + (i % kHd)] = s.akv[i];
       }
-    int o0 = 0, o1 = 0;
-    if (a.nkv * nch <= static_cast<int>(gridDim.x)) {
-      // every item is in flight at once: each combines a slice of the head's outputs
-      const int per = (G * kHd + nch - 1) / nch;
-      o0 = min(c * per, G * kHd);
-      o1 = min(o0 + per, G * kHd);
-    } else if (c == nch - 1) {
-      // the head's last chunk (an item no other item waits behind) combines all of it
-      o1 = G * kHd;
-    }
-    if (o1 > o0) {
-      cbar();
-      attn_combine(T, s, a, h, G, nch, part_out, out, tag, limit, ok, o0, o1);
-    }
     cbar();   // xs / aq / akv / asc / ascr are rewritten by the next item
+  }
+  // the combine: every CTA, once its own items are done, takes a slice of the n_q hd outputs
+  // (so a combine never waits on an item queued behind it on the same CTA)
+  const int total = a.nq * kHd;
+  const int P = (total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  const int o0 = min(static_cast<int>(blockIdx.x) * P, total), o1 = min(o0 + P, total);
+  if (o1 > o0) {
+    attn_combine(T, s, a, nch, part_out, out, tag, limit, ok, o0, o1);
+    cbar();   // xs / asc / ascr are rewritten by the next stage
   }
 }
 
