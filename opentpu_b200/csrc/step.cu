@@ -569,16 +569,18 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
     const int c = item / a.nkv, h = item % a.nkv;
     const int j0 = c * kAttnChunk, j1 = min(j0 + kAttnChunk, pos + 1);
     // the chunk's cached keys and values (positions before pos) into shared memory, every copy
-    // in flight at once: keys at xs[0 ..), values at xs[kAttnChunk * hd ..); a row is 32 copies
+    // in flight at once: keys at xs[0 ..), values at xs[kAttnChunk * hd ..); warp w copies rows
+    // w, w + 8, .., lane l their bytes 16 l .. 16 l + 15
     {
       const int nold = min(j1, pos) - j0;
-      const uint32_t kv_s = smem_addr(s.xs);
-      for (int i = threadIdx.x; i < 64 * nold; i += kCT) {
-        const int rr = i >> 5, q4 = i & 31;
-        const int which = rr >= nold ? 1 : 0, r = rr - which * nold;
-        const float* src = (which ? a.vc : a.kc) + (static_cast<long long>(j0 + r) * a.nkv + h) * kHd + 4 * q4;
-        const uint32_t dst = kv_s + 16u * static_cast<uint32_t>((which * kAttnChunk + r) * (kHd / 4) + q4);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+      const uint32_t kv_s = smem_addr(s.xs) + 16u * static_cast<uint32_t>(lane);
+      const long long rstride = static_cast<long long>(a.nkv) * kHd;
+      const long long first = (static_cast<long long>(j0) * a.nkv + h) * kHd + 4 * lane;
+      for (int r = warp; r < nold; r += kCW) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(kv_s + static_cast<uint32_t>(r) * (kHd * 4)),
+                     "l"(a.kc + first + r * rstride) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(kv_s + static_cast<uint32_t>(kAttnChunk + r) * (kHd * 4)),
+                     "l"(a.vc + first + r * rstride) : "memory");
       }
     }
     // the head norm's gains and this position's rotation, ahead of their use
