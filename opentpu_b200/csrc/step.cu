@@ -12,29 +12,35 @@
 // copy over NVLink (the all-gather fused in). A projection that reads p's output reads those
 // words until every tag has arrived; no fence, flag or barrier stands between projections.
 //
-// Weight streaming. One producer warp a CTA walks the CTA's items -- an item is one 8-row block
+// Weight streaming. One producer warp a CTA walks the CTA's items -- an item is one 16-row tile
 // of a projection and up to 8 chunks of its K (128 bytes of a row a chunk), ONE 3-D tensor copy
-// of up to 8 KB with the 128-byte swizzle (plus, for 4-bit rows, a 2-D copy of the block's fp16
+// of up to 16 KB with the 128-byte swizzle (plus, for 4-bit rows, a 2-D copy of the tile's fp16
 // group scales) -- in the order the CTA computes them, across projection boundaries, into a ring
 // of shared-memory stages (full / empty mbarriers). Weights never depend on activations, so
 // while the CTA waits for projection p's input the weights of the next projections arrive. (One
 // tensor copy a 1 KB box, issued by the computing warps themselves, measured 0.3-0.5 us of issue
-// stall a copy on a B200: eight times fewer, larger copies from a warp that does nothing else.)
+// stall a copy on a B200: far fewer, larger copies from a warp that does nothing else.)
 //
-// Work split. A projection's 8-row blocks go in balanced ranges to the CTAs (one CTA an SM, all
-// resident: cooperative launch). Within a CTA either the 8 compute warps share each block's K
-// chunks (short projections; the warps' row totals meet in shared memory) or each warp takes
-// whole blocks (the LM head).
+// Work split. A projection's 16-row tiles go in balanced ranges to the CTAs (one CTA an SM, all
+// resident: cooperative launch). Within a CTA either the 8 compute warps share each tile's K
+// chunks (fewer than 8 tiles; the warps' row totals meet in shared memory) or each warp owns
+// whole tiles, int8 two at a time (the LM head).
 //
-// Arithmetic, int8 rows: the class path of gemv.cu -- a group's multiplier 2^(16 - da) depends on
-// the activation only, so A row c of an mma.sync m16n8k32 (s8) holds the bytes of the groups
-// whose offset is c, and a block's groups accumulate exactly in int32; per block one int64
-// scaling per class and a lane reduction. A row with a group of offset 16 (multiplier 1, no class
-// row) takes the general path for that projection: each group's int32 result times its
-// multiplier into int64. Epilogue (i2f(acc) * Sw) * (Sa * 2^-16), three flushed RNE products:
-// bit-identical to otq_qmm. 4-bit rows: x is staged once per projection as x'[k] = x[k] *
-// 2^(-4 (k mod 4)) with each group's sum of x, so a nibble masked in place under 2^23's
+// Arithmetic, int8 rows: a group's multiplier 2^(16 - d) depends on the activation only (its
+// QACT offset d). One mma.sync m16n8k32 (s8) a group and tile: A = the tile's 16 weight rows,
+// B = the group's activation bytes in column (d mod 8) of accumulator set d / 8, zero in the
+// other columns; each accumulator column is one offset class, exact in int32; a row's total is
+// sum over columns of D * 2^(16 - class) in int64 after two lane shuffles. Offsets above 16
+// drop out (the MM window). Epilogue (i2f(acc) * Sw) * (Sa * 2^-16), three flushed RNE
+// products: bit-identical to otq_qmm. 4-bit rows: x is staged once per projection as x'[k] =
+// x[k] * 2^(-4 (k mod 4)) with each group's sum of x, so a nibble masked in place under 2^23's
 // exponent, less 2^23, times x' is (code + 8) * x; a group adds s * (sum - 8 sum x).
+//
+// Decoder stages: a projection's input may be the RMSNorm of the residual row (each CTA keeps
+// the residual in shared memory and adds the named projection's output to it) or SwiGLU of an
+// earlier output; the GateUp projection may write SwiGLU itself (OTQ_EPI_SWIGLU); an attention
+// stage runs the new token's attention over the KV cache in chunks spread over the CTAs and
+// combines them (attn_stage).
 //
 // The last projection (the LM head) also yields the greedy token: with one GPU each CTA folds
 // its rows' (value, index) keys into one 64-bit atomicMax as it stores them; with several GPUs a
