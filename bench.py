@@ -465,7 +465,33 @@ def decode_4bit(args, world, rank, group, hbm, peak_kind):
     c4.release()
     del c4
     torch.cuda.synchronize()
+    out["mx_int4x"] = decode_mx_int4(args, world, rank, group)
     return out
+
+
+def decode_mx_int4(args, world, rank, group):
+    """The same step with the reference's own MX 4-bit format (int4x: a byte of offsets and 4-bit
+    multipliers a 128-element block, opentpu/quant.py:325-369) in the layers and the int8-row
+    head, exact QACT + MM, through the launch chain (one launch a projection; the step kernel
+    takes int8-row and int4-g32 only)."""
+    import torch
+    from opentpu_b200.decode import DecodeChain
+    shape = WL.QWEN3_0_6B
+    ch = DecodeChain(shape, fmt="int4", head_fmt="int8-row", world=world, rank=rank, group=group)
+    ch.capture()
+    ch.replay(args.warmup)
+    torch.cuda.synchronize()
+    n = max(10, args.steps)
+    ms = graph_ms(ch.graph, ch.stream, n, world)
+    res = {"metric": METRIC, "value": ch.weight_bytes / (ms * 1e-3) / 1e9, "unit": UNIT,
+           "ms_per_step": ms, "tok_s": 1e3 / ms, "steps": n,
+           "weights_bytes_per_step": ch.weight_bytes,
+           "launch": "one gemv launch a projection + the argmax, one CUDA graph a step",
+           "gpu_launches": ch.launches * n}
+    ch.release()
+    del ch
+    torch.cuda.synchronize()
+    return res
 
 
 def parity_vs_one_gpu(chain, world, rank):
