@@ -695,13 +695,17 @@ __device__ __noinline__ void attn_stage(const StepHead& T, const SAttn& a, int q
 }
 
 // kFeat: bit 0, the step has 4-bit projections; bit 1, decoder stages (norm / SwiGLU inputs, the
-// SwiGLU epilogue, attention). A step without them runs an instantiation without their code,
-// which measured ~11 % faster than the full kernel on the same projections.
-constexpr int kFeatG32 = 1, kFeatDecoder = 2;
+// SwiGLU epilogue, attention); bit 2, more than one GPU. A step without them runs an
+// instantiation without their code, which measured ~11 % faster than the full kernel on the same
+// projections.
+constexpr int kFeatG32 = 1, kFeatDecoder = 2, kFeatMulti = 4;
 
 template <int kFeat>
 __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restrict__ Tp) {
   constexpr bool kG32 = (kFeat & kFeatG32) != 0, kDec = (kFeat & kFeatDecoder) != 0;
+  // (the projection-only instantiations keep the several-GPU code: measured 2.7 % faster with it,
+  // a register-allocation effect; the decoder ones measured faster without it)
+  constexpr bool kMulti = (kFeat & kFeatMulti) != 0 || !kDec;
   __shared__ long long s_delta[kMaxWorld];
   __shared__ float s_Sa;
   __shared__ unsigned int s_seq;
@@ -774,7 +778,7 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
   const uint32_t mNS = 0xFFFFFFFFu / static_cast<uint32_t>(NS) + 1u;   // j / NS = umulhi(j, mNS), j < 2^16
   const uint32_t base = s_seq * kTagStride;
   const uint32_t limit = g_step_wait_limit;
-  const bool fused_amax = T.token != nullptr && T.world == 1;
+  const bool fused_amax = T.token != nullptr && (!kMulti || T.world == 1);
   unsigned long long best = 0;   // this thread's largest head key (fused argmax)
   bool ok = true;
   int item_base = 0;             // the CTA's items before projection p
@@ -848,7 +852,7 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
     const bool last = p == count - 1;
 
     auto store_row = [&](int row, float y) {
-      if (ok) st_word(yw + row, __float_as_uint(y) | (static_cast<unsigned long long>(tag) << 32), T.world, T.rank, s_delta);
+      if (ok) st_word(yw + row, __float_as_uint(y) | (static_cast<unsigned long long>(tag) << 32), kMulti ? T.world : 1, T.rank, s_delta);
       if (fused_amax && last) {
         const unsigned long long k = amax_key(y, static_cast<uint32_t>(T.rank * N + row));
         best = k > best ? k : best;
@@ -1151,7 +1155,7 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
 
   // ---- the greedy token
   if (T.token != nullptr) {
-    if (!fused_amax) {
+    if (kMulti && !fused_amax) {
       // several GPUs: the whole tagged logit row, every rank's part, once it has arrived
       const SInfo& h = s.info[count - 1];
       const unsigned long long* row = T.words + h.out;
@@ -1404,19 +1408,21 @@ int step_launch(const otq_step* st, const void* table, cudaStream_t stream) {
     if (q.fmt == OTQ_STEP_G32) feat |= kFeatG32;
     if (q.fmt == OTQ_STEP_ATTN || q.input != OTQ_IN_DEFAULT || q.epilogue != OTQ_EPI_NONE) feat |= kFeatDecoder;
   }
-  const void* const kernels[4] = {reinterpret_cast<const void*>(step_kernel<0>),
-                                  reinterpret_cast<const void*>(step_kernel<1>),
-                                  reinterpret_cast<const void*>(step_kernel<2>),
-                                  reinterpret_cast<const void*>(step_kernel<3>)};
+  if (st->world > 1) feat |= kFeatMulti;
+  const void* const kernels[8] = {
+      reinterpret_cast<const void*>(step_kernel<0>), reinterpret_cast<const void*>(step_kernel<1>),
+      reinterpret_cast<const void*>(step_kernel<2>), reinterpret_cast<const void*>(step_kernel<3>),
+      reinterpret_cast<const void*>(step_kernel<4>), reinterpret_cast<const void*>(step_kernel<5>),
+      reinterpret_cast<const void*>(step_kernel<6>), reinterpret_cast<const void*>(step_kernel<7>)};
   const void* kernel = kernels[feat];
-  static size_t configured[kMaxDevices][4] = {};
+  static size_t configured[kMaxDevices][8] = {};
   if (configured[dev][feat] < L.smem) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(L.smem)) != cudaSuccess)
       return kErrCuda;
     configured[dev][feat] = L.smem;
   }
-  static int occupancy[kMaxDevices][4] = {};
+  static int occupancy[kMaxDevices][8] = {};
   if (occupancy[dev][feat] == 0) {
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kTh, L.smem) != cudaSuccess)
