@@ -429,13 +429,13 @@ def decode_4bit(args, world, rank, group, hbm, peak_kind):
     from opentpu_b200.decode import DecodeStep
     shape = WL.QWEN3_0_6B
     c4 = DecodeStep(shape, fmt="int4-g32", head_fmt="int8-row", world=world, rank=rank,
-                    group=group)
+                    group=group, shard=args.shard)
     c4.capture()
     c4.replay(args.warmup)
     torch.cuda.synchronize()
     n4 = max(10, args.steps)
     ms4 = graph_ms(c4.graph, c4.stream, n4, world)
-    per_rank = c4.weight_bytes / world + sum(4 * K + 8 * N for _, N, K, _ in c4.plan)
+    per_rank = c4.rank_bytes + sum(4 * K + 8 * N for _, N, K, _ in c4.plan)
     ach = per_rank / (ms4 * 1e-3) / 1e9
     roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
             "traffic": read_traffic("step_kernel_qwen3_0_6b_int4g32.md", world),
@@ -922,6 +922,9 @@ def main():
     ap.add_argument("--no-config1", action="store_true")
     ap.add_argument("--no-phi4", action="store_true")
     ap.add_argument("--no-decoder", action="store_true")
+    ap.add_argument("--shard", choices=["head", "all"], default="head",
+                    help="with more than one GPU: shard only the LM head (every rank computes the "
+                         "layers whole) or every projection")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -948,7 +951,8 @@ def main():
     hbm, _, peak_kind = peaks()
     shape = WL.QWEN3_0_6B
     fmt = "int8-row"
-    chain = DecodeStep(shape, fmt=fmt, head_fmt=fmt, world=world, rank=rank, group=group)
+    chain = DecodeStep(shape, fmt=fmt, head_fmt=fmt, world=world, rank=rank, group=group,
+                       shard=args.shard)
     chain.capture()
     total_bytes = chain.weight_bytes
     chain.replay(args.warmup)
@@ -962,13 +966,13 @@ def main():
         e2e_ms, h2d, d2h, _ = closed_loop(chain, max(10, min(args.steps, 200)), world)
         # the dominant (only) kernel: the step's one launch; its bytes are this rank's weights
         # and scales plus every projection's input row and output words
-        per_rank = total_bytes / world + sum(4 * K + 8 * N for _, N, K, _ in chain.plan)
+        per_rank = chain.rank_bytes + sum(4 * K + 8 * N for _, N, K, _ in chain.plan)
         ach = per_rank / (ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
                 "frac": ach / hbm,
                 "traffic": read_traffic("step_kernel_qwen3_0_6b_int8row.md", world),
                 "kernel": "step_kernel (the whole decode step, 113 projections + greedy token, "
-                          "one persistent launch" + (f", this rank's 1/{world} row shard"
+                          "one persistent launch" + (f", this rank's rows ({args.shard} sharded)"
                                                      if world > 1 else "") + ")",
                 "bytes_per_launch": per_rank, "us_per_launch": ms * 1e3,
                 "peak_kind": f"{peak_kind} (copy)"}
@@ -1001,11 +1005,11 @@ def main():
                                    "(QKV, O, GateUp, Down) + 151936x1024 LM head + greedy "
                                    "token, M=1",
                        "weights_bytes_per_step": total_bytes, "format": fmt,
-                       "parallelism": f"row-shard x{world}" + (" + all-gather per projection "
-                                                              "fused into the step kernel (tagged "
-                                                              "8-byte words stored to every rank "
-                                                              "over NVLink)"
-                                                              if world > 1 else ""),
+                       "parallelism": (f"row-shard x{world} of " + ("the LM head (every rank "
+                                       "computes the layers' projections whole)" if args.shard
+                                       == "head" else "every projection") + ", the sharded "
+                                       "outputs' words stored to every rank over NVLink inside "
+                                       "the step kernel") if world > 1 else "one GPU",
                        "l2": "weights 598 MB > 126 MB L2 (no flush needed)",
                        "launch": "one persistent launch a step (otq_decode_step), replayed "
                                  "from a CUDA graph"},

@@ -268,6 +268,10 @@ typedef struct otq_step_proj {
   float* vcache;
   int n_q, n_kv, head_dim;   /* head_dim 128, n_q / n_kv at most 4 */
   int epilogue;          /* OTQ_EPI_* (projections; not the last stage) */
+  int replicated;        /* world > 1: 0, the rows are this rank's contiguous shard of the
+                            projection (its output words go to every rank); 1, every rank holds
+                            all N rows and computes the projection alone (its output stays on
+                            this GPU: no NVLink traffic) */
 } otq_step_proj;
 
 #define OTQ_STEP_MAX 160

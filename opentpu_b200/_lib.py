@@ -38,7 +38,8 @@ class StepProj(ctypes.Structure):
                 ("N", c_int64), ("K", c_int64), ("src", c_int), ("fmt", c_int),
                 ("input", c_int), ("res", c_int), ("gamma", c_void_p), ("q_gain", c_void_p),
                 ("k_gain", c_void_p), ("kcache", c_void_p), ("vcache", c_void_p),
-                ("n_q", c_int), ("n_kv", c_int), ("head_dim", c_int), ("epilogue", c_int)]
+                ("n_q", c_int), ("n_kv", c_int), ("head_dim", c_int), ("epilogue", c_int),
+                ("replicated", c_int)]
 
 
 STEP_RSC, STEP_G32, STEP_ATTN = 0, 1, 2

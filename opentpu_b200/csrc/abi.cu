@@ -456,7 +456,7 @@ int check_step(const otq_step* s) {
   bool plain_in = false, attn = false;
   auto full = [&](int i) {   // a projection's output row
     const otq_step_proj& q = s->projs[i];
-    return (q.epilogue == OTQ_EPI_SWIGLU ? q.N / 2 : q.N) * s->world;
+    return (q.epilogue == OTQ_EPI_SWIGLU ? q.N / 2 : q.N) * (q.replicated ? 1 : s->world);
   };
   auto is_proj = [&](int j, int i) {
     return j >= 0 && j < i && s->projs[j].fmt != OTQ_STEP_ATTN;
@@ -478,6 +478,7 @@ int check_step(const otq_step* s) {
     }
     const bool g32 = p.fmt == OTQ_STEP_G32;
     if (p.fmt != OTQ_STEP_RSC && !g32) return kErrFormat;
+    if (p.replicated != 0 && p.replicated != 1) return kErrArg;
     if (p.epilogue != OTQ_EPI_NONE &&
         (p.epilogue != OTQ_EPI_SWIGLU || p.N % 16 || i == s->count - 1))
       return kErrArg;

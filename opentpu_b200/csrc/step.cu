@@ -109,7 +109,8 @@ struct SInfo {            // one stage, as the kernel reads it (shared memory)
   int input;              // OTQ_IN_*
   int res;                // OTQ_IN_NORM: -2 (start from x0) or the projection added first
   int epi;                // OTQ_EPI_*
-  int pad[2];
+  int rep;                // world > 1 and every rank computes all rows (no NVLink stores)
+  int pad[1];
 };
 static_assert(sizeof(SInfo) == 80, "SInfo is 80 bytes");
 
@@ -778,7 +779,8 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
   const uint32_t mNS = 0xFFFFFFFFu / static_cast<uint32_t>(NS) + 1u;   // j / NS = umulhi(j, mNS), j < 2^16
   const uint32_t base = s_seq * kTagStride;
   const uint32_t limit = g_step_wait_limit;
-  const bool fused_amax = T.token != nullptr && (!kMulti || T.world == 1);
+  // the greedy token folded into the head's epilogue when its whole row is computed here
+  const bool fused_amax = T.token != nullptr && (!kMulti || T.world == 1 || s.info[count - 1].rep);
   unsigned long long best = 0;   // this thread's largest head key (fused argmax)
   bool ok = true;
   int item_base = 0;             // the CTA's items before projection p
@@ -847,14 +849,16 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
     // OTQ_EPI_SWIGLU: rows 16j .. 16j + 7 gate, 16j + 8 .. 16j + 15 up; output word 8j + r is
     // silu(gate) * up of tile rows r and r + 8 (the formula of the SwiGLU prologue)
     const bool swi = kDec && d.epi == kEpiSwiglu;
-    unsigned long long* const yw = T.words + d.out + static_cast<long long>(T.rank) * (swi ? N / 2 : N);
+    const bool rep = kMulti && d.rep;   // every rank computes all rows: stores stay here
+    const int rank_off = rep ? 0 : T.rank * (swi ? N / 2 : N);
+    unsigned long long* const yw = T.words + d.out + rank_off;
     auto swiglu = [](float gv, float uv) { return (gv / (1.0f + expf(-gv))) * uv; };
     const bool last = p == count - 1;
 
     auto store_row = [&](int row, float y) {
-      if (ok) st_word(yw + row, __float_as_uint(y) | (static_cast<unsigned long long>(tag) << 32), kMulti ? T.world : 1, T.rank, s_delta);
+      if (ok) st_word(yw + row, __float_as_uint(y) | (static_cast<unsigned long long>(tag) << 32), (kMulti && !rep) ? T.world : 1, T.rank, s_delta);
       if (fused_amax && last) {
-        const unsigned long long k = amax_key(y, static_cast<uint32_t>(T.rank * N + row));
+        const unsigned long long k = amax_key(y, static_cast<uint32_t>(rank_off + row));
         best = k > best ? k : best;
       }
     };
@@ -1303,7 +1307,8 @@ int step_layout(const otq_step_proj* pr, int count, int world, int64_t* offsets,
     if (offsets) offsets[i] = off;
     // an attention stage's partial results stay on each rank (every rank computes them)
     const int64_t n = pr[i].fmt == OTQ_STEP_ATTN ? pr[i].N
-                      : (pr[i].epilogue == OTQ_EPI_SWIGLU ? pr[i].N / 2 : pr[i].N) * world;
+                      : (pr[i].epilogue == OTQ_EPI_SWIGLU ? pr[i].N / 2 : pr[i].N) *
+                            (pr[i].replicated ? 1 : world);
     off += ((n + 1) / 2) * 2;
   }
   *total = off;
@@ -1366,7 +1371,8 @@ int step_prepare(const otq_step* st, void* table) {
     d.gamma = q.gamma;
     d.out = static_cast<int>(offs[i]);
     d.epi = q.epilogue;
-    d.nfull = static_cast<int>((q.epilogue == OTQ_EPI_SWIGLU ? q.N / 2 : q.N) * st->world);
+    d.rep = st->world > 1 && q.replicated ? 1 : 0;
+    d.nfull = static_cast<int>((q.epilogue == OTQ_EPI_SWIGLU ? q.N / 2 : q.N) * (d.rep ? 1 : st->world));
   }
   T.count = count;
   T.world = st->world;

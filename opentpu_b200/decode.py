@@ -71,22 +71,23 @@ def step_plan(shape: DecoderShape, fmt: str, head_fmt: str):
     return plan
 
 
-def seeded_weights(plan, seed: int, world: int, rank: int, std: float = 0.02):
-    """The step's packed weights (this rank's row shard of each) and first-input rows, drawn
-    from one generator in plan order: every world size and rank sees the same matrices.
-    Returns (weights, inputs {K: [1, K]}, weight bytes of the whole step over all ranks)."""
+def seeded_weights(plan, seed: int, world: int, rank: int, std: float = 0.02, whole=()):
+    """The step's packed weights (this rank's row shard of each; all rows of the projections
+    whose indices are in `whole`) and first-input rows, drawn from one generator in plan order:
+    every world size and rank sees the same matrices. Returns (weights, inputs {K: [1, K]},
+    the step's weight bytes -- each projection once)."""
     gen = torch.Generator(device="cuda").manual_seed(seed)
     weights, inputs, nbytes = [], {}, 0
-    for name, N, K, f in plan:
+    for i, (name, N, K, f) in enumerate(plan):
         try:
-            n0, n1 = shard_rows(N, world, rank)
+            n0, n1 = (0, N) if i in whole else shard_rows(N, world, rank)
         except ValueError as e:
             raise ValueError(f"{name}: {e}") from None
         W = torch.randn((N, K), generator=gen, device="cuda")[n0:n1] * std
         w = linear.PackedWeight.from_float(W, f)
         del W
         weights.append(w)
-        nbytes += w.stream_bytes * world
+        nbytes += w.stream_bytes * (1 if i in whole else world)
         if K not in inputs:
             inputs[K] = torch.randn((1, K), generator=gen, device="cuda")
     return weights, inputs, nbytes
@@ -100,19 +101,28 @@ class DecodeStep:
     int8-row (bit-identical to DecodeChain) or int4-g32 (weight-only, fp32 sums in another
     order than otq_linear_g32's); the head in int8-row. With world > 1 the rows are sharded and
     every output word is stored into every rank's copy of a symmetric buffer over NVLink (the
-    all-gather fused in): bit-identical to one GPU."""
+    all-gather fused in): bit-identical to one GPU. shard="head" shards only the LM head and
+    has every rank compute the layers' projections whole (their outputs never cross NVLink:
+    at this model size a projection's NVLink hand-off costs more than its rows take to stream).
+    """
 
     def __init__(self, shape: DecoderShape, fmt: str = "int8-row", head_fmt: str = "int8-row",
-                 seed: int = 0, world: int = 1, rank: int = 0, group=None):
+                 seed: int = 0, world: int = 1, rank: int = 0, group=None, shard: str = "all"):
         import ctypes
         from . import _lib as L
         if fmt not in ("int8-row", "int4-g32") or head_fmt != "int8-row":
             raise ValueError("the persistent decode step takes int8-row or int4-g32 layers and "
                              "an int8-row head")
+        if shard not in ("all", "head"):
+            raise ValueError("shard is 'all' or 'head'")
         self.shape, self.world, self.rank, self.group = shape, world, rank, group
         self.plan = step_plan(shape, fmt, head_fmt)
-        self.weights, self.inputs, self.weight_bytes = seeded_weights(self.plan, seed, world, rank)
         n = len(self.plan)
+        whole = set(range(n - 1)) if (shard == "head" and world > 1) else set()
+        self.weights, self.inputs, self.weight_bytes = seeded_weights(self.plan, seed, world, rank,
+                                                                      whole=whole)
+        # the bytes this rank streams a step
+        self.rank_bytes = sum(w.stream_bytes for w in self.weights)
         self.projs = (L.StepProj * n)()
         for i, w in enumerate(self.weights):
             p = self.projs[i]
@@ -121,6 +131,7 @@ class DecodeStep:
             p.srs = w.srows.stride(0) * w.srows.element_size()
             p.N, p.K, p.src = w.N, w.K, i - 1
             p.fmt = L.STEP_G32 if w.fmt == "int4-g32" else L.STEP_RSC
+            p.replicated = 1 if i in whole else 0
         offs = (ctypes.c_int64 * n)()
         total = ctypes.c_int64(0)
         L.call("otq_step_layout", ctypes.addressof(self.projs), n, world, ctypes.addressof(offs),

@@ -57,6 +57,9 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
+CASES = [("int8-row", "all"), ("int4-g32", "all"), ("int8-row", "head"), ("int4-g32", "head")]
+
+
 def _rank_step(rank, world, port, q):
     """One rank of the one-launch decode step (DecodeStep) on `world` GPUs: int8-row and 4-bit
     layers, several graph replays; rank 0 compares with the unsharded step on one GPU."""
@@ -72,13 +75,13 @@ def _rank_step(rank, world, port, q):
         from opentpu_b200 import workloads as WL
         from opentpu_b200.decode import DecodeStep
         res = {}
-        for fmt in ("int8-row", "int4-g32"):
-            st = DecodeStep(WL.TINY, fmt=fmt, world=world, rank=rank, seed=7)
+        for fmt, shard in CASES:
+            st = DecodeStep(WL.TINY, fmt=fmt, world=world, rank=rank, seed=7, shard=shard)
             st.capture()
             st.replay(4)
             torch.cuda.synchronize()
-            res[fmt] = ([st.full_out(i).cpu().clone() for i in range(len(st.plan))],
-                        int(st.token[0]))
+            res[(fmt, shard)] = ([st.full_out(i).cpu().clone() for i in range(len(st.plan))],
+                                 int(st.token[0]))
             dist.barrier()
             st.release()
         if rank == 0:
@@ -103,9 +106,10 @@ def _rank_step(rank, world, port, q):
 
 def test_step_on_two_gpus_equals_one_gpu():
     """The one-launch decode step row-sharded over 2 GPUs, the all-gather fused into the kernel
-    (tagged words stored into both ranks' copies over NVLink): every projection's output row and
-    the greedy token bit-identical to the unsharded step on one GPU (int8-row layers: exact;
-    int4-g32 layers: each output row computed by one rank in the same order as on one GPU)."""
+    (tagged words stored into both ranks' copies over NVLink), or only its head sharded (every
+    rank computes the layers whole): every projection's output row and the greedy token
+    bit-identical to the unsharded step on one GPU (int8-row layers: exact; int4-g32 layers:
+    each output row computed by one rank in the same order as on one GPU)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -121,8 +125,8 @@ def test_step_on_two_gpus_equals_one_gpu():
         assert p.exitcode == 0
     res = [r for _, r in got if r is not None][0]
     assert res["status"] == 0
-    for fmt in ("int8-row", "int4-g32"):
-        outs, tok = res[fmt]
+    for fmt, shard in CASES:
+        outs, tok = res[(fmt, shard)]
         one, tok1 = res["one_" + fmt]
         assert tok == tok1
         for a, b in zip(outs, one):
