@@ -364,6 +364,53 @@ OTQ_API int otq_gemm_w8a16(int flags, const uint8_t* rows, int64_t rs, const uin
  * each other. No counterpart in the reference (its projections are separate programs). */
 OTQ_API int otq_gemm_w8a16_group(const otq_gemm_proj* projs, int count, void* stream);
 
+/* ------------------------------------------------------------------ exact W8A8 MM on tcgen05 */
+
+/* Bytes of the activation planes buffer for M rows of K (M >= 0, K > 0 and K % 32 == 0), or a
+ * negative OTQ_ERR_*: about 3 M K. */
+OTQ_API int64_t otq_qact_planes_bytes(int64_t M, int64_t K);
+
+/* QACT of x [M, K] fp32 (ldx elements a row; the reference's quantize_mx with an offset per 32
+ * elements, opentpu/fp32.py:321-343; row_mode = QACT ROW) into `planes` (device memory, 16-byte
+ * aligned, at least otq_qact_planes_bytes(M, K) bytes), the form otq_gemm_w8a8_group reads: a
+ * row's QACT scale, its largest kept offset D, and its bytes times 2^(D - d) split into up to
+ * three signed base-256 int8 planes. K % 32 == 0, K <= 65536. No counterpart in the reference
+ * (its QACT writes bytes and offsets; this is the same quantization laid out for the tensor
+ * cores). */
+OTQ_API int otq_qact_planes(const float* x, int64_t ldx, int64_t M, int64_t K, int row_mode,
+                            void* planes, int64_t bytes, void* stream);
+
+/* One projection of otq_gemm_w8a8_group. */
+typedef struct otq_gemm8_proj {
+  int flags;             /* OTQ_MM_RSC (Sw = the first fp32 word of each scale row) or
+                            OTQ_MM_UNIT (Sw = 1), either one | OTQ_MM_ACC */
+  const uint8_t* rows;   /* int8 weight rows [N][rs] (16-byte aligned, rs a multiple of 16) */
+  int64_t rs;
+  const uint8_t* srows;  /* scale rows [N][srs] (4-byte aligned), or NULL with OTQ_MM_UNIT */
+  int64_t srs;
+  int64_t N;
+  int64_t K;             /* K % 32 == 0, K <= 65536 */
+  const void* planes;    /* otq_qact_planes of the activations [M][K] */
+  int64_t M;
+  float* y;              /* fp32 output [M][ldy] (4-byte aligned) */
+  int64_t ldy;
+} otq_gemm8_proj;
+
+/* MM of int8-row weights (RSC or UNIT) and QACT activations on the tcgen05 tensor cores
+ * (kind::i8), up to 8 independent projections in one launch: y = MM(QACT(x), rows), the same
+ * bits as otq_qmm(OTQ_FMT_INT8, flags) -- the reference's exact integer accumulation
+ * (opentpu/isasim.py:749-910) and fp32 epilogue, for any M (prefill; batched decode). ACC:
+ * y = fadd(y, MM). Outputs must not overlap the inputs or each other. M is at most
+ * 32768 tokens a projection. */
+OTQ_API int otq_gemm_w8a8_group(const otq_gemm8_proj* projs, int count, void* stream);
+
+/* otq_qact_planes then otq_gemm_w8a8_group of one projection: otq_qmm(OTQ_FMT_INT8, flags, ...,
+ * k0 = 0, alpha = NULL) on the tensor cores, with the caller's planes buffer as scratch. */
+OTQ_API int otq_qmm_tc(int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows,
+                       int64_t srs, int64_t N, int64_t K, const float* x, int64_t ldx,
+                       int row_mode, int64_t M, void* planes, int64_t planes_bytes, float* y,
+                       int64_t ldy, void* stream);
+
 /* ------------------------------------------------------------------ greedy token */
 
 /* The index of the first maximum of x[0], x[stride], ..., x[(n - 1) * stride] (stride 2 reads

@@ -64,6 +64,13 @@ class GemmProj(ctypes.Structure):
                 ("ldx", c_int64), ("M", c_int64), ("y", c_void_p), ("ldy", c_int64)]
 
 
+class Gemm8Proj(ctypes.Structure):
+    """struct otq_gemm8_proj of include/otq.h: one projection of otq_gemm_w8a8_group."""
+    _fields_ = [("flags", c_int), ("rows", c_void_p), ("rs", c_int64), ("srows", c_void_p),
+                ("srs", c_int64), ("N", c_int64), ("K", c_int64), ("planes", c_void_p),
+                ("M", c_int64), ("y", c_void_p), ("ldy", c_int64)]
+
+
 # name -> (restype, argtypes); every pointer is passed as an integer address
 _P, _I, _L = c_void_p, c_int, c_int64
 SIGNATURES = {
@@ -82,6 +89,10 @@ SIGNATURES = {
     "otq_qmm_peer": (_I, [_I, _I, _P, _L, _P, _L, _I, _L, _L, _P, _L, _I, _P, _P, _I, _P]),
     "otq_gemm_w8a16": (_I, [_I, _P, _L, _P, _L, _L, _L, _P, _L, _L, _P, _L, _P]),
     "otq_gemm_w8a16_group": (_I, [_P, _I, _P]),
+    "otq_qact_planes_bytes": (_L, [_L, _L]),
+    "otq_qact_planes": (_I, [_P, _L, _L, _L, _I, _P, _L, _P]),
+    "otq_gemm_w8a8_group": (_I, [_P, _I, _P]),
+    "otq_qmm_tc": (_I, [_I, _P, _L, _P, _L, _L, _L, _P, _L, _I, _L, _P, _L, _P, _L, _P]),
     "otq_status_word": (_I, [_P, _I]),
     "otq_set_wait_limit": (_I, [ctypes.c_uint32]),
     "otq_step_layout": (_I, [_P, _I, _I, _P, _P]),

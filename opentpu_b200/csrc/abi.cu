@@ -388,6 +388,62 @@ int otq_gemm_w8a16(int flags, const uint8_t* rows, int64_t rs, const uint8_t* sr
   return otq_gemm_w8a16_group(&p, 1, stream);
 }
 
+int64_t otq_qact_planes_bytes(int64_t M, int64_t K) {
+  if (M < 0 || K <= 0 || K % 32 || K > 65536 || M > (int64_t{1} << 30)) return kErrArg;
+  return qact_planes_bytes(M, K);
+}
+
+int otq_qact_planes(const float* x, int64_t ldx, int64_t M, int64_t K, int row_mode,
+                    void* planes, int64_t bytes, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  const int64_t need = otq_qact_planes_bytes(M, K);
+  if (need < 0) return static_cast<int>(need);
+  if (x == nullptr || planes == nullptr || ldx < K || ldx >= kStrideLimit || bytes < need ||
+      (row_mode != 0 && row_mode != 1))
+    return kErrArg;
+  if (!aligned(x, 4) || !aligned(planes, 16)) return kErrAlign;
+  return finish(qact_planes_launch(x, ldx, M, K, row_mode, planes, static_cast<cudaStream_t>(stream)));
+}
+
+int otq_gemm_w8a8_group(const otq_gemm8_proj* projs, int count, void* stream) {
+  int st = device_ok();
+  if (st) return st;
+  if (projs == nullptr || count < 0 || count > kW8A8MaxGroup) return kErrArg;
+  W8A8Proj w[kW8A8MaxGroup];
+  int n = 0;
+  for (int i = 0; i < count; ++i) {
+    const otq_gemm8_proj& p = projs[i];
+    if (p.flags & ~(kMmUnit | kMmRsc | kMmAcc)) return kErrArg;
+    if (!(p.flags & (kMmUnit | kMmRsc))) return kErrFormat;   // int8x block offsets: otq_qmm
+    if (p.N <= 0 || p.M < 0 || p.M > 32768 || p.N > 0x7FFFFFFF || otq_qact_planes_bytes(p.M, p.K) < 0)
+      return kErrArg;
+    if (p.rows == nullptr || p.planes == nullptr || p.y == nullptr) return kErrArg;
+    if (!(p.flags & kMmUnit) && p.srows == nullptr) return kErrArg;
+    if (p.rs < p.K || p.ldy < p.N || p.rs >= kStrideLimit || p.ldy >= kStrideLimit) return kErrArg;
+    if (!aligned(p.rows, 16) || p.rs % 16 || !aligned(p.planes, 16) || !aligned(p.y, 4))
+      return kErrAlign;
+    if (!(p.flags & kMmUnit) && (!aligned(p.srows, 4) || p.srs % 4 || p.srs < 4)) return kErrAlign;
+    if (p.M == 0) continue;
+    w[n++] = W8A8Proj{p.flags, p.rows, p.rs, p.srows, p.srs, p.N, p.K, p.planes, p.M, p.y, p.ldy};
+  }
+  if (n == 0) return kOk;
+  return finish(w8a8_launch(w, n, static_cast<cudaStream_t>(stream)));
+}
+
+int otq_qmm_tc(int flags, const uint8_t* rows, int64_t rs, const uint8_t* srows, int64_t srs,
+               int64_t N, int64_t K, const float* x, int64_t ldx, int row_mode, int64_t M,
+               void* planes, int64_t planes_bytes, float* y, int64_t ldy, void* stream) {
+  const otq_gemm8_proj p{flags, rows, rs, srows, srs, N, K, planes, M, y, ldy};
+  // the projection's checks first: nothing is launched for a call that would fail
+  if (flags & ~(kMmUnit | kMmRsc | kMmAcc)) return kErrArg;
+  if (!(flags & (kMmUnit | kMmRsc))) return kErrFormat;
+  if (rows == nullptr || y == nullptr || N <= 0 || M > 32768 || rs < K || ldy < N) return kErrArg;
+  int st = otq_qact_planes(x, ldx, M, K, row_mode, planes, planes_bytes, stream);
+  if (st) return st;
+  return otq_gemm_w8a8_group(&p, 1, stream);
+}
+
 int otq_argmax(const float* x, int64_t n, int64_t stride, int64_t* out, void* stream) {
   int st = device_ok();
   if (st) return st;

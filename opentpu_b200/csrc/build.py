@@ -11,8 +11,8 @@ CSRC = Path(__file__).resolve().parent
 PKG = CSRC.parent
 ROOT = PKG.parent
 LIB = PKG / "libotq.so"
-SOURCES = ["abi.cu", "quantize.cu", "quantize4.cu", "gemv.cu", "g32.cu", "prefill.cu", "argmax.cu",
-           "step.cu"]
+SOURCES = ["abi.cu", "quantize.cu", "quantize4.cu", "gemv.cu", "g32.cu", "prefill.cu", "w8a8.cu",
+           "argmax.cu", "step.cu"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-ftz=false", "-prec-div=true", "-prec-sqrt=true", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr"]

@@ -76,6 +76,24 @@ struct W8A16Proj {
 };
 constexpr int kW8A16MaxGroup = 8;
 
+// One projection of the exact W8A8 tensor-core MM (w8a8.cu), checked by the caller: rows int8
+// [N, K] (rs bytes, 16-byte aligned), Sw the first fp32 word of each scale row (srows unused
+// with OTQ_MM_UNIT), planes the buffer qact_planes_launch wrote for M rows of K, y fp32 [M, N]
+// (ldy floats).
+struct W8A8Proj {
+  int flags;
+  const uint8_t* rows;
+  int64_t rs;
+  const uint8_t* srows;
+  int64_t srs;
+  int64_t N, K;
+  const void* planes;
+  int64_t M;
+  float* y;
+  int64_t ldy;
+};
+constexpr int kW8A8MaxGroup = 8;
+
 int sm_count(int dev);
 // argmax.cu: acc = two words (key accumulator, CTA count) zeroed on the stream here; the index
 // goes to *index (acc itself for otq_argmax)
@@ -85,6 +103,11 @@ int argmax_launch(const float* x, int64_t n, int64_t stride, int64_t* acc, int64
 int argmax_noalloc_launch(const float* x, int64_t n, int64_t stride, int64_t* index,
                           cudaStream_t stream);
 int w8a16_launch(const W8A16Proj* projs, int count, cudaStream_t stream);   // prefill.cu
+// w8a8.cu: the planes buffer (bytes for M rows of K; QACT into it) and the tensor-core MM
+int64_t qact_planes_bytes(int64_t M, int64_t K);
+int qact_planes_launch(const float* x, int64_t ldx, int64_t M, int64_t K, int row_mode,
+                       void* planes, cudaStream_t stream);
+int w8a8_launch(const W8A8Proj* projs, int count, cudaStream_t stream);
 int mm_launch(const MMParams& p, cudaStream_t stream, bool pdl);    // gemv.cu
 int chain_launch(const otq_proj* projs, int count, cudaStream_t stream);
 int chain_reset();   // the grid barrier's count back to zero

@@ -44,6 +44,7 @@
 #include <vector>
 
 #include "mm_common.cuh"
+#include "tcgen05.cuh"
 #include "otq_internal.h"
 
 namespace otq {
@@ -162,23 +163,6 @@ __device__ __forceinline__ Span my_units(const GroupArgs& g) {
   return Span{static_cast<int>(blockIdx.x), g.nunits, static_cast<int>(gridDim.x)};
 }
 
-__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-
-// UMMA shared-memory descriptor of a K-major tile in the 128-byte swizzle layout: rows 128 bytes
-// apart, 8-row groups 1024 bytes apart (leading offset 16 bytes, unused by this layout; stride
-// offset 1024 bytes; version 1; layout type 2 = 128-byte swizzle). A K step of 16 bf16 advances
-// the start address by 32 bytes inside the swizzle atom.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
-  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1u) << 16) |
-         (static_cast<uint64_t>(1024u >> 4) << 32) | (static_cast<uint64_t>(1u) << 46) |
-         (static_cast<uint64_t>(2u) << 61);
-}
-
 // Instruction descriptor of kind::f16: fp32 accumulator (bits 4-5 = 1), bf16 A and B (bits 7-9,
 // 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24.
 constexpr uint32_t idesc_bf16(int M, int N) {
@@ -193,12 +177,6 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, 
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
       "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
       : "memory");
-}
-
-// The barrier's next phase completes when every MMA this thread issued so far has completed.
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
 }
 
 // 16 consecutive fp32 columns of this warp's 32 tensor-memory lanes (one lane a thread); the
@@ -248,12 +226,6 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
 __device__ __forceinline__ void epi_sync() {   // the epilogue warps
   asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
 }
@@ -585,32 +557,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_kernel(const __grid_constan
   }
 }
 
-using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
-
-EncodeFn encoder() {
-  static EncodeFn fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeFn>(p);
-  }
-  return fn;
-}
-
-bool encode_2d(EncodeFn enc, CUtensorMap* map, CUtensorMapDataType type, const void* base,
-               int64_t inner, int64_t outer, int64_t stride_bytes, CUtensorMapSwizzle swizzle,
-               int box_inner = kBK, int box_outer = 256) {
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride_bytes)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
-  const cuuint32_t estr[2] = {1, 1};
-  return enc(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 }  // namespace
 
 namespace {
@@ -777,9 +723,9 @@ int w8a16_launch(const W8A16Proj* projs, int count, cudaStream_t stream) {
     const W8A16Proj& w = projs[i];
     GProj& P = g.proj[i];
     if (!encode_2d(enc, &P.amap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w.x, w.K, w.M, w.ldx * 2,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+                   CU_TENSOR_MAP_SWIZZLE_128B, kBK, 256) ||
         !encode_2d(enc, &P.bmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.rows, w.K, w.N, w.rs,
-                   CU_TENSOR_MAP_SWIZZLE_NONE))
+                   CU_TENSOR_MAP_SWIZZLE_NONE, kBK, 256))
       return kErrArg;
     P.srows = w.srows;
     P.y = w.y;

@@ -328,6 +328,76 @@ def gemm_w8a16_group(items) -> list:
     return outs
 
 
+class QActPlanes:
+    """QACT'd activations laid out for the tensor-core MM (otq_qact_planes): a device buffer
+    for up to `rows` rows of K; `fill(x)` quantizes x [M, K] (M <= rows) into it. One buffer
+    serves every projection that reads the same x (a layer's q / k / v, gate / up)."""
+
+    def __init__(self, rows: int, K: int, device=None):
+        n = L.load().otq_qact_planes_bytes(int(rows), int(K))
+        if n < 0:
+            raise ValueError(f"planes of {rows} x {K}: {L.load().otq_status_string(n).decode()}")
+        self.buf = torch.empty(n, dtype=torch.uint8, device=device or "cuda")
+        self.K, self.M = int(K), 0
+
+    def fill(self, x: torch.Tensor, row_mode: bool = False) -> "QActPlanes":
+        x2, _ = _as_rows(x, self.K)
+        L.call("otq_qact_planes", x2.data_ptr(), x2.stride(0), x2.shape[0], self.K,
+               int(row_mode), self.buf.data_ptr(), self.buf.numel(), _stream())
+        self.M = x2.shape[0]
+        return self
+
+
+def _tc_weight(w: PackedWeight):
+    if w.fmt != "int8-row" and not (w.fmt == "int8" and w.srows is None):
+        raise ValueError("the tensor-core MM takes int8-row weights (or UNIT int8)")
+
+
+def qlinear_tc(x: torch.Tensor, w: PackedWeight, *, out=None, acc: bool = False,
+               row_mode: bool = False, planes: QActPlanes | None = None) -> torch.Tensor:
+    """y = MM(QACT(x), w) on the tcgen05 tensor cores (kind::i8, otq_qmm_tc): the same bits as
+    `qlinear` for int8-row (or UNIT int8) weights, at any M (prefill, batched decode). x [M, K]
+    or [K] fp32; planes: a QActPlanes of at least M rows to reuse as the scratch buffer."""
+    _tc_weight(w)
+    x2, vec = _as_rows(x, w.K)
+    M = x2.shape[0]
+    y = _out(out, M, w.N, x.device, acc)
+    if planes is None:
+        planes = QActPlanes(M, w.K, x.device)
+    elif planes.K != w.K:
+        raise ValueError(f"planes hold K = {planes.K}, the weight has K = {w.K}")
+    L.call("otq_qmm_tc", w.flags | (L.MM_ACC if acc else 0), w.rows.data_ptr(), w.rows.stride(0),
+           _ptr(w.srows), 0 if w.srows is None else w.srows.stride(0), w.N, w.K, x2.data_ptr(),
+           x2.stride(0), int(row_mode), M, planes.buf.data_ptr(), planes.buf.numel(),
+           y.data_ptr(), y.stride(0), _stream())
+    planes.M = M
+    return y.reshape(-1) if vec and out is None else y
+
+
+def gemm_w8a8_group(items) -> list:
+    """Up to 8 independent tensor-core MMs in one launch (otq_gemm_w8a8_group): items is a list
+    of (planes, w, out, acc), planes a filled QActPlanes. Returns the outputs in order."""
+    import ctypes
+    arr = (L.Gemm8Proj * len(items))()
+    outs = []
+    for i, (planes, w, out, acc) in enumerate(items):
+        _tc_weight(w)
+        if planes.K != w.K or planes.M < 1:
+            raise ValueError("planes must be filled with rows of the weight's K")
+        y = _out(out, planes.M, w.N, planes.buf.device, acc)
+        p = arr[i]
+        p.flags = w.flags | (L.MM_ACC if acc else 0)
+        p.rows, p.rs = w.rows.data_ptr(), w.rows.stride(0)
+        p.srows = _ptr(w.srows)
+        p.srs = 0 if w.srows is None else w.srows.stride(0)
+        p.N, p.K = w.N, w.K
+        p.planes, p.M = planes.buf.data_ptr(), planes.M
+        p.y, p.ldy = y.data_ptr(), y.stride(0)
+        outs.append(y)
+    L.call("otq_gemm_w8a8_group", ctypes.addressof(arr), len(items), _stream())
+    return outs
+
+
 def qlinear_peer(x: torch.Tensor, w: PackedWeight, y: torch.Tensor, peer, *,
                  row_mode: bool = False, pdl: bool = False) -> torch.Tensor:
     """QACT + MM of one activation row against this rank's rows of a row-sharded projection,
