@@ -551,14 +551,18 @@ def phi4_sweep(args, world, rank, group, hbm):
                 w = linear.PackedWeight(f, n, K, codes, sc)
             ws.append(w)
             nbytes += w.stream_bytes * world
-        for B in (1, 8, 64):
+        for B, tc in ((1, False), (8, False), (8, True), (64, False), (64, True)):
             xs = {K: torch.randn((B, K), device="cuda", generator=gen) for _, _, K in projs}
             ys = [torch.empty((B, w.N), device="cuda") for w in ws]
             gath = [torch.empty((world, B, w.N), device="cuda") for w in ws] if world > 1 else None
+            planes = {K: linear.QActPlanes(B, K) for _, _, K in projs} if tc else None
 
             def run():
                 for i, ((_, N, K), w) in enumerate(zip(projs, ws)):
-                    linear.qlinear(xs[K], w, out=ys[i], pdl=True)
+                    if tc and w.fmt == "int8-row":   # QACT + the exact MM on tcgen05
+                        linear.qlinear_tc(xs[K], w, out=ys[i], planes=planes[K])
+                    else:
+                        linear.qlinear(xs[K], w, out=ys[i], pdl=True)
                     if world > 1:
                         dist.all_gather_into_tensor(gath[i], ys[i], group=group)
             g = capture(run, stream, warm=1)
@@ -566,6 +570,8 @@ def phi4_sweep(args, world, rank, group, hbm):
             ms = graph_ms(g, stream, max(5, min(args.steps, 20)), world)
             del g
             out.append({"format": fmt, "batch": B, "ms": ms,
+                        "int8_path": "tcgen05 kind::i8 (otq_qmm_tc)" if tc else "cuda-core GEMV",
+                        "launches": sum(2 if tc and w.fmt == "int8-row" else 1 for w in ws),
                         "GB/s": nbytes / (ms * 1e-3) / 1e9,
                         "hbm_frac_per_gpu": nbytes / world / (ms * 1e-3) / 1e9 / hbm,
                         "weights_bytes": nbytes})
@@ -579,7 +585,7 @@ def phi4_sweep(args, world, rank, group, hbm):
                                    "head); batch 1/8/64; one CUDA graph of the 8 launches",
                        "parallelism": f"row-shard x{world}" + (" + NCCL all-gather of every "
                                                               "output" if world > 1 else "")},
-            "gpu_launches": len(out) * 8}
+            "gpu_launches": sum(r["launches"] for r in out)}
 
 
 # ------------------------------------------------------------------------------ prefill
@@ -797,6 +803,9 @@ def prefill_bench(args, world, rank, local, group, steps, warmup):
         barrier(world)
     del g
     torch.cuda.synchronize()
+    w8a8 = None
+    if world == 1 and not args.no_w8a8:
+        w8a8 = prefill_w8a8_bench(steps, warmup, layers)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, desc, threads = prefill_cpu_sample()
@@ -826,6 +835,89 @@ def prefill_bench(args, world, rank, local, group, steps, warmup):
         "parity": parity,
         "cpu_baseline": cpu,
         "gpu_launches": shape.layers * steps,
+        "w8a8": w8a8,
+    }
+
+
+def prefill_w8a8_bench(steps, warmup, layers_in=None):
+    """The exact prefill of BASELINE configuration 4's shapes (one GPU): the reference's own
+    prefill numerics, QACT of fp32 activations and the exact integer MM (otq_qact_planes +
+    otq_gemm_w8a8_group on tcgen05 kind::i8), bit-identical to the reference's MM. A layer is
+    four QACT launches (the inputs of q / k / v, of o, of gate / up, of down: the layer's data
+    flow) and one grouped MM launch of its seven projections; 36 layers in one CUDA graph.
+    Activations are bf16 N(0, 1) values widened to fp32."""
+    import torch
+    from opentpu_b200 import linear
+    shape = WL.SMOLLM3_3B
+    gen = torch.Generator(device="cuda").manual_seed(4321)
+    projs = shape.projections()          # q, k, v, o, gate, up, down
+    src = [0, 0, 0, 1, 2, 2, 3]          # which of the layer's four inputs each reads
+    Ks = [projs[0][2], projs[3][2], projs[4][2], projs[6][2]]
+    xs = [torch.randn((PREFILL_TOKENS, K), device="cuda", generator=gen)
+          .to(torch.bfloat16).float() for K in Ks]
+    planes = [linear.QActPlanes(PREFILL_TOKENS, K) for K in Ks]
+    if layers_in is None:
+        layers_in = [prefill_layer(shape, 1, 0, gen)[0] for _ in range(shape.layers)]
+    layers = [[(planes[src[i]], it[1], it[2], False) for i, it in enumerate(items)]
+              for items in layers_in]
+    flops_layer = sum(2.0 * PREFILL_TOKENS * it[1].N * it[1].K for it in layers_in[0])
+
+    def fill():
+        for x, p in zip(xs, planes):
+            p.fill(x)
+
+    def step():
+        for items in layers:
+            fill()
+            linear.gemm_w8a8_group(items)
+    stream = torch.cuda.Stream()
+    g = capture(step, stream, warm=1)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            g.replay()
+    ms = graph_ms(g, stream, steps, 1)
+    gk = capture(lambda: [linear.gemm_w8a8_group(items) for items in layers], stream, warm=1)
+    graph_ms(gk, stream, 1, 1)
+    kms = graph_ms(gk, stream, steps, 1)
+    del g, gk
+    # parity: every projection of layer 0 against the CUDA-core MM (otq_qmm), bit for bit
+    outs = [torch.empty_like(it[2]) for it in layers[0]]
+    with torch.cuda.stream(stream):
+        fill()
+        linear.gemm_w8a8_group([(p, w, y, a) for (p, w, _, a), y in zip(layers[0], outs)])
+    stream.synchronize()
+    differ = 0
+    for i, ((_, w, _, _), y) in enumerate(zip(layers[0], outs)):
+        ref = linear.qlinear(xs[src[i]], w)
+        differ += int((ref.view(torch.int32) != y.view(torch.int32)).sum().item())
+    counts = []
+    for p in planes:
+        Mp = -(-PREFILL_TOKENS // 128) * 128
+        counts += p.buf[8 * Mp: 8 * Mp + PREFILL_TOKENS].tolist()
+    _, bf16_peak, peak_kind = peaks()
+    launch_us = kms * 1e3 / shape.layers
+    achieved = flops_layer / (launch_us * 1e-6) / 1e12
+    total = flops_layer * shape.layers
+    return {
+        "metric": "prefill TOP/s (exact W8A8)", "value": total / (ms * 1e-3) / 1e12,
+        "unit": "TOP/s", "ms_per_step": ms, "steps": steps,
+        "dtype": "int8 x int8 -> int64 exact, fp32 epilogue",
+        "config": {"workload": "SmolLM3-3B-shaped prefill, 36 layers x 7 projections, 512 "
+                               "tokens, QACT of fp32 activations (bf16 N(0,1) values) + exact "
+                               "MM; the reference's prefill numerics",
+                   "launch": "4 QACT launches + one grouped MM launch a layer, 36 layers in "
+                             "one CUDA graph"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": 2 * bf16_peak,
+                     "unit": "TOP/s", "frac": achieved / (2 * bf16_peak), "traffic": None,
+                     "kernel": "w8a8_kernel (one layer's 7 projections, M=512)",
+                     "us_per_launch": launch_us, "ops_per_launch": flops_layer,
+                     "peak_kind": f"2 x {peak_kind} bf16 burst (int8 dense is twice bf16)",
+                     "planes_per_row": {str(k): counts.count(k) for k in (1, 2, 3)},
+                     "note": "a row with offsets 1..8 runs two int8 planes (exactness), so "
+                             "tensor work is planes x the algorithmic ops"},
+        "parity": {"vs_cuda_core_mm": "bit-identical" if differ == 0 else "differs",
+                   "outputs_differing": differ, "layer": 0},
+        "gpu_launches": 5 * shape.layers * steps,
     }
 
 
@@ -876,6 +968,28 @@ def profile_run(what: str):
                                  torch.Generator(device="cuda").manual_seed(0))
         for _ in range(3):
             linear.gemm_w8a16_group(items)
+    elif what == "w8a8":
+        items, _ = prefill_layer(WL.SMOLLM3_3B, 1, 0,
+                                 torch.Generator(device="cuda").manual_seed(0))
+        planes = {}
+        for x, w, _, _ in items:
+            if w.K not in planes:
+                planes[w.K] = linear.QActPlanes(PREFILL_TOKENS, w.K).fill(x.float())
+        group = [(planes[w.K], w, y, False) for _, w, y, _ in items]
+        for _ in range(3):
+            linear.gemm_w8a8_group(group)
+    elif what == "phi4tc":
+        shape = WL.PHI4_MINI
+        W = torch.randint(-127, 128, (shape.vocab, shape.hidden), dtype=torch.int8,
+                          device="cuda").view(torch.uint8)
+        sw = torch.rand(shape.vocab, device="cuda") * 1e-3 + 1e-4
+        w = linear.PackedWeight("int8-row", shape.vocab, shape.hidden, W,
+                                sw.view(torch.uint8).reshape(-1, 4))
+        x = torch.randn((64, shape.hidden), device="cuda")
+        y = torch.empty((64, shape.vocab), device="cuda")
+        planes = linear.QActPlanes(64, shape.hidden)
+        for _ in range(3):
+            linear.qlinear_tc(x, w, out=y, planes=planes)
     else:
         chain = DecodeChain(shape)
         chain.capture()
@@ -915,9 +1029,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["head", "step", "prefill", "g32", "stepkernel",
+    ap.add_argument("--profile", choices=["head", "step", "prefill", "w8a8", "phi4tc", "g32",
+                                          "stepkernel",
                                           "stepkernel4", "decoderkernel"])
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-w8a8", action="store_true")
     ap.add_argument("--no-4bit", action="store_true")
     ap.add_argument("--no-config1", action="store_true")
     ap.add_argument("--no-phi4", action="store_true")

@@ -120,6 +120,10 @@ __device__ __forceinline__ void prefetch_rows_l2(const G32Params& p, int64_t row
 
 // LPR lanes per weight row, one 16-byte chunk (a whole group) per lane step; activations of
 // MT rows in shared memory as fp32. Signed nibbles become exact floats by the 2^23 + u trick.
+// The lanes of a row read different groups at once, 128 bytes apart: the same banks. So each
+// group's eight float4 are stored rotated by the group's index (float4 v of group c at slot
+// (v + c) % 8), and the eight lanes of a quarter warp, reading consecutive groups, hit eight
+// different slots: conflict-free (8-way conflicted unrotated).
 template <int MT, int LPR>
 __global__ void __launch_bounds__(kThreads) linear_g32_kernel(const G32Params p) {
   extern __shared__ __align__(16) float xs[];   // [MT][K]
@@ -142,12 +146,14 @@ __global__ void __launch_bounds__(kThreads) linear_g32_kernel(const G32Params p)
       for (int j = 0; j < mt; ++j) {
         const float4* xr = reinterpret_cast<const float4*>(p.x + static_cast<int64_t>(m0 + j) * p.ldx);
         for (int i = threadIdx.x; i < (K >> 2); i += kThreads)
-          reinterpret_cast<float4*>(xs + j * K)[i] = __ldcg(xr + i);
+          reinterpret_cast<float4*>(xs + j * K)[(i & ~7) | (((i & 7) + (i >> 3)) & 7)] =
+              __ldcg(xr + i);
       }
     } else {
       for (int j = 0; j < mt; ++j)
         for (int i = threadIdx.x; i < K; i += kThreads)
-          xs[j * K + i] = __ldcg(p.x + static_cast<int64_t>(m0 + j) * p.ldx + i);
+          xs[j * K + ((i & ~31) | (((((i >> 2) & 7) + (i >> 5)) & 7) << 2) | (i & 3))] =
+              __ldcg(p.x + static_cast<int64_t>(m0 + j) * p.ldx + i);
     }
     __syncthreads();
     for (int64_t t = wfirst; t < ntasks; t += wstride) {
@@ -190,7 +196,7 @@ __global__ void __launch_bounds__(kThreads) linear_g32_kernel(const G32Params p)
               float part = 0.0f;
 #pragma unroll
               for (int v = 0; v < 8; ++v) {
-                const float4 xv = xp[v];
+                const float4 xv = xp[(v + c) & 7];
                 part = __fmaf_rn(wf[4 * v + 0], xv.x, part);
                 part = __fmaf_rn(wf[4 * v + 1], xv.y, part);
                 part = __fmaf_rn(wf[4 * v + 2], xv.z, part);

@@ -21,7 +21,7 @@
 // two planes.)
 //
 // Two kernels:
-//   qact_planes_kernel  one CTA a row: QACT (qact.cuh) into shared memory, D(m), the planes,
+//   qact_planes_kernel  one CTA a row: QACT (the arithmetic of qact.cuh), D(m), the planes,
 //                       S[m], the shift 16 - D(m) and the row's plane count (the "planes"
 //                       buffer, otq_qact_planes);
 //   w8a8_kernel         a persistent CTA an SM over tiles of 128 weight rows x NT tokens
@@ -86,7 +86,8 @@ __host__ __device__ inline PlanesView planes_view(void* base, int64_t M) {
                     reinterpret_cast<int8_t*>(b + 9 * Mp)};
 }
 
-constexpr int kQThreads = 256;
+constexpr int kQThreads = 512;
+constexpr int kQWarps = kQThreads / 32;
 
 struct PlanesParams {
   const float* x;
@@ -104,15 +105,20 @@ __device__ __forceinline__ int digit(int v, int& rest) {
   return p;
 }
 
+// QACT of one row (the reference's quantize_mx with 32-element groups: the arithmetic of
+// qact.cuh's qact_row, step for step) written as planes. A group's offset d depends only on the
+// row's and the group's magnitude maxima, so D, the largest kept offset, is known after the
+// first pass, and the second pass writes each element's planes straight away.
 __global__ void __launch_bounds__(kQThreads) qact_planes_kernel(const PlanesParams p) {
   extern __shared__ __align__(16) uint32_t qsm[];
-  const int K = p.K;
+  const int K = p.K, G = K >> 5;
   const int64_t Mp = rows_padded(p.M);
   const int64_t row = blockIdx.x;
   const PlanesView v = planes_view(p.planes, p.M);
   int8_t* const out0 = v.data + row * K;
   int8_t* const out1 = out0 + Mp * K;
   int8_t* const out2 = out1 + Mp * K;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (row >= p.M) {   // padding rows: zero planes (read by the MMA, never stored)
     for (int i = threadIdx.x * 4; i < K; i += kQThreads * 4) {
       *reinterpret_cast<uint32_t*>(out0 + i) = 0u;
@@ -127,51 +133,69 @@ __global__ void __launch_bounds__(kQThreads) qact_planes_kernel(const PlanesPara
     return;
   }
   float* xs = reinterpret_cast<float*>(qsm);
-  uint32_t* seg = qsm + K;
-  uint32_t* red = seg + (K >> 5);
-  int8_t* qs = reinterpret_cast<int8_t*>(red + 40);
-  uint8_t* ds = reinterpret_cast<uint8_t*>(qs + K);
+  uint32_t* seg = qsm + K;        // [G] group magnitude maxima (bit patterns)
+  uint32_t* red = seg + G;        // [kQWarps + 3] the reductions
   const ThreadGroup<kQThreads> grp{static_cast<int>(threadIdx.x)};
   stage_row(grp, p.x + row * p.ldx, xs, K);
-  const QactRowResult r = qact_row(grp, xs, K, 32, p.row_mode != 0, seg, red,
-                                   [&](int i, int qv, int dg) {
-                                     qs[i] = static_cast<int8_t>(qv);
-                                     if ((i & 31) == 0) ds[i >> 5] = static_cast<uint8_t>(dg);
-                                   });
+  // pass 1: group maxima and the row maximum (amax by bit pattern after the flush)
+  uint32_t tmax = 0u;
+  for (int g = warp; g < G; g += kQWarps) {
+    const uint32_t mb = __float_as_uint(otq_flush(xs[(g << 5) + lane])) & 0x7FFFFFFFu;
+    const uint32_t gm = __reduce_max_sync(0xFFFFFFFFu, mb);
+    if (lane == 0) seg[g] = gm;
+    tmax = gm > tmax ? gm : tmax;
+  }
+  if (lane == 0) red[warp] = tmax;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t m = lane < kQWarps ? red[lane] : 0u;
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if (lane == 0) {
+      float S = 0.0f, inv = 0.0f;
+      if (m != 0u) {
+        const float amax = __uint_as_float(m);
+        S = fmul(amax, __uint_as_float(kInv127Bits));
+        inv = fmul(127.0f, recip(amax));
+      }
+      red[kQWarps] = __float_as_uint(S);
+      red[kQWarps + 1] = __float_as_uint(inv);
+      red[kQWarps + 2] = m;
+    }
+  }
+  __syncthreads();
+  const float S = __uint_as_float(red[kQWarps]);
+  const float inv = __uint_as_float(red[kQWarps + 1]);
+  const uint32_t amax_bits = red[kQWarps + 2];
+  const bool row_mode = p.row_mode != 0;
   // D = the largest kept offset (groups with d > 16 are dropped by MM)
   int dl = 0;
-  for (int g = threadIdx.x; g < (K >> 5); g += kQThreads) {
-    const int d = ds[g];
-    if (d <= 16) dl = max(dl, d);
-  }
+  if (!row_mode)
+    for (int g = threadIdx.x; g < G; g += kQThreads) {
+      const int d = group_offset(seg[g], amax_bits);
+      if (d <= 16) dl = max(dl, d);
+    }
   dl = __reduce_max_sync(0xFFFFFFFFu, dl);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = static_cast<uint32_t>(dl);
+  __syncthreads();   // red[0 .. kQWarps) is read above by warp 0 only; reuse it now
+  if (lane == 0) red[warp] = static_cast<uint32_t>(dl);
   __syncthreads();
   int D = 0;
 #pragma unroll
-  for (int w = 0; w < kQThreads / 32; ++w) D = max(D, static_cast<int>(red[w]));
-  for (int i = threadIdx.x * 4; i < K; i += kQThreads * 4) {
-    const int d = ds[i >> 5];
-    uint32_t b0 = 0u, b1 = 0u, b2 = 0u;
-    if (d <= 16) {
-      const int sh = D - d;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int a = static_cast<int>(qs[i + e]) * (1 << sh);
-        int r1, r2;
-        const int p0 = digit(a, r1);
-        const int p1 = digit(r1, r2);
-        b0 |= (static_cast<uint32_t>(p0) & 255u) << (8 * e);
-        b1 |= (static_cast<uint32_t>(p1) & 255u) << (8 * e);
-        b2 |= (static_cast<uint32_t>(r2) & 255u) << (8 * e);
-      }
-    }
-    *reinterpret_cast<uint32_t*>(out0 + i) = b0;
-    *reinterpret_cast<uint32_t*>(out1 + i) = b1;
-    *reinterpret_cast<uint32_t*>(out2 + i) = b2;
+  for (int w = 0; w < kQWarps; ++w) D = max(D, static_cast<int>(red[w]));
+  // pass 2: q = q8(x * (inv * 2^d)), a' = q * 2^(D - d) (0 for a dropped group), its digits
+  for (int g = warp; g < G; g += kQWarps) {
+    const int d = row_mode ? 0 : group_offset(seg[g], amax_bits);
+    const int i = (g << 5) + lane;
+    int a = 0;
+    if (d <= 16) a = q8(fmul(xs[i], fmul(inv, pow2i(d)))) * (1 << (D - d));
+    int r1, r2;
+    const int p0 = digit(a, r1);
+    const int p1 = digit(r1, r2);
+    out0[i] = static_cast<int8_t>(p0);
+    out1[i] = static_cast<int8_t>(p1);
+    out2[i] = static_cast<int8_t>(r2);
   }
   if (threadIdx.x == 0) {
-    v.S[row] = r.S;
+    v.S[row] = S;
     v.shift[row] = 16 - D;
     v.count[row] = static_cast<uint8_t>(D == 0 ? 1 : (D <= 8 ? 2 : 3));
   }
@@ -609,8 +633,8 @@ int qact_planes_launch(const float* x, int64_t ldx, int64_t M, int64_t K, int ro
                        void* planes, cudaStream_t stream) {
   if (M == 0) return kOk;
   const int64_t Mp = rows_padded(M);
-  const size_t smem = (static_cast<size_t>(K) * 5 + static_cast<size_t>(K / 32) * 5 + 160 + 15) &
-                      ~static_cast<size_t>(15);
+  const size_t smem = (static_cast<size_t>(K) * 4 + static_cast<size_t>(K / 32) * 4 +
+                       4 * (kQWarps + 3) + 15) & ~static_cast<size_t>(15);
   if (Mp > 0x7FFFFFFF || K > 0x7FFFFFFF || smem > 227 * 1024) return kErrArg;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kErrCuda;
