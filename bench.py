@@ -533,6 +533,7 @@ def phi4_sweep(args, world, rank, group, hbm):
     projs = shape.projections() + [("head", shape.vocab, shape.hidden)]
     gen = torch.Generator(device="cuda").manual_seed(77)
     out = []
+    gemv_roof = None
     stream = torch.cuda.Stream()
     for fmt in ("int8-row", "int4-g32"):
         ws, nbytes = [], 0
@@ -575,9 +576,26 @@ def phi4_sweep(args, world, rank, group, hbm):
                         "GB/s": nbytes / (ms * 1e-3) / 1e9,
                         "hbm_frac_per_gpu": nbytes / world / (ms * 1e-3) / 1e9 / hbm,
                         "weights_bytes": nbytes})
+        if fmt == "int8-row":
+            # the 614 MB head alone at batch 1: the GEMV's streaming rate on a large matrix
+            head = ws[-1]
+            hx = torch.randn((1, head.K), device="cuda", generator=gen)
+            hy = torch.empty((1, head.N), device="cuda")
+            g = capture(lambda: [linear.qlinear(hx, head, out=hy, pdl=True) for _ in range(10)],
+                        stream, warm=1)
+            graph_ms(g, stream, 1, world)
+            hms = graph_ms(g, stream, 5, world) / 10
+            del g
+            hb = head.stream_bytes + 4 * head.K + 4 * head.N
+            gemv_roof = {"bound": "hbm", "achieved": hb / (hms * 1e-3) / 1e9, "peak": hbm,
+                         "unit": "GB/s", "frac": hb / (hms * 1e-3) / 1e9 / hbm,
+                         "kernel": f"gemv_kernel ({head.N}x{head.K} int8-row head, M=1, this "
+                                   "rank's rows; 10 launches in a graph)",
+                         "bytes_per_launch": hb, "us_per_launch": hms * 1e3}
         del ws
         torch.cuda.synchronize()
     return {"metric": "quantized linear GB/s (Phi-4-mini shapes)", "unit": "GB/s",
+            "gemv_roofline": gemv_roof,
             "value": max(r["GB/s"] for r in out), "results": out,
             "config": {"workload": "BASELINE configuration 5: Phi-4-mini projections q 3072x3072, "
                                    "k/v 1024x3072, o 3072x3072, gate/up 8192x3072, down 3072x8192 "

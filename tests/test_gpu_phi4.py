@@ -1,7 +1,8 @@
 """BASELINE configuration 5 on the GPU: the Phi-4-mini-shaped quantized linears (hidden 3072, MLP
 8192, vocab 200064) at batches of 1, 8 and 64 activation rows, in int8 per-row (QACT + MM,
 bit-exact against the oracle) and 4-bit group-32 fp16 (weight-only, against float64 `deq @ x`
-within the 4-bit tolerance), the 200064 x 3072 LM head included, and their row shards over
+within the 4-bit tolerance), the 200064 x 3072 LM head included, the int8 ones also through the
+exact tensor-core MM (qlinear_tc, the same bits), and their row shards over
 2 / 4 / 8 ranks (runtime.Weight(shard=0)): the ranks' outputs, gathered in rank order, are the
 unsharded output bit for bit."""
 import numpy as np
@@ -46,6 +47,9 @@ def test_phi4_layer_int8_row(ops, name, N, K, M):
     rows = w.rows.cpu().numpy()[:, :K]
     srows = w.srows.cpu().numpy()
     assert np.array_equal(bits(y), bits(_oracle_rsc(x, rows, srows, K)))
+    # the exact tensor-core path (QACT planes + tcgen05 kind::i8): the same bits
+    ytc = ops.qlinear_tc(torch.from_numpy(x).cuda(), w).cpu().numpy()
+    assert np.array_equal(bits(ytc), bits(y))
     for G in (2, 4, 8):   # row shards, gathered in rank order
         n = N // G
         parts = [ops.qlinear(torch.from_numpy(x).cuda(), w.row_slice(r * n, (r + 1) * n))
@@ -83,6 +87,8 @@ def test_phi4_head_int8_row(ops, M):
     rows = w.rows.cpu().numpy()[:, :shape.hidden]
     srows = w.srows.cpu().numpy()
     assert np.array_equal(bits(y), bits(_oracle_rsc(x, rows, srows, shape.hidden)))
+    ytc = ops.qlinear_tc(torch.from_numpy(x).cuda(), w).cpu().numpy()
+    assert np.array_equal(bits(ytc), bits(y))
     n = shape.vocab // 8
     parts = [ops.qlinear(torch.from_numpy(x).cuda(), w.row_slice(r * n, (r + 1) * n))
              for r in range(8)]
