@@ -9,6 +9,7 @@
 
 #include <cstdint>
 
+#include "mm_common.cuh"
 #include "otq_internal.h"
 
 namespace otq {
@@ -332,6 +333,195 @@ __global__ void __launch_bounds__(kThreads) linear_g32_row_kernel(const G32Param
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// One activation row on the tensor pipe (K a multiple of 256). Per 32-element group g, x becomes
+// the fixed-point integer xi = rint(x * 2^e_g), |xi| < 2^30 (e_g from the group's largest |x|:
+// at most 2^-30 of it is lost), split into four signed base-256 digits (limbs). A code (a
+// signed byte -8..7) times a limb summed over the group is an exact int32: one mma.sync
+// m16n8k32 (s8 x s8) gives, for 16 weight rows, the group's four limb sums (the MMA's columns
+// 0-3), and sum_k w_k x_k = 2^-e_g sum_j 256^j D_j. Each row adds s_g 2^-e_g D_j into a fp32 sum
+// per limb (the weight 256^j applied once at the end): every integer product is exact and the
+// fp32 sums round like the FMA form's, within the 4-bit tolerance.
+//
+// A CTA (8 warps) takes a block of 16 weight rows at a time and splits its K chunks (8 groups,
+// 128 bytes of codes a row) over the warps (chunk c to warp c % 8, every warp one at least);
+// each warp streams its chunks of the CTA's row blocks through a cp.async ring (a row's eight
+// 16-byte pieces rotated by the row: conflict-free fragment reads; the 16 rows' 8 fp16 scales),
+// and the warps' row sums meet in shared memory in a fixed order. x's limbs (in the MMA's K
+// order) and 2^-e_g are built once a CTA.
+constexpr int kMmaStages = 6;
+constexpr int kChunkGroups = 8;                       // groups a K chunk (128 bytes of codes)
+constexpr int kStageCodes = 16 * 128;                 // 16 rows x 128 bytes
+constexpr int kStageBytes = kStageCodes + 16 * 16;    // + 16 rows x 8 fp16 scales
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+
+// Eight two's-complement nibbles -> signed bytes: the even elements in lo, the odd in hi. With
+// u = nibble ^ 8 (0..15), (u + 0x78) ^ 0x80 is u - 8 as a byte, and u + 0x78 <= 0x87 never
+// carries into the next byte.
+__device__ __forceinline__ void int4_sbytes(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x8 = w ^ 0x88888888u;
+  lo = ((x8 & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+  hi = (((x8 >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+}
+
+size_t g32_mma_smem(int K) {
+  return static_cast<size_t>(K / 32) * 132 + 2 * 8 * 16 * 4 +
+         static_cast<size_t>(8) * kMmaStages * kStageBytes;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) linear_g32_mma_kernel(const G32Params p) {
+  extern __shared__ __align__(16) unsigned char gsm[];
+  const int K = p.K, G = K >> 5, nch = G / kChunkGroups;
+  // [G][4 limbs][32 K slots] limbs; [G] 2^-e_g; [2][8 warps][16 rows] partial sums; the rings
+  uint8_t* const xl = gsm;
+  float* const xf = reinterpret_cast<float*>(gsm + G * 128);
+  float* const part = xf + G;
+  unsigned char* const ring = gsm + G * 132 + 2 * 8 * 16 * 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int64_t nblocks = (p.N + 15) / 16;
+  if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) * 16 < p.N)
+    prefetch_rows_l2(p, static_cast<int64_t>(blockIdx.x) * 16, 16);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // x -> limbs: a warp a group at a time, lane l holding element l, stored at the K slot s
+  // whose element is l (slots 4t + i hold elements 8t + 2i, slots 16 + 4t + i elements 8t + 2i + 1)
+  const int slot = (lane & 1) ? 16 + 4 * (lane >> 3) + ((lane >> 1) & 3)
+                              : 4 * (lane >> 3) + ((lane >> 1) & 3);
+  for (int g = warp; g < G; g += kThreads / 32) {
+    const float v = __ldcg(p.x + g * 32 + lane);
+    float m = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    // e = 29 - exponent(m), at most 126 (|x| tiny or zero): m 2^e in [2^29, 2^30)
+    const int e = m > 0.0f ? min(126, 156 - static_cast<int>((__float_as_uint(m) >> 23) & 255u))
+                           : 0;
+    int r = __float2int_rn(__fmul_rn(v, __int_as_float((127 + e) << 23)));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int d = j < 3 ? ((r + 128) & 255) - 128 : r;   // |r| <= 64 for the last
+      xl[g * 128 + j * 32 + slot] = static_cast<uint8_t>(d);
+      r = (r - d) >> 8;
+    }
+    if (lane == 0) xf[g] = __int_as_float((127 - e) << 23);
+  }
+  __syncthreads();
+
+  // this warp's items: for each of the CTA's row blocks, its chunks warp, warp + 8, ...
+  const int per_block = (nch - 1 - warp) / 8 + 1;   // nch >= 8: at least one
+  const int64_t my_blocks = nblocks > blockIdx.x ? (nblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t total = my_blocks * per_block;
+  const uint32_t wbase = static_cast<uint32_t>(__cvta_generic_to_shared(ring)) +
+                         static_cast<uint32_t>(warp * kMmaStages * kStageBytes);
+  const unsigned char* const wring = ring + warp * kMmaStages * kStageBytes;
+  auto issue = [&](int64_t it) {
+    if (it < total) {
+      const int64_t rb = blockIdx.x + (it / per_block) * gridDim.x;
+      const int c = warp + 8 * static_cast<int>(it % per_block);
+      const uint32_t st = wbase + static_cast<uint32_t>((it % kMmaStages) * kStageBytes);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int pc = lane + 32 * i, r = pc >> 3, q = pc & 7;
+        const int64_t row = rb * 16 + r;
+        const bool ok = row < p.N;
+        const uint8_t* src = p.codes + (ok ? row : 0) * (K / 2) + c * 128 + q * 16;
+        cp_async16(st + r * 128 + ((q + r) & 7) * 16, src, ok ? 16u : 0u);
+      }
+      if (lane < 16) {
+        const int64_t row = rb * 16 + lane;
+        const bool ok = row < p.N;
+        const uint16_t* src = p.scales + (ok ? row : 0) * G + c * kChunkGroups;
+        cp_async16(st + kStageCodes + lane * 16, src, ok ? 16u : 0u);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int i = 0; i < kMmaStages - 1; ++i) issue(i);
+  float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+  const float w0 = tig == 0 ? 1.0f : 65536.0f, w1 = tig == 0 ? 256.0f : 16777216.0f;
+  for (int64_t it = 0; it < total; ++it) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kMmaStages - 2) : "memory");
+    __syncwarp();
+    const unsigned char* st = wring + (it % kMmaStages) * kStageBytes;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + kStageCodes);
+    const int c = warp + 8 * static_cast<int>(it % per_block);
+#pragma unroll
+    for (int q = 0; q < kChunkGroups; ++q) {
+      const int g = c * kChunkGroups + q;
+      const uint32_t wa =
+          *reinterpret_cast<const uint32_t*>(st + gid * 128 + ((q + gid) & 7) * 16 + 4 * tig);
+      const uint32_t wb = *reinterpret_cast<const uint32_t*>(
+          st + (gid + 8) * 128 + ((q + gid + 8) & 7) * 16 + 4 * tig);
+      uint32_t a0, a1, a2, a3;
+      int4_sbytes(wa, a0, a2);
+      int4_sbytes(wb, a1, a3);
+      uint32_t b0 = 0u, b1 = 0u;   // columns 4-7 stay zero
+      if (gid < 4) {
+        b0 = *reinterpret_cast<const uint32_t*>(xl + g * 128 + gid * 32 + 4 * tig);
+        b1 = *reinterpret_cast<const uint32_t*>(xl + g * 128 + gid * 32 + 16 + 4 * tig);
+      }
+      int d[4];
+      imma(a0, a1, a2, a3, b0, b1, d);
+      const float f = xf[g];
+      const float sf0 = __fmul_rn(half_bits_to_float(sc[gid * 8 + q]), f);
+      const float sf1 = __fmul_rn(half_bits_to_float(sc[(gid + 8) * 8 + q]), f);
+      a00 = __fmaf_rn(sf0, static_cast<float>(d[0]), a00);
+      a01 = __fmaf_rn(sf0, static_cast<float>(d[1]), a01);
+      a10 = __fmaf_rn(sf1, static_cast<float>(d[2]), a10);
+      a11 = __fmaf_rn(sf1, static_cast<float>(d[3]), a11);
+    }
+    __syncwarp();
+    issue(it + kMmaStages - 1);
+    if ((it + 1) % per_block == 0) {
+      // this warp's last chunk of the row block: its rows' sums, then every warp's in order
+      const int64_t blk = it / per_block;
+      float v0 = tig < 2 ? __fmaf_rn(a01, w1, __fmul_rn(a00, w0)) : 0.0f;
+      float v1 = tig < 2 ? __fmaf_rn(a11, w1, __fmul_rn(a10, w0)) : 0.0f;
+      v0 = __fadd_rn(v0, __shfl_xor_sync(0xFFFFFFFFu, v0, 1));
+      v1 = __fadd_rn(v1, __shfl_xor_sync(0xFFFFFFFFu, v1, 1));
+      float* const pb = part + (blk & 1) * 128;
+      if (tig == 0) {
+        pb[warp * 16 + gid] = v0;
+        pb[warp * 16 + gid + 8] = v1;
+      }
+      a00 = a01 = a10 = a11 = 0.f;
+      __syncthreads();   // every warp calls it once a row block, in the same order
+      if (threadIdx.x < 16) {
+        const int64_t row = (blockIdx.x + blk * gridDim.x) * 16 + threadIdx.x;
+        float v = pb[threadIdx.x];
+#pragma unroll
+        for (int w2 = 1; w2 < kThreads / 32; ++w2) v = __fadd_rn(v, pb[w2 * 16 + threadIdx.x]);
+        if (row < p.N) {
+          float* yp = p.y + row;
+          *yp = p.accumulate ? __fadd_rn(*yp, v) : v;
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+int launch_g32_mma(const G32Params& p, cudaStream_t stream) {
+  const size_t smem = g32_mma_smem(p.K);
+  static size_t configured[kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return kErrCuda;
+  if (configured[dev] < smem) {
+    if (cudaFuncSetAttribute(linear_g32_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return kErrCuda;
+    configured[dev] = smem;
+  }
+  const int64_t blocks = (p.N + 15) / 16;
+  const int64_t cap = sm_count(dev);
+  return launch_kernel(reinterpret_cast<const void*>(linear_g32_mma_kernel),
+                       static_cast<int>(blocks < cap ? blocks : cap), kThreads, smem, stream,
+                       kG32Pdl, p);
+}
+
 int launch_g32_row(const G32Params& p, cudaStream_t stream) {
   const size_t smem = (static_cast<size_t>(p.K) + p.K / 32 + kThreads) * 4;
   static size_t configured[kMaxDevices] = {0};
@@ -416,7 +606,14 @@ int linear_g32_launch(const uint8_t* codes, const uint16_t* scales, int64_t N, i
   G32Params p{codes, scales, N, K, x, ldx, M, accumulate, y, ldy};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
-  // one activation row: a weight row a lane, once there are enough 32-row blocks to fill the GPU
+  // one activation row: 16-row blocks on the tensor pipe when K is whole 8-group chunks, at
+  // least 8 of them (one a warp), the fixed-point limbs fit shared memory and the codes and
+  // scales are 16-byte aligned (cp.async); else a weight row a lane, once there are enough
+  // 32-row blocks to fill the GPU
+  const bool al16 = (reinterpret_cast<uintptr_t>(codes) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(scales) & 15u) == 0;
+  if (M == 1 && al16 && K % 256 == 0 && K >= 2048 && g32_mma_smem(K) <= 220 * 1024)
+    return launch_g32_mma(p, stream);
   if (M == 1 && (N + 31) / 32 >= 64) return launch_g32_row(p, stream);
   const int nc = K / 32;
   int lpr = 4;
