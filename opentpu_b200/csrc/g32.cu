@@ -336,19 +336,22 @@ __global__ void __launch_bounds__(kThreads) linear_g32_row_kernel(const G32Param
 // One activation row on the tensor pipe (K a multiple of 256). Per 32-element group g, x becomes
 // the fixed-point integer xi = rint(x * 2^e_g), |xi| < 2^30 (e_g from the group's largest |x|:
 // at most 2^-30 of it is lost), split into four signed base-256 digits (limbs). A code (a
-// signed byte -8..7) times a limb summed over the group is an exact int32: one mma.sync
-// m16n8k32 (s8 x s8) gives, for 16 weight rows, the group's four limb sums (the MMA's columns
-// 0-3), and sum_k w_k x_k = 2^-e_g sum_j 256^j D_j. Each row adds s_g 2^-e_g D_j into a fp32 sum
-// per limb (the weight 256^j applied once at the end): every integer product is exact and the
-// fp32 sums round like the FMA form's, within the 4-bit tolerance.
+// code plus 8 (u in 0..15) times a limb summed over the group is an exact int32: one mma.sync
+// m16n8k32 (u8 x s8) gives, for 16 weight rows, the group's four limb sums D_j (the MMA's
+// columns 0-3), and sum_k w_k x_k = 2^-e_g (sum_j 256^j D_j - 8 sum_k xi_k). A thread holds two
+// adjacent limbs of a row, P = D_2t + 256 D_2t+1 - C_t (|P| < 2^24, exact in fp32; C_t the
+// limbs' share of 8 sum xi), and adds s_g 2^-e_g P into a fp32 sum (the limb weight 1 or 2^16
+// applied once at the end): every integer product is exact and the fp32 sums round like the FMA
+// form's, within the 4-bit tolerance.
 //
-// A CTA (8 warps) takes a block of 16 weight rows at a time and splits its K chunks (8 groups,
+// A CTA (8 warps; two an SM for K up to about 5000) takes a block of 16 weight rows at a time and splits its K chunks (8 groups,
 // 128 bytes of codes a row) over the warps (chunk c to warp c % 8, every warp one at least);
-// each warp streams its chunks of the CTA's row blocks through a cp.async ring (a row's eight
-// 16-byte pieces rotated by the row: conflict-free fragment reads; the 16 rows' 8 fp16 scales),
+// each warp streams its chunks of the CTA's row blocks through a cp.async ring (piece q of row r
+// at q ^ (r % 8): conflict-free fragment reads, rows r and r + 8 one address apart; the 16 rows'
+// 8 fp16 scales),
 // and the warps' row sums meet in shared memory in a fixed order. x's limbs (in the MMA's K
-// order) and 2^-e_g are built once a CTA.
-constexpr int kMmaStages = 6;
+// order), 2^-e_g and the corrections C are built once a CTA.
+constexpr int kMmaStages = 4;
 constexpr int kChunkGroups = 8;                       // groups a K chunk (128 bytes of codes)
 constexpr int kStageCodes = 16 * 128;                 // 16 rows x 128 bytes
 constexpr int kStageBytes = kStageCodes + 16 * 16;    // + 16 rows x 8 fp16 scales
@@ -358,28 +361,25 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
                : "memory");
 }
 
-// Eight two's-complement nibbles -> signed bytes: the even elements in lo, the odd in hi. With
-// u = nibble ^ 8 (0..15), (u + 0x78) ^ 0x80 is u - 8 as a byte, and u + 0x78 <= 0x87 never
-// carries into the next byte.
-__device__ __forceinline__ void int4_sbytes(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t x8 = w ^ 0x88888888u;
-  lo = ((x8 & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-  hi = (((x8 >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-}
+// The two halves of a word of two fp16 -> fp32.
+__device__ __forceinline__ float half_lo(uint32_t w) { return half_bits_to_float(static_cast<uint16_t>(w)); }
+__device__ __forceinline__ float half_hi(uint32_t w) { return half_bits_to_float(static_cast<uint16_t>(w >> 16)); }
 
 size_t g32_mma_smem(int K) {
-  return static_cast<size_t>(K / 32) * 132 + 2 * 8 * 16 * 4 +
+  return static_cast<size_t>(K / 32) * 140 + 2 * 8 * 16 * 4 +
          static_cast<size_t>(8) * kMmaStages * kStageBytes;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) linear_g32_mma_kernel(const G32Params p) {
+__global__ void __launch_bounds__(kThreads, 2) linear_g32_mma_kernel(const G32Params p) {
   extern __shared__ __align__(16) unsigned char gsm[];
   const int K = p.K, G = K >> 5, nch = G / kChunkGroups;
-  // [G][4 limbs][32 K slots] limbs; [G] 2^-e_g; [2][8 warps][16 rows] partial sums; the rings
+  // [G][4 limbs][32 K slots] limbs; [G] 2^-e_g; [G][2] corrections; [2][8 warps][16 rows]
+  // partial sums; the rings
   uint8_t* const xl = gsm;
   float* const xf = reinterpret_cast<float*>(gsm + G * 128);
-  float* const part = xf + G;
-  unsigned char* const ring = gsm + G * 132 + 2 * 8 * 16 * 4;
+  int* const corr = reinterpret_cast<int*>(xf + G);
+  float* const part = reinterpret_cast<float*>(corr + 2 * G);
+  unsigned char* const ring = gsm + G * 140 + 2 * 8 * 16 * 4;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
   const int64_t nblocks = (p.N + 15) / 16;
@@ -399,13 +399,25 @@ __global__ void __launch_bounds__(kThreads, 1) linear_g32_mma_kernel(const G32Pa
     const int e = m > 0.0f ? min(126, 156 - static_cast<int>((__float_as_uint(m) >> 23) & 255u))
                            : 0;
     int r = __float2int_rn(__fmul_rn(v, __int_as_float((127 + e) << 23)));
+    int lj[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int d = j < 3 ? ((r + 128) & 255) - 128 : r;   // |r| <= 64 for the last
-      xl[g * 128 + j * 32 + slot] = static_cast<uint8_t>(d);
-      r = (r - d) >> 8;
+      lj[j] = j < 3 ? ((r + 128) & 255) - 128 : r;   // |r| <= 64 for the last
+      xl[g * 128 + j * 32 + slot] = static_cast<uint8_t>(lj[j]);
+      r = (r - lj[j]) >> 8;
     }
-    if (lane == 0) xf[g] = __int_as_float((127 - e) << 23);
+    // C_t = 8 (sum_k l_2t + 256 sum_k l_2t+1): the bias of u = code + 8 in limbs 2t, 2t + 1
+    int c01 = lj[0] + 256 * lj[1], c23 = lj[2] + 256 * lj[3];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      c01 += __shfl_xor_sync(0xFFFFFFFFu, c01, o);
+      c23 += __shfl_xor_sync(0xFFFFFFFFu, c23, o);
+    }
+    if (lane == 0) {
+      xf[g] = __int_as_float((127 - e) << 23);
+      corr[2 * g] = 8 * c01;
+      corr[2 * g + 1] = 8 * c23;
+    }
   }
   __syncthreads();
 
@@ -416,18 +428,22 @@ __global__ void __launch_bounds__(kThreads, 1) linear_g32_mma_kernel(const G32Pa
   const uint32_t wbase = static_cast<uint32_t>(__cvta_generic_to_shared(ring)) +
                          static_cast<uint32_t>(warp * kMmaStages * kStageBytes);
   const unsigned char* const wring = ring + warp * kMmaStages * kStageBytes;
-  auto issue = [&](int64_t it) {
-    if (it < total) {
-      const int64_t rb = blockIdx.x + (it / per_block) * gridDim.x;
-      const int c = warp + 8 * static_cast<int>(it % per_block);
-      const uint32_t st = wbase + static_cast<uint32_t>((it % kMmaStages) * kStageBytes);
+  // the copy side's position (row block, chunk, stage), advanced one item a call
+  int64_t irb = blockIdx.x;
+  int ici = 0, ist = 0;
+  int64_t issued = 0;
+  auto issue = [&]() {
+    if (issued < total) {
+      const int64_t rb = irb;
+      const int c = warp + 8 * ici;
+      const uint32_t st = wbase + static_cast<uint32_t>(ist * kStageBytes);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int pc = lane + 32 * i, r = pc >> 3, q = pc & 7;
         const int64_t row = rb * 16 + r;
         const bool ok = row < p.N;
         const uint8_t* src = p.codes + (ok ? row : 0) * (K / 2) + c * 128 + q * 16;
-        cp_async16(st + r * 128 + ((q + r) & 7) * 16, src, ok ? 16u : 0u);
+        cp_async16(st + r * 128 + ((q ^ (r & 7)) * 16), src, ok ? 16u : 0u);
       }
       if (lane < 16) {
         const int64_t row = rb * 16 + lane;
@@ -435,50 +451,71 @@ __global__ void __launch_bounds__(kThreads, 1) linear_g32_mma_kernel(const G32Pa
         const uint16_t* src = p.scales + (ok ? row : 0) * G + c * kChunkGroups;
         cp_async16(st + kStageCodes + lane * 16, src, ok ? 16u : 0u);
       }
+      ++issued;
+      if (++ici == per_block) {
+        ici = 0;
+        irb += gridDim.x;
+      }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
+    if (++ist == kMmaStages) ist = 0;
   };
-  for (int i = 0; i < kMmaStages - 1; ++i) issue(i);
-  float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
-  const float w0 = tig == 0 ? 1.0f : 65536.0f, w1 = tig == 0 ? 256.0f : 16777216.0f;
+  for (int i = 0; i < kMmaStages - 1; ++i) issue();
+  float a0s = 0.f, a1s = 0.f;   // rows gid, gid + 8: this thread's limb pair
+  const float wt = tig == 0 ? 1.0f : 65536.0f;
+  // the compute side's position: row block (its index among this CTA's), chunk, stage
+  int64_t blk = 0;
+  int ci = 0, cst = 0;
   for (int64_t it = 0; it < total; ++it) {
     asm volatile("cp.async.wait_group %0;" ::"n"(kMmaStages - 2) : "memory");
     __syncwarp();
-    const unsigned char* st = wring + (it % kMmaStages) * kStageBytes;
-    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + kStageCodes);
-    const int c = warp + 8 * static_cast<int>(it % per_block);
+    const unsigned char* st = wring + cst * kStageBytes;
+    const int c = warp + 8 * ci;
+    // the chunk's 8 scales of rows gid and gid + 8, its 2^-e_g
+    const uint4 s0 = *reinterpret_cast<const uint4*>(st + kStageCodes + gid * 16);
+    const uint4 s1 = *reinterpret_cast<const uint4*>(st + kStageCodes + (gid + 8) * 16);
+    const float4 f0 = *reinterpret_cast<const float4*>(xf + c * kChunkGroups);
+    const float4 f1 = *reinterpret_cast<const float4*>(xf + c * kChunkGroups + 4);
+    const uint32_t sw0[4] = {s0.x, s0.y, s0.z, s0.w}, sw1[4] = {s1.x, s1.y, s1.z, s1.w};
+    const float fv[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+    const unsigned char* const arow = st + gid * 128 + 4 * tig;
+    const uint8_t* const xlc = xl + c * kChunkGroups * 128 + gid * 32 + 4 * tig;
+    const int* const cc = corr + c * kChunkGroups * 2 + (tig & 1);
 #pragma unroll
     for (int q = 0; q < kChunkGroups; ++q) {
-      const int g = c * kChunkGroups + q;
-      const uint32_t wa =
-          *reinterpret_cast<const uint32_t*>(st + gid * 128 + ((q + gid) & 7) * 16 + 4 * tig);
-      const uint32_t wb = *reinterpret_cast<const uint32_t*>(
-          st + (gid + 8) * 128 + ((q + gid + 8) & 7) * 16 + 4 * tig);
+      const unsigned char* const ap = arow + ((q ^ gid) * 16);
+      const uint32_t wa = *reinterpret_cast<const uint32_t*>(ap);
+      const uint32_t wb = *reinterpret_cast<const uint32_t*>(ap + 8 * 128);
       uint32_t a0, a1, a2, a3;
-      int4_sbytes(wa, a0, a2);
-      int4_sbytes(wb, a1, a3);
+      int4_bytes(wa, a0, a2);
+      int4_bytes(wb, a1, a3);
       uint32_t b0 = 0u, b1 = 0u;   // columns 4-7 stay zero
       if (gid < 4) {
-        b0 = *reinterpret_cast<const uint32_t*>(xl + g * 128 + gid * 32 + 4 * tig);
-        b1 = *reinterpret_cast<const uint32_t*>(xl + g * 128 + gid * 32 + 16 + 4 * tig);
+        b0 = *reinterpret_cast<const uint32_t*>(xlc + q * 128);
+        b1 = *reinterpret_cast<const uint32_t*>(xlc + q * 128 + 16);
       }
       int d[4];
-      imma(a0, a1, a2, a3, b0, b1, d);
-      const float f = xf[g];
-      const float sf0 = __fmul_rn(half_bits_to_float(sc[gid * 8 + q]), f);
-      const float sf1 = __fmul_rn(half_bits_to_float(sc[(gid + 8) * 8 + q]), f);
-      a00 = __fmaf_rn(sf0, static_cast<float>(d[0]), a00);
-      a01 = __fmaf_rn(sf0, static_cast<float>(d[1]), a01);
-      a10 = __fmaf_rn(sf1, static_cast<float>(d[2]), a10);
-      a11 = __fmaf_rn(sf1, static_cast<float>(d[3]), a11);
+      asm volatile(
+          "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+          "{%10,%10,%10,%10};"
+          : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+          : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+      const int cq = cc[q * 2];
+      const float sc0 = (q & 1) ? half_hi(sw0[q >> 1]) : half_lo(sw0[q >> 1]);
+      const float sc1 = (q & 1) ? half_hi(sw1[q >> 1]) : half_lo(sw1[q >> 1]);
+      const float p0 = static_cast<float>(d[0] + 256 * d[1] - cq);
+      const float p1 = static_cast<float>(d[2] + 256 * d[3] - cq);
+      a0s = __fmaf_rn(__fmul_rn(sc0, fv[q]), p0, a0s);
+      a1s = __fmaf_rn(__fmul_rn(sc1, fv[q]), p1, a1s);
     }
     __syncwarp();
-    issue(it + kMmaStages - 1);
-    if ((it + 1) % per_block == 0) {
+    issue();
+    if (++cst == kMmaStages) cst = 0;
+    if (++ci == per_block) {
       // this warp's last chunk of the row block: its rows' sums, then every warp's in order
-      const int64_t blk = it / per_block;
-      float v0 = tig < 2 ? __fmaf_rn(a01, w1, __fmul_rn(a00, w0)) : 0.0f;
-      float v1 = tig < 2 ? __fmaf_rn(a11, w1, __fmul_rn(a10, w0)) : 0.0f;
+      ci = 0;
+      float v0 = tig < 2 ? __fmul_rn(a0s, wt) : 0.0f;
+      float v1 = tig < 2 ? __fmul_rn(a1s, wt) : 0.0f;
       v0 = __fadd_rn(v0, __shfl_xor_sync(0xFFFFFFFFu, v0, 1));
       v1 = __fadd_rn(v1, __shfl_xor_sync(0xFFFFFFFFu, v1, 1));
       float* const pb = part + (blk & 1) * 128;
@@ -486,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_g32_mma_kernel(const G32Pa
         pb[warp * 16 + gid] = v0;
         pb[warp * 16 + gid + 8] = v1;
       }
-      a00 = a01 = a10 = a11 = 0.f;
+      a0s = a1s = 0.f;
       __syncthreads();   // every warp calls it once a row block, in the same order
       if (threadIdx.x < 16) {
         const int64_t row = (blockIdx.x + blk * gridDim.x) * 16 + threadIdx.x;
@@ -498,6 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_g32_mma_kernel(const G32Pa
           *yp = p.accumulate ? __fadd_rn(*yp, v) : v;
         }
       }
+      ++blk;
     }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
@@ -515,8 +553,18 @@ int launch_g32_mma(const G32Params& p, cudaStream_t stream) {
       return kErrCuda;
     configured[dev] = smem;
   }
+  static int occ_cache[kMaxDevices] = {0};
+  static size_t occ_smem[kMaxDevices] = {0};
+  if (occ_cache[dev] == 0 || occ_smem[dev] != smem) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, linear_g32_mma_kernel, kThreads,
+                                                      smem) != cudaSuccess)
+      return kErrCuda;
+    occ_cache[dev] = occ > 0 ? occ : 1;
+    occ_smem[dev] = smem;
+  }
   const int64_t blocks = (p.N + 15) / 16;
-  const int64_t cap = sm_count(dev);
+  const int64_t cap = static_cast<int64_t>(sm_count(dev)) * occ_cache[dev];
   return launch_kernel(reinterpret_cast<const void*>(linear_g32_mma_kernel),
                        static_cast<int>(blocks < cap ? blocks : cap), kThreads, smem, stream,
                        kG32Pdl, p);
