@@ -362,8 +362,27 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
 }
 
 // The two halves of a word of two fp16 -> fp32.
-__device__ __forceinline__ float half_lo(uint32_t w) { return half_bits_to_float(static_cast<uint16_t>(w)); }
-__device__ __forceinline__ float half_hi(uint32_t w) { return half_bits_to_float(static_cast<uint16_t>(w >> 16)); }
+__device__ __forceinline__ float half_lo(uint32_t w) {
+  float f;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; cvt.f32.f16 %0, l; }" : "=f"(f) : "r"(w));
+  return f;
+}
+__device__ __forceinline__ float half_hi(uint32_t w) {
+  float f;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; cvt.f32.f16 %0, h; }" : "=f"(f) : "r"(w));
+  return f;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
 
 size_t g32_mma_smem(int K) {
   return static_cast<size_t>(K / 32) * 140 + 2 * 8 * 16 * 4 +
@@ -427,34 +446,51 @@ __global__ void __launch_bounds__(kThreads, 2) linear_g32_mma_kernel(const G32Pa
   const int64_t total = my_blocks * per_block;
   const uint32_t wbase = static_cast<uint32_t>(__cvta_generic_to_shared(ring)) +
                          static_cast<uint32_t>(warp * kMmaStages * kStageBytes);
-  const unsigned char* const wring = ring + warp * kMmaStages * kStageBytes;
-  // the copy side's position (row block, chunk, stage), advanced one item a call
+  // the copy side's position (row block, chunk, stage), advanced one item a call; a lane's
+  // sources (its 4 code pieces, lanes 0-15 a scale row) advance 8 chunks a step within a row
+  // block and are recomputed at the next row block (a row past N copies zeros)
   int64_t irb = blockIdx.x;
   int ici = 0, ist = 0;
   int64_t issued = 0;
+  const uint8_t* csrc[4];
+  uint32_t cbytes[4], cdst[4];
+  const uint16_t* ssrc = p.scales;
+  uint32_t sbytes = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int pc = lane + 32 * i, r = pc >> 3, q = pc & 7;
+    cdst[i] = static_cast<uint32_t>(r * 128 + ((q ^ (r & 7)) * 16));
+  }
+  auto set_rows = [&]() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pc = lane + 32 * i, r = pc >> 3, q = pc & 7;
+      const int64_t row = irb * 16 + r;
+      const bool ok = row < p.N;
+      csrc[i] = p.codes + (ok ? row : 0) * (K / 2) + warp * 128 + q * 16;
+      cbytes[i] = ok ? 16u : 0u;
+    }
+    const int64_t row = irb * 16 + (lane & 15);
+    const bool ok = row < p.N && lane < 16;
+    ssrc = p.scales + (ok ? row : 0) * G + warp * kChunkGroups;
+    sbytes = ok ? 16u : 0u;
+  };
+  set_rows();
   auto issue = [&]() {
     if (issued < total) {
-      const int64_t rb = irb;
-      const int c = warp + 8 * ici;
       const uint32_t st = wbase + static_cast<uint32_t>(ist * kStageBytes);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int pc = lane + 32 * i, r = pc >> 3, q = pc & 7;
-        const int64_t row = rb * 16 + r;
-        const bool ok = row < p.N;
-        const uint8_t* src = p.codes + (ok ? row : 0) * (K / 2) + c * 128 + q * 16;
-        cp_async16(st + r * 128 + ((q ^ (r & 7)) * 16), src, ok ? 16u : 0u);
-      }
-      if (lane < 16) {
-        const int64_t row = rb * 16 + lane;
-        const bool ok = row < p.N;
-        const uint16_t* src = p.scales + (ok ? row : 0) * G + c * kChunkGroups;
-        cp_async16(st + kStageCodes + lane * 16, src, ok ? 16u : 0u);
-      }
+      for (int i = 0; i < 4; ++i) cp_async16(st + cdst[i], csrc[i], cbytes[i]);
+      if (lane < 16) cp_async16(st + kStageCodes + lane * 16, ssrc, sbytes);
       ++issued;
       if (++ici == per_block) {
         ici = 0;
         irb += gridDim.x;
+        set_rows();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) csrc[i] += 8 * 128;
+        ssrc += 8 * kChunkGroups;
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -463,36 +499,40 @@ __global__ void __launch_bounds__(kThreads, 2) linear_g32_mma_kernel(const G32Pa
   for (int i = 0; i < kMmaStages - 1; ++i) issue();
   float a0s = 0.f, a1s = 0.f;   // rows gid, gid + 8: this thread's limb pair
   const float wt = tig == 0 ? 1.0f : 65536.0f;
-  // the compute side's position: row block (its index among this CTA's), chunk, stage
+  // the compute side's position: row block (its index among this CTA's), chunk, stage; the
+  // fragment reads through 32-bit shared addresses
   int64_t blk = 0;
   int ci = 0, cst = 0;
+  const uint32_t xl_s = static_cast<uint32_t>(__cvta_generic_to_shared(xl)) + gid * 32 + 4 * tig;
+  const uint32_t xf_s = static_cast<uint32_t>(__cvta_generic_to_shared(xf));
+  const uint32_t cr_s = static_cast<uint32_t>(__cvta_generic_to_shared(corr)) + 4 * (tig & 1);
   for (int64_t it = 0; it < total; ++it) {
     asm volatile("cp.async.wait_group %0;" ::"n"(kMmaStages - 2) : "memory");
     __syncwarp();
-    const unsigned char* st = wring + cst * kStageBytes;
+    const uint32_t st = wbase + static_cast<uint32_t>(cst * kStageBytes);
     const int c = warp + 8 * ci;
     // the chunk's 8 scales of rows gid and gid + 8, its 2^-e_g
-    const uint4 s0 = *reinterpret_cast<const uint4*>(st + kStageCodes + gid * 16);
-    const uint4 s1 = *reinterpret_cast<const uint4*>(st + kStageCodes + (gid + 8) * 16);
-    const float4 f0 = *reinterpret_cast<const float4*>(xf + c * kChunkGroups);
-    const float4 f1 = *reinterpret_cast<const float4*>(xf + c * kChunkGroups + 4);
+    const uint4 s0 = lds128(st + kStageCodes + gid * 16);
+    const uint4 s1 = lds128(st + kStageCodes + (gid + 8) * 16);
+    const uint4 f0 = lds128(xf_s + c * kChunkGroups * 4);
+    const uint4 f1 = lds128(xf_s + c * kChunkGroups * 4 + 16);
     const uint32_t sw0[4] = {s0.x, s0.y, s0.z, s0.w}, sw1[4] = {s1.x, s1.y, s1.z, s1.w};
-    const float fv[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-    const unsigned char* const arow = st + gid * 128 + 4 * tig;
-    const uint8_t* const xlc = xl + c * kChunkGroups * 128 + gid * 32 + 4 * tig;
-    const int* const cc = corr + c * kChunkGroups * 2 + (tig & 1);
+    const uint32_t fv[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+    const uint32_t arow = st + gid * 128 + 4 * tig;
+    const uint32_t xlc = xl_s + c * kChunkGroups * 128;
+    const uint32_t cc = cr_s + c * kChunkGroups * 8;
 #pragma unroll
     for (int q = 0; q < kChunkGroups; ++q) {
-      const unsigned char* const ap = arow + ((q ^ gid) * 16);
-      const uint32_t wa = *reinterpret_cast<const uint32_t*>(ap);
-      const uint32_t wb = *reinterpret_cast<const uint32_t*>(ap + 8 * 128);
+      const uint32_t ap = arow + ((q ^ gid) * 16);
+      const uint32_t wa = lds32(ap);
+      const uint32_t wb = lds32(ap + 8 * 128);
       uint32_t a0, a1, a2, a3;
       int4_bytes(wa, a0, a2);
       int4_bytes(wb, a1, a3);
       uint32_t b0 = 0u, b1 = 0u;   // columns 4-7 stay zero
       if (gid < 4) {
-        b0 = *reinterpret_cast<const uint32_t*>(xlc + q * 128);
-        b1 = *reinterpret_cast<const uint32_t*>(xlc + q * 128 + 16);
+        b0 = lds32(xlc + q * 128);
+        b1 = lds32(xlc + q * 128 + 16);
       }
       int d[4];
       asm volatile(
@@ -500,13 +540,14 @@ __global__ void __launch_bounds__(kThreads, 2) linear_g32_mma_kernel(const G32Pa
           "{%10,%10,%10,%10};"
           : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
           : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-      const int cq = cc[q * 2];
+      const int cq = static_cast<int>(lds32(cc + q * 8));
       const float sc0 = (q & 1) ? half_hi(sw0[q >> 1]) : half_lo(sw0[q >> 1]);
       const float sc1 = (q & 1) ? half_hi(sw1[q >> 1]) : half_lo(sw1[q >> 1]);
+      const float fq = __uint_as_float(fv[q]);
       const float p0 = static_cast<float>(d[0] + 256 * d[1] - cq);
       const float p1 = static_cast<float>(d[2] + 256 * d[3] - cq);
-      a0s = __fmaf_rn(__fmul_rn(sc0, fv[q]), p0, a0s);
-      a1s = __fmaf_rn(__fmul_rn(sc1, fv[q]), p1, a1s);
+      a0s = __fmaf_rn(__fmul_rn(sc0, fq), p0, a0s);
+      a1s = __fmaf_rn(__fmul_rn(sc1, fq), p1, a1s);
     }
     __syncwarp();
     issue();
