@@ -421,6 +421,33 @@ def config1(world: int, reps: int):
                        "l2_resident": "one copy launched 256 times"}}
 
 
+def g32_gemv_roofline(hbm, peak_kind):
+    """The standalone int4-g32 GEMV (otq_linear_g32, one activation row) on a 65536 x 4096
+    weight (151 MB of codes and fp16 scales, more than L2): 20 launches in a CUDA graph with
+    programmatic dependent launch, CUDA events."""
+    import torch
+    from opentpu_b200 import linear
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    N, K = 65536, 4096
+    codes = torch.randint(0, 256, (N, K // 2), dtype=torch.int32, device="cuda",
+                          generator=gen).to(torch.uint8)
+    sc = (torch.rand((N, K // 32), device="cuda", generator=gen) * 1e-3 + 1e-4).half()
+    w = linear.PackedWeight("int4-g32", N, K, codes, sc)
+    x = torch.randn((1, K), device="cuda", generator=gen)
+    y = torch.empty((1, N), device="cuda")
+    stream = torch.cuda.Stream()
+    g = capture(lambda: [linear.qlinear(x, w, out=y, pdl=True) for _ in range(20)], stream, warm=1)
+    graph_ms(g, stream, 2, 1)
+    ms = graph_ms(g, stream, 10, 1) / 20
+    del g
+    nbytes = w.stream_bytes + 4 * K + 4 * N
+    ach = nbytes / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+            "kernel": "linear_g32_mma_kernel (65536x4096 int4-g32, M=1)",
+            "bytes_per_launch": nbytes, "us_per_launch": ms * 1e3,
+            "peak_kind": f"{peak_kind} (copy)"}
+
+
 def decode_4bit(args, world, rank, group, hbm, peak_kind):
     """BASELINE configuration 3's decode step: the Qwen3-0.6B step with int4-g32 layers (fp16
     group scales, weight-only, fp32 activations) and the int8-row head, as one persistent launch
@@ -466,6 +493,8 @@ def decode_4bit(args, world, rank, group, hbm, peak_kind):
     del c4
     torch.cuda.synchronize()
     out["mx_int4x"] = decode_mx_int4(args, world, rank, group)
+    if world == 1:
+        out["gemv_roofline"] = g32_gemv_roofline(hbm, peak_kind)
     return out
 
 
