@@ -52,3 +52,14 @@ def test_flag_and_format_codes_are_the_references():
     text = HEADER.read_text()
     for name, val in (("OTQ_MM_UNIT", "0x1"), ("OTQ_MM_RSC", "0x80"), ("OTQ_FMT_NVFP4", "3")):
         assert re.search(rf"#define {name} {val}\b", text)
+
+
+def test_qact_planes_size_without_a_device():
+    """otq_qact_planes_bytes is arithmetic only: 9 Mp + 3 Mp K bytes, Mp = M rounded up to 128;
+    K must be whole 32-element groups (and at most 65536)."""
+    lib = L.load()
+    for M, K in ((1, 32), (128, 1024), (129, 2048), (512, 11008), (0, 64)):
+        Mp = -(-M // 128) * 128
+        assert lib.otq_qact_planes_bytes(M, K) == 9 * Mp + 3 * Mp * K
+    for M, K in ((4, 48), (4, 0), (-1, 64), (4, 65568)):
+        assert lib.otq_qact_planes_bytes(M, K) < 0
