@@ -317,13 +317,18 @@ __device__ __forceinline__ float4 read_tagged4(const unsigned long long* xt, uin
                      __uint_as_float(static_cast<uint32_t>(w[2])), __uint_as_float(static_cast<uint32_t>(w[3])));
 }
 
-// The 4-bit input row: x' = x * 2^(-4 (k mod 4)) and the groups' sums, from plain fp32 x, from
-// tagged words (read until their tags reach `expect`), or (both null) from xs itself. The
-// compute threads meet at the end.
-__device__ void stage_x4(const float* x, const unsigned long long* xt, uint32_t expect, int K,
-                         float* xs, float* xsum, int* status, uint32_t limit) {
+// The 4-bit input row as the operands of the group MMAs (the form of otq_linear_g32's tensor-pipe
+// kernel): per 32-element group g, xi = rint(x * 2^e_g) with |xi| < 2^30 (e_g from the group's
+// largest |x|), four signed base-256 limbs of xi in the MMA's K order at bytes [128 g, 128 g + 128)
+// of xs (the group's own 32 floats, read by the same 8 lanes before they write), 2^-e_g in
+// xsum[g], and the codes' +8 bias in corr[2 g + t] = 8 sum_k (l_2t + 256 l_2t+1). x comes from
+// plain fp32 x, from tagged words (read until their tags reach `expect`), or (both null) from xs
+// itself. The compute threads meet at the end.
+__device__ void stage_limbs(const float* x, const unsigned long long* xt, uint32_t expect, int K,
+                            float* xs, float* xsum, int* corr, int* status, uint32_t limit) {
   const int tid = threadIdx.x;
-  for (int i = tid; i < K / 4; i += kCT) {   // K / 4 is a multiple of 32: whole warps
+  uint8_t* const xl = reinterpret_cast<uint8_t*>(xs);
+  for (int i = tid; i < K / 4; i += kCT) {   // K / 4 is a multiple of 32: whole warps, 8 lanes a group
     float4 v;
     if (xt != nullptr) {
       v = read_tagged4(xt + 4 * i, expect, status, limit);
@@ -332,50 +337,55 @@ __device__ void stage_x4(const float* x, const unsigned long long* xt, uint32_t 
     } else {
       v = ld_cg4(x + 4 * i);
     }
-    *reinterpret_cast<float4*>(xs + 4 * i) =
-        make_float4(v.x, v.y * 0.0625f, v.z * 0.00390625f, v.w * 0.000244140625f);
-    float sum = (v.x + v.y) + (v.z + v.w);
-    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
-    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 4);
-    if ((tid & 7) == 0) xsum[i >> 3] = sum;
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
+    // e = 29 - exponent(m), at most 126: m 2^e in [2^29, 2^30)
+    const int e = m > 0.0f ? min(126, 156 - static_cast<int>((__float_as_uint(m) >> 23) & 255u)) : 0;
+    const float p2 = __int_as_float((127 + e) << 23);
+    int r[4] = {__float2int_rn(__fmul_rn(v.x, p2)), __float2int_rn(__fmul_rn(v.y, p2)),
+                __float2int_rn(__fmul_rn(v.z, p2)), __float2int_rn(__fmul_rn(v.w, p2))};
+    int l[4][4];   // [limb][element]
+#pragma unroll
+    for (int el = 0; el < 4; ++el) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        l[j][el] = j < 3 ? ((r[el] + 128) & 255) - 128 : r[el];   // |r| <= 64 for the last
+        r[el] = (r[el] - l[j][el]) >> 8;
+      }
+    }
+    int c0 = 0, c1 = 0;
+#pragma unroll
+    for (int el = 0; el < 4; ++el) {
+      c0 += l[0][el] + 256 * l[1][el];
+      c1 += l[2][el] + 256 * l[3][el];
+    }
+    c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 1);
+    c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 1);
+    c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 2);
+    c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 2);
+    c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 4);
+    c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 4);
+    // elements 4q .. 4q + 3 of the group (q = i % 8): the even two at K slots b, b + 1 and the
+    // odd two at 16 + b, 17 + b, b = 4 (q / 2) + 2 (q % 2) (slots 4t + i hold element 8t + 2i,
+    // slots 16 + 4t + i element 8t + 2i + 1)
+    const int gq = i >> 3, q = i & 7;
+    uint8_t* const gl = xl + gq * 128 + 4 * (q >> 1) + 2 * (q & 1);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      *reinterpret_cast<uint16_t*>(gl + j * 32) =
+          static_cast<uint16_t>((l[j][0] & 0xFF) | ((l[j][2] & 0xFF) << 8));
+      *reinterpret_cast<uint16_t*>(gl + j * 32 + 16) =
+          static_cast<uint16_t>((l[j][1] & 0xFF) | ((l[j][3] & 0xFF) << 8));
+    }
+    if (q == 0) {
+      xsum[gq] = __int_as_float((127 - e) << 23);
+      corr[2 * gq] = 8 * c0;
+      corr[2 * gq + 1] = 8 * c1;
+    }
   }
   cbar();
-}
-
-// Sum over the 16 elements of a group that one 64-bit piece of codes holds, against x' (nibble p
-// of each 16-bit half masked in place under 2^23's exponent: 2^23 + u 16^p; less 2^23, times
-// x'[k] = x[k] 16^-p: u x[k], u = code + 8).
-__device__ __forceinline__ float dot16(uint32_t w0, uint32_t w1, const float* xq) {
-  w0 ^= 0x88888888u;
-  w1 ^= 0x88888888u;
-  const float4 a = *reinterpret_cast<const float4*>(xq);
-  const float4 b = *reinterpret_cast<const float4*>(xq + 4);
-  const float4 c = *reinterpret_cast<const float4*>(xq + 8);
-  const float4 d = *reinterpret_cast<const float4*>(xq + 12);
-  constexpr float kB = 8388608.0f;
-  float s = 0.0f;
-  uint32_t h = w0;
-  s = fmaf(__uint_as_float((h & 0xFu) | 0x4B000000u) - kB, a.x, s);
-  s = fmaf(__uint_as_float((h & 0xF0u) | 0x4B000000u) - kB, a.y, s);
-  s = fmaf(__uint_as_float((h & 0xF00u) | 0x4B000000u) - kB, a.z, s);
-  s = fmaf(__uint_as_float((h & 0xF000u) | 0x4B000000u) - kB, a.w, s);
-  h = w0 >> 16;
-  s = fmaf(__uint_as_float((h & 0xFu) | 0x4B000000u) - kB, b.x, s);
-  s = fmaf(__uint_as_float((h & 0xF0u) | 0x4B000000u) - kB, b.y, s);
-  s = fmaf(__uint_as_float((h & 0xF00u) | 0x4B000000u) - kB, b.z, s);
-  s = fmaf(__uint_as_float((h & 0xF000u) | 0x4B000000u) - kB, b.w, s);
-  h = w1;
-  s = fmaf(__uint_as_float((h & 0xFu) | 0x4B000000u) - kB, c.x, s);
-  s = fmaf(__uint_as_float((h & 0xF0u) | 0x4B000000u) - kB, c.y, s);
-  s = fmaf(__uint_as_float((h & 0xF00u) | 0x4B000000u) - kB, c.z, s);
-  s = fmaf(__uint_as_float((h & 0xF000u) | 0x4B000000u) - kB, c.w, s);
-  h = w1 >> 16;
-  s = fmaf(__uint_as_float((h & 0xFu) | 0x4B000000u) - kB, d.x, s);
-  s = fmaf(__uint_as_float((h & 0xF0u) | 0x4B000000u) - kB, d.y, s);
-  s = fmaf(__uint_as_float((h & 0xF00u) | 0x4B000000u) - kB, d.z, s);
-  s = fmaf(__uint_as_float((h & 0xF000u) | 0x4B000000u) - kB, d.w, s);
-  return s;
 }
 
 __device__ __forceinline__ float half_to_float(uint16_t h) {
@@ -832,7 +842,7 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
     }
     float Sa = 0.0f;
     if (g32) {
-      stage_x4(xsrc, xt, expect, K, s.xs, s.xsum, T.status, limit);
+      stage_limbs(xsrc, xt, expect, K, s.xs, s.xsum, reinterpret_cast<int*>(s.act), T.status, limit);
     } else {
       qact_row4<kCT, 1, true>(
           xsrc, true, s.xs, K, false, s.segm, s.qred,
@@ -985,25 +995,44 @@ __global__ void __launch_bounds__(kTh, 1) step_kernel(const StepTable* __restric
       rg += __shfl_xor_sync(0xFFFFFFFFu, rg, 2);
       rg8 += __shfl_xor_sync(0xFFFFFFFFu, rg8, 2);
     };
-    // 4-bit chunk k for rows g (st: the chunk's sub-stage, sc: the lane's two fp16 scales of the
-    // row) and g + 8: lane quarter t is bytes 32t .. 32t + 31 of a row's chunk, groups 2t, 2t + 1
-    auto chunk4 = [&](const uint8_t* st, const uint8_t* sc, int k, float& acc) {
-      const uint8_t* row = st + g * kChunkB;
-      const uint4 c0 = *reinterpret_cast<const uint4*>(row + 16 * ((2 * t) ^ g));
-      const uint4 c1 = *reinterpret_cast<const uint4*>(row + 16 * ((2 * t + 1) ^ g));
-      const uint32_t sw = *reinterpret_cast<const uint32_t*>(sc);
-      const int G = k * 8 + 2 * t;
-      const float* xq = s.xs + k * 256 + 64 * t;
-      const float s0 = fmaf(-8.0f, s.xsum[G], dot16(c0.x, c0.y, xq) + dot16(c0.z, c0.w, xq + 16));
-      const float s1 = fmaf(-8.0f, s.xsum[G + 1], dot16(c1.x, c1.y, xq + 32) + dot16(c1.z, c1.w, xq + 48));
-      acc = fmaf(half_to_float(static_cast<uint16_t>(sw & 0xFFFFu)), s0, acc);
-      acc = fmaf(half_to_float(static_cast<uint16_t>(sw >> 16)), s1, acc);
-    };
+    // 4-bit chunk k (8 groups) of the tile's rows g (into fg) and g + 8 (fg8): per group one
+    // mma.sync m16n8k32 (codes + 8 as u8 x the limbs of xs) gives the 16 rows' four exact limb
+    // sums; lane t < 2 adds s 2^-e (D_2t + 256 D_2t+1 - corr) 2^16t, so the quad's sum is the row's
+    // sum_k w x for the group (stage_limbs). Code pieces: piece q of row r at (q ^ r % 8) 16.
     auto chunk4x2 = [&](uint32_t stg, int jj, int k, float& fg, float& fg8) {
-      const uint8_t* st = s.ring + (stg - ring_s) + jj * kSub;
-      const uint8_t* sc = s.ring + (stg - ring_s) + kCodeStage + g * (16 * cbn) + jj * 16 + 4 * t;
-      chunk4(st, sc, k, fg);
-      chunk4(st + 1024, sc + 8 * (16 * cbn), k, fg8);
+      const uint8_t* const st = s.ring + (stg - ring_s) + jj * kSub;
+      const uint8_t* const scb = s.ring + (stg - ring_s) + kCodeStage + g * (16 * cbn) + jj * 16;
+      const uint16_t* const sc0p = reinterpret_cast<const uint16_t*>(scb);
+      const uint16_t* const sc1p = reinterpret_cast<const uint16_t*>(scb + 8 * (16 * cbn));
+      const uint8_t* const xl = reinterpret_cast<const uint8_t*>(s.xs) + k * 1024 + g * 32 + 4 * t;
+      const int* const cr = reinterpret_cast<const int*>(s.act) + k * 16 + (t & 1);
+      const float* const xf = s.xsum + k * 8;
+      const float wt = t == 0 ? 1.0f : (t == 1 ? 65536.0f : 0.0f);
+#pragma unroll 2
+      for (int q = 0; q < 8; ++q) {
+        const uint8_t* const ap = st + g * kChunkB + ((q ^ g) * 16) + 4 * t;
+        const uint32_t wa = *reinterpret_cast<const uint32_t*>(ap);
+        const uint32_t wb = *reinterpret_cast<const uint32_t*>(ap + 8 * kChunkB);
+        uint32_t a0, a1, a2, a3;
+        int4_bytes(wa, a0, a2);
+        int4_bytes(wb, a1, a3);
+        uint32_t b0 = 0u, b1 = 0u;   // columns 4-7 stay zero
+        if (g < 4) {
+          b0 = *reinterpret_cast<const uint32_t*>(xl + q * 128);
+          b1 = *reinterpret_cast<const uint32_t*>(xl + q * 128 + 16);
+        }
+        int dd[4];
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%10,%10,%10};"
+            : "=r"(dd[0]), "=r"(dd[1]), "=r"(dd[2]), "=r"(dd[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+        const int cq = cr[q * 2];
+        const float fw = __fmul_rn(xf[q], wt);
+        const float sc0 = half_to_float(sc0p[q]), sc1 = half_to_float(sc1p[q]);
+        fg = fmaf(__fmul_rn(sc0, fw), static_cast<float>(dd[0] + 256 * dd[1] - cq), fg);
+        fg8 = fmaf(__fmul_rn(sc1, fw), static_cast<float>(dd[2] + 256 * dd[3] - cq), fg8);
+      }
     };
     auto quad_sum = [&](float& f) {
       f += __shfl_xor_sync(0xFFFFFFFFu, f, 1);
