@@ -225,7 +225,8 @@ def test_g32_quantizer_matches_reference(ops, golden):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 1024, 1024), (4, 3072, 1024), (1, 1024, 3072),
-                                   (8, 640, 8192), (2, 100, 11008), (1, 151936, 1024)])
+                                   (8, 640, 8192), (2, 100, 11008), (1, 151936, 1024),
+                                   (1, 1000, 4096), (1, 37, 11008)])
 def test_g32_linear_within_tolerance(ops, M, N, K):
     rng = np.random.default_rng(N + K + M)
     W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
